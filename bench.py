@@ -1,0 +1,448 @@
+#!/usr/bin/env python
+"""Replica sparse-GEMM throughput on B200: one Llama-3-8B-shaped replica layer.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference] [--tokens T]
+
+A step is one forward pass of the replica layer's seven compact projections (q, k, v, o at keep 33; gate, up, down at
+keep 36; values bf16 + int16 column indices) over a batch of T = 272 tokens (16 sequences x 17 draft-pass tokens).
+Weights are N(0, 0.02), activations N(0, 1) times a lognormal per-channel scale, all seeded and synthetic; the
+calibration sums come from 128 x 2048 synthetic tokens per projection input through the package's own calibration
+kernel, and the selection from its Wanda top-k kernel.
+
+value: tokens/s of the whole job (N ranks, each with its own replica layer: weak scaling, no data-path collective),
+device-timed with CUDA events, the max over ranks. e2e: the same through the public API (Compact.apply) with the
+inputs copied from pinned host memory and the outputs read back inside the timed region. roofline: the compact GEMM's
+algorithmic bytes (values + indices + x + y, each once) per launch over its event-timed duration, against the measured
+HBM copy bandwidth. cpu_baseline: the reference's CPU forward (dense masked F.linear of the unpacked rows) on the
+host's cores, on a bounded sample of the same layer.
+
+--impl reference times that CPU path alone (rank 0; other ranks exit) and prints the same metric with impl=reference.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+from p2pllm_b200 import workloads  # noqa: E402
+
+METRIC = "replica sparse-GEMM tokens/s (Llama-3-8B replica layer, keep 33/36, T=272)"
+UNIT = "tokens/s"
+# Which synthetic activation each projection reads: q/k/v share the attention input, gate/up the MLP input.
+INPUT_OF = {"q": "attn_in", "k": "attn_in", "v": "attn_in", "o": "attn_out", "gate": "mlp_in", "up": "mlp_in",
+            "down": "mlp_mid"}
+L2_BYTES = 126 * 1024 * 1024
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=200)
+    p.add_argument("--warmup", type=int, default=10)
+    p.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    p.add_argument("--tokens", type=int, default=272)
+    p.add_argument("--calib-tokens", type=int, default=128 * 2048)
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    return p.parse_args()
+
+
+def measured_peaks() -> dict:
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            d = json.load(f)
+        return {"hbm_gbs": float(d["hbm_gbs"]), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "source": "fallback"}
+
+
+# ---------------------------------------------------------------------------------------------------------- clocks --
+
+_REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
+            0x80: "hw_power_brake_slowdown", 0x2: "applications_clocks_setting", 0x10: "sync_boost"}
+
+
+class ClockSampler:
+    """SM clock and clock-event reasons of this rank's GPU through NVML, every few ms while running."""
+
+    def __init__(self, device: int, period_s: float = 0.005):
+        self.samples, self.reasons, self.max_mhz = [], set(), None
+        self.period, self._stop, self._thread = period_s, threading.Event(), None
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            uuid = str(torch.cuda.get_device_properties(device).uuid)
+            try:
+                self.h = pynvml.nvmlDeviceGetHandleByUUID(("GPU-" + uuid) if not uuid.startswith("GPU-") else uuid)
+            except Exception:
+                self.h = pynvml.nvmlDeviceGetHandleByIndex(device)
+            self.nvml = pynvml
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+            self._reason_fn = getattr(pynvml, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+                getattr(pynvml, "nvmlDeviceGetCurrentClocksThrottleReasons")
+        except Exception as e:                                         # no NVML: report that, keep going
+            self.nvml, self.error = None, str(e)
+
+    def _run(self):
+        while not self._stop.is_set():
+            self.sample()
+            time.sleep(self.period)
+
+    def sample(self):
+        if self.nvml is None:
+            return
+        try:
+            self.samples.append(self.nvml.nvmlDeviceGetClockInfo(self.h, self.nvml.NVML_CLOCK_SM))
+            bits = self._reason_fn(self.h)
+            self.reasons |= {name for bit, name in _REASONS.items() if bits & bit}
+        except Exception:
+            pass
+
+    def __enter__(self):
+        self.sample()
+        self._thread = threading.Thread(target=self._run, daemon=True)
+        self._thread.start()
+        return self
+
+    def __exit__(self, *exc):
+        self.sample()
+        self._stop.set()
+        self._thread.join()
+
+    def summary(self) -> dict:
+        if self.nvml is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "error": getattr(self, "error", "")}
+        return {"sm_mhz": statistics.median(self.samples) if self.samples else None, "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons), "samples": len(self.samples)}
+
+
+# ------------------------------------------------------------------------------------------------------- the layer --
+
+class ReplicaLayer:
+    """Seven compact projections of a Llama-3-8B replica layer, calibrated and selected on the GPU."""
+
+    def __init__(self, seed: int, tokens: int, calib_tokens: int, device: torch.device):
+        from p2pllm_b200 import compact, kernels, wanda
+        self.device, self.tokens = device, tokens
+        self.proj = {p.name: p for p in workloads.LLAMA3_8B}
+        self.inputs, self.tiles, self.methods, self.k = {}, {}, {}, {}
+        self.host_rows = {}
+        calib_ms, select_ms = 0.0, 0.0
+        ev = lambda: torch.cuda.Event(enable_timing=True)
+        for gi, group in enumerate(("attn_in", "attn_out", "mlp_in", "mlp_mid")):
+            names = [n for n, g in INPUT_OF.items() if g == group]
+            cols = self.proj[names[0]].cols
+            g = torch.Generator(device=device).manual_seed(seed * 1000 + gi)
+            scale = workloads.channel_scale(cols, g, device)
+            # Calibration: the hook's reduction over 128 x 2048 synthetic tokens, 16 calls.
+            sums = torch.zeros(cols, dtype=torch.float64, device=device)
+            chunk = max(1, calib_tokens // 16)
+            t_cal = 0.0
+            for _ in range(max(1, calib_tokens // chunk)):
+                xc = (torch.randn(chunk, cols, generator=g, device=device) * scale).bfloat16()
+                a, b = ev(), ev()
+                a.record()
+                kernels.sumsq_cols(xc, sums)
+                b.record()
+                b.synchronize()
+                t_cal += a.elapsed_time(b)
+                del xc
+            calib_ms += t_cal
+            norms = kernels.channel_norms(sums)
+            self.inputs[group] = (torch.randn(tokens, cols, generator=g, device=device) * scale).bfloat16()
+            for n in names:
+                p = self.proj[n]
+                w = workloads.projection_weights(p, seed * 1000 + 17 * (list(self.proj).index(n) + 1), device)
+                a, b = ev(), ev()
+                a.record()
+                values, idx = wanda.select(w, p.keep, norms)
+                b.record()
+                b.synchronize()
+                select_ms += a.elapsed_time(b)
+                del w
+                self.k[n] = values.shape[1]
+                self.tiles[n] = compact.Tiles([("compact", values, idx, p.cols)])
+                self.methods[n] = compact.Compact.__new__(compact.Compact)
+                self.methods[n].tiles = self.tiles[n]
+        self.calib_ms, self.select_ms = calib_ms, select_ms
+        torch.cuda.synchronize(device)
+
+    def algorithmic_bytes(self, n: str, tokens: int) -> int:
+        p = self.proj[n]
+        return p.rows * self.k[n] * (2 + 2) + tokens * p.cols * 2 + tokens * p.rows * 2
+
+    def mask_format_bytes(self, n: str) -> int:
+        p = self.proj[n]
+        return p.rows * self.k[n] * 2 + p.rows * ((p.cols + 31) // 32) * 4
+
+    def step(self, events=None, x=None):
+        """One pass of the layer; with events, records (start, end) around each projection's launch."""
+        x = x or self.inputs
+        outs = {}
+        for i, n in enumerate(self.tiles):
+            if events is not None:
+                events[i][0].record()
+            outs[n] = self.tiles[n](x[INPUT_OF[n]])
+            if events is not None:
+                events[i][1].record()
+        return outs
+
+
+def cpu_layer_time(layer: ReplicaLayer, budget_s: float) -> tuple:
+    """The reference's CPU forward of every projection (F.linear of the unpacked rows, in bf16) on the host cores, on
+    a sample of each projection's rows scaled to all of them. Returns (seconds per layer pass, sample description)."""
+    from oracle import cpu_ref
+    torch.set_num_threads(os.cpu_count() or 1)
+    per = {}
+    first = True
+    frac = 1.0 / 16
+    for n, tiles in layer.tiles.items():
+        _, values, idx = tiles.blocks[0]
+        rows = max(64, int(values.shape[0] * frac))
+        dense = cpu_ref.unpack_rows(values[:rows].cpu(), idx[:rows].cpu(), tiles.cols)
+        x = layer.inputs[INPUT_OF[n]].cpu()
+        cpu_ref.forward(x, dense)                                  # warm-up
+        reps, times = 0, []
+        t_start = time.perf_counter()
+        while reps < 3 or (time.perf_counter() - t_start < budget_s / 7 and reps < 20):
+            t0 = time.perf_counter()
+            cpu_ref.forward(x, dense)
+            times.append(time.perf_counter() - t0)
+            reps += 1
+        per[n] = statistics.median(times) * values.shape[0] / rows
+        first = False
+    sample = (f"rows 1/16 of each projection (>= 64), {layer.tokens} tokens, bf16 F.linear of the unpacked rows, "
+              f"median of >= 3 runs per projection, scaled to all rows")
+    return sum(per.values()), sample
+
+
+# ---------------------------------------------------------------------------------------------------------- driver --
+
+def dist_env():
+    rank = int(os.environ.get("RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", 1))
+    local = int(os.environ.get("LOCAL_RANK", 0))
+    return rank, world, local
+
+
+def max_over_ranks(v: float, world: int, device) -> float:
+    if world == 1:
+        return v
+    import torch.distributed as dist
+    t = torch.tensor([v], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world: int):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def run_reference(args, rank, world):
+    """The reference's CPU forward on the host cores, rank 0 only."""
+    if rank != 0:
+        return
+    from oracle import cpu_ref
+    torch.set_num_threads(os.cpu_count() or 1)
+    cores = torch.get_num_threads()
+    tokens = args.tokens
+    g = torch.Generator().manual_seed(0)
+    projs = list(workloads.LLAMA3_8B)
+    frac = 1.0 / 16
+    mats, xs = {}, {}
+    for p in projs:
+        rows = max(64, int(p.rows * frac))
+        k = max(1, round(p.keep / 100 * p.cols))
+        w = (torch.randn(rows, p.cols, generator=g) * 0.02).bfloat16()
+        # a random k-subset of each row, as a Wanda selection would give: the CPU cost does not depend on which
+        idx = torch.rand(rows, p.cols, generator=g).topk(k, dim=1).indices.sort(dim=1).values
+        mats[p.name] = (cpu_ref.unpack_rows(torch.gather(w, 1, idx), idx, p.cols), p.rows / rows)
+        if INPUT_OF[p.name] not in xs:
+            xs[INPUT_OF[p.name]] = (torch.randn(tokens, p.cols, generator=g) * workloads.channel_scale(p.cols, g)).bfloat16()
+
+    def step():
+        total = 0.0
+        for p in projs:
+            dense, scale = mats[p.name]
+            t0 = time.perf_counter()
+            cpu_ref.forward(xs[INPUT_OF[p.name]], dense)
+            total += (time.perf_counter() - t0) * scale
+        return total
+
+    for _ in range(args.warmup):
+        step()
+    times = [step() for _ in range(args.steps)]
+    layer_s = statistics.median(times)
+    value = tokens / layer_s
+    sample = (f"rows 1/16 of each projection (>= 64), {tokens} tokens, bf16 F.linear of the unpacked rows, "
+              "scaled to all rows; median over steps")
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": layer_s * 1e3, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": "cfg2 Llama-3-8B replica layer (q,k,v,o keep 33; gate,up,down keep 36), T=%d" % tokens,
+                   "tokens": tokens, "path": "reference CPU forward (oracle port of compact.unpack + F.linear)"},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+def run_b200(args, rank, world, local):
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    peaks = measured_peaks()
+    layer = ReplicaLayer(seed=rank, tokens=args.tokens, calib_tokens=args.calib_tokens, device=device)
+    stream = torch.cuda.current_stream(device)
+    n_proj = len(layer.tiles)
+
+    # warm-up
+    for _ in range(args.warmup):
+        layer.step()
+    torch.cuda.synchronize(device)
+
+    # timed region: exactly K steps, per-launch events for the roofline
+    events = [[[torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)] for _ in range(n_proj)]
+              for _ in range(args.steps)]
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier(world)
+    torch.cuda.synchronize(device)
+    clocks = ClockSampler(local)
+    with clocks:
+        start.record(stream)
+        for s in range(args.steps):
+            layer.step(events[s])
+        end.record(stream)
+        torch.cuda.synchronize(device)
+    barrier(world)
+    local_ms = start.elapsed_time(end)
+    total_ms = max_over_ranks(local_ms, world, device)
+    ms_per_step = total_ms / args.steps
+    value = args.tokens * world * args.steps / (total_ms / 1e3)
+
+    names = list(layer.tiles)
+    launch_ms = {n: statistics.mean(events[s][i][0].elapsed_time(events[s][i][1]) for s in range(args.steps))
+                 for i, n in enumerate(names)}
+    alg = {n: layer.algorithmic_bytes(n, args.tokens) for n in names}
+    achieved = sum(alg.values()) / (sum(launch_ms.values()) / 1e3) / 1e9
+    flops = sum(2 * layer.proj[n].rows * layer.k[n] * args.tokens for n in names)
+    traffic = None
+    tpath = os.path.join(ROOT, "profiles", "spmm_traffic.json")
+    if os.path.exists(tpath):
+        with open(tpath) as f:
+            traffic = json.load(f).get("bytes_per_layer_T%d" % args.tokens)
+
+    # e2e through the public API: pinned host inputs in, outputs back to pinned host memory, every step
+    host_x = {g: t.cpu().pin_memory() for g, t in layer.inputs.items()}
+    dev_x = {g: torch.empty_like(t) for g, t in layer.inputs.items()}
+    host_y = {n: torch.empty(args.tokens, layer.proj[n].rows, dtype=torch.bfloat16).pin_memory() for n in names}
+    h2d = sum(t.numel() * t.element_size() for t in host_x.values())
+    d2h = sum(t.numel() * t.element_size() for t in host_y.values())
+
+    def e2e_step():
+        for g in host_x:
+            dev_x[g].copy_(host_x[g], non_blocking=True)
+        for n in names:
+            y = layer.methods[n].apply(None, dev_x[INPUT_OF[n]])
+            host_y[n].copy_(y, non_blocking=True)
+
+    for _ in range(max(3, args.warmup)):
+        e2e_step()
+    torch.cuda.synchronize(device)
+    barrier(world)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for _ in range(args.steps):
+        e2e_step()
+    b.record(stream)
+    torch.cuda.synchronize(device)
+    barrier(world)
+    e2e_ms = max_over_ranks(a.elapsed_time(b), world, device)
+    e2e_value = args.tokens * world * args.steps / (e2e_ms / 1e3)
+
+    # T = 17 (a single draft pass), same layer: reported beside the headline
+    x17 = {g: t[:17].contiguous() for g, t in layer.inputs.items()}
+    for _ in range(3):
+        layer.step(x=x17)
+    ev17 = [[torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)] for _ in range(n_proj)]
+    reps17 = max(10, args.steps // 4)
+    t17 = {n: 0.0 for n in names}
+    for _ in range(reps17):
+        layer.step(events=ev17, x=x17)
+        torch.cuda.synchronize(device)
+        for i, n in enumerate(names):
+            t17[n] += ev17[i][0].elapsed_time(ev17[i][1]) / reps17
+    alg17 = sum(layer.algorithmic_bytes(n, 17) for n in names)
+    ms17 = sum(t17.values())
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        layer_s, sample = cpu_layer_time(layer, budget_s=15.0)
+        cpu = {"value": args.tokens / layer_s, "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port",
+               "sample": sample}
+
+    if rank == 0:
+        weights = sum(layer.proj[n].rows * layer.k[n] * 4 for n in names)
+        out = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,0.02) weights, lognormal-scaled "
+                                                          "N(0,1) activations; no checkpoint or dataset)",
+            "config": {"workload": "cfg2 Llama-3-8B replica layer (q,k,v,o keep 33; gate,up,down keep 36), "
+                                   f"T={args.tokens}", "tokens": args.tokens, "format": "bf16 values + int16 idx",
+                       "weights_bytes_per_gpu": weights,
+                       "l2": "inputs larger than L2: %.0f MB of weights streamed per step vs %d MB L2"
+                             % (weights / 1e6, L2_BYTES >> 20),
+                       "parallelism": f"{world} independent replica layers (one per GPU)"},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                         "frac": achieved / peaks["hbm_gbs"], "traffic": traffic,
+                         "peak_source": peaks["source"], "kernel": "spmm (7 launches a step)",
+                         "algorithmic_bytes_per_step": sum(alg.values()),
+                         "algorithmic_flops_per_step": flops,
+                         "achieved_tflops": flops / (sum(launch_ms.values()) / 1e3) / 1e12},
+            "per_projection_us": {n: launch_ms[n] * 1e3 for n in names},
+            "t17": {"ms_per_pass": ms17, "tokens_per_s": 17 / (ms17 / 1e3), "hbm_gbs": alg17 / (ms17 / 1e3) / 1e9,
+                    "frac": alg17 / (ms17 / 1e3) / 1e9 / peaks["hbm_gbs"],
+                    "per_projection_us": {n: t17[n] * 1e3 for n in names}},
+            "setup": {"calib_ms": layer.calib_ms, "select_ms": layer.select_ms,
+                      "calib_gbs": None},
+            "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+            "gpu_launches": args.steps * n_proj,
+            "clocks": clocks.summary(),
+            "cpu_baseline": cpu,
+            "mask_format_bytes_per_step": sum(layer.mask_format_bytes(n) for n in names),
+        }
+        print(json.dumps(out), flush=True)
+
+
+def main():
+    args = parse()
+    rank, world, local = dist_env()
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+        return
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    try:
+        run_b200(args, rank, world, local)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

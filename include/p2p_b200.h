@@ -1,0 +1,156 @@
+/*
+ * p2p_b200.h -- C ABI of the B200 (sm_100a) replica hot path of p2pLLM.
+ *
+ * Every entry point takes plain device pointers, element counts, strides (in elements) and a CUDA stream passed as
+ * `void*` (a cudaStream_t; NULL is the legacy default stream). Nothing here allocates device memory unless its comment
+ * says so: scratch space is passed in by the caller, sized by the matching *_workspace() query. Entry points launch
+ * asynchronously on the given stream and never synchronise the host, except where a comment says they read a status
+ * word back.
+ *
+ * Return value: P2P_OK (0) or a negative P2P_E* code; p2p_last_error() then holds a message for this host thread.
+ *
+ * Reference interfaces are cited as path:line inside the p2pLLM source tree.
+ */
+#ifndef P2P_B200_H
+#define P2P_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Element types of weights, activations and outputs. */
+enum { P2P_BF16 = 0, P2P_F16 = 1, P2P_F32 = 2 };
+
+/* Status codes. */
+enum {
+    P2P_OK = 0,
+    P2P_EINVAL = -1,      /* a null pointer, a negative size, a stride below the row length, misalignment */
+    P2P_EUNSUPPORTED = -2,/* a dtype or a size this build does not handle (the message names the limit) */
+    P2P_ECUDA = -3,       /* a CUDA runtime error at launch */
+    P2P_EDATA = -4        /* the data broke a format rule (rows of unequal length, a column index out of range) */
+};
+
+/* The message of the last failed call on this host thread ("" if none). */
+const char* p2p_last_error(void);
+/* ABI version: bumped when a signature changes. */
+int p2p_abi_version(void);
+
+/* ------------------------------------------------------------------------------------------------------------------
+ * (1) Wanda calibration and selection
+ * ------------------------------------------------------------------------------------------------------------------ */
+
+/* Bytes of workspace p2p_sumsq_cols needs for this shape (0 if none). */
+size_t p2p_sumsq_workspace(int64_t tokens, int64_t cols, int dtype);
+
+/* sums[c] += (double)(float)(sum_t x[t, c]^2) for x [tokens, cols] (row stride ldx) of `dtype`: each square in fp32,
+ * the column total accumulated in fp64 and rounded to fp32 once per call, as the reference's hook does.
+ * Deterministic: a fixed reduction order, whatever the launch shape.
+ * Replaces p2p/wanda.py:37-40 (Calibration._linear: x.float().pow(2).sum(0).double()) and wanda.py:34-35 (_add).
+ * workspace: p2p_sumsq_workspace() bytes of device memory, zeroed once before its first use (the kernel leaves it
+ * zeroed again); calls that share a workspace must not overlap on the GPU. */
+int p2p_sumsq_cols(const void* x, int dtype, int64_t tokens, int64_t cols, int64_t ldx, double* sums,
+                   void* workspace, size_t workspace_bytes, void* stream);
+
+/* Per-expert sums of squares of the tokens routed to each expert: into[e, c] += (double)(float)sum over the tokens t
+ * whose ids row holds e (each token once per expert) of x[t, c]^2. order: the `tokens * topk` (token, slot) pairs
+ * sorted by expert and then token (order[i] = token * topk + slot), seg: [n_experts + 1] offsets into order per expert.
+ * Replaces the `into` half of p2p/wanda.py:10-20 (expert_inputs). */
+int p2p_expert_sumsq(const void* x, int dtype, int64_t tokens, int64_t cols, int64_t ldx, const int64_t* order,
+                     const int64_t* seg, int64_t topk, int64_t n_experts, double* into, void* stream);
+
+/* norms[g, c] = (float)sqrt(sums[g, c]) for `groups` rows of `cols` sums; with experts != 0 a row whose fp32 norms
+ * add up to 0 becomes all ones (an expert no token reached).
+ * Replaces p2p/wanda.py:63-73 (channel_norms; the rank slice is taken by the caller). */
+int p2p_channel_norms(const double* sums, int64_t groups, int64_t cols, int experts, float* norms, void* stream);
+
+/* Per-row Wanda top-k of w [rows, cols] (row stride ldw): score[r, c] = |float(w[r, c])| * norms[g(r), c] in fp32,
+ * g(r) = r / norm_group_rows (norm_group_rows 0: one norms row for all rows). Keeps the k highest scores of each row,
+ * ties going to the lower column, and writes any of:
+ *   vals [rows, k] (row stride ldo, dtype of w) and idx [rows, k] (int16 if idx_bytes == 2, int32 if 4): the kept
+ *     weights and their columns, in ascending column order;
+ *   words [rows, ceil(cols/32)] int32 (row stride ldwords): bit c%32 of word c/32 set where kept (the reference's
+ *     mask words, p2p/compact.py:36-45);
+ *   mask [rows, cols] uint8 (row stride ldm): 1 where kept;
+ *   pruned [rows, cols] (row stride ldp, dtype of w): w where kept, w * 0.0f elsewhere.
+ * Null outputs are skipped. cols <= 52,000.
+ * Replaces p2p/wanda.py:76-87 (prune, with_mask) and p2p/compact.py:36-45 (pack). */
+int p2p_wanda_select(const void* w, int dtype, int64_t rows, int64_t cols, int64_t ldw, const float* norms,
+                     int64_t norm_group_rows, int64_t k, void* vals, void* idx, int idx_bytes, int64_t ldo,
+                     int32_t* words, int64_t ldwords, uint8_t* mask, int64_t ldm, void* pruned, int64_t ldp,
+                     void* stream);
+
+/* ------------------------------------------------------------------------------------------------------------------
+ * Compact formats: reference mask words <-> values + column indices <-> dense
+ * ------------------------------------------------------------------------------------------------------------------ */
+
+/* idx [rows, k] (ascending columns) from the reference's mask words [rows, ceil(cols/32)] int32. Checks that every
+ * row sets exactly k bits below `cols`; otherwise P2P_EDATA (this call reads one status word back, so it syncs the
+ * stream). Used to load p2p/compact.py:36-45 blocks and p2p/prepare.py:42-73 files. */
+int p2p_words_to_idx(const int32_t* words, int64_t rows, int64_t cols, int64_t ldwords, int64_t k, void* idx,
+                     int idx_bytes, int64_t ldi, void* stream);
+
+/* values [rows, k] + mask words from w [rows, cols] and a uint8 mask that keeps k weights in each row (P2P_EDATA,
+ * after a status read-back, if a row keeps another number). Replaces p2p/compact.py:36-45 (pack). */
+int p2p_pack_mask(const void* w, int dtype, int64_t rows, int64_t cols, int64_t ldw, const uint8_t* mask,
+                  int64_t ldm, int64_t k, void* vals, int64_t ldo, int32_t* words, int64_t ldwords, void* stream);
+
+/* dense [rows, cols] (row stride ldd) from values [rows, k] and either mask words (idx == NULL) or column indices:
+ * kept weights in place, zeros elsewhere. Replaces p2p/compact.py:48-61 (unpack) and the Triton kernel _unpack
+ * (p2p/compact.py:64-85); p2p/compact.py:88-97 (expand) calls it per expert. */
+int p2p_unpack(const void* vals, int dtype, int64_t rows, int64_t k, int64_t ldv, const int32_t* words,
+               int64_t ldwords, const void* idx, int idx_bytes, int64_t ldi, int64_t cols, void* dense, int64_t ldd,
+               void* stream);
+
+/* P2P_OK if every column index of idx [rows, k] (row stride ldi) lies in [0, cols), else P2P_EDATA (reads one status
+ * word back, so it syncs the stream). The GEMMs clamp indices instead of checking them; the host checks once, at
+ * load. Guards what p2p/compact.py:113-166 (Tiles.__init__) assumes of the blocks it is given. */
+int p2p_check_idx(const void* idx, int idx_bytes, int64_t rows, int64_t k, int64_t ldi, int64_t cols, void* stream);
+
+/* ------------------------------------------------------------------------------------------------------------------
+ * (2) Compact sparse GEMM  y[t, r] = sum_j vals[r, j] * x[t, idx[r, j]]
+ * ------------------------------------------------------------------------------------------------------------------ */
+
+/* One row block of a module: rows [row0, row0 + rows) of y read values [rows, k] (row stride ld, dtype of x) and
+ * column indices [rows, k] (same stride; idx == NULL means a dense block, k == cols, column j = j). */
+typedef struct {
+    const void* vals;
+    const void* idx;
+    int64_t row0;
+    int64_t rows;
+    int64_t k;
+    int64_t ld;
+} p2p_row_block;
+
+/* y [tokens, ldy] (columns row0.. of each block) = x [tokens, cols] (row stride ldx) times the blocks' rows, fp32
+ * sums, on CUDA cores straight from the row layout (values + column indices). Any token count. bf16, f16 or f32;
+ * idx_bytes 2 or 4. cols * element size <= 200 KiB.
+ * Replaces p2p/compact.cu:265-278 (spmm) for row-layout weights; p2p/compact.py:192-199 (Tiles.__call__). */
+int p2p_spmm_rows(const void* x, int dtype, int64_t tokens, int64_t cols, int64_t ldx, const p2p_row_block* blocks,
+                  int nblocks, int idx_bytes, void* y, int64_t ldy, void* stream);
+
+/* ------------------------------------------------------------------------------------------------------------------
+ * (3) Group combine epilogue
+ * ------------------------------------------------------------------------------------------------------------------ */
+
+/* out = dtype(float(parts[0]) + sum_{0<k<n-1} dtype(float(parts[k]) - float(h))
+ *                             + dtype(float(parts[n-1]) - float(h_copy)))       (n >= 2; fp32 sums in member order)
+ * over n_elem elements: a group of n layers run in parallel, member k's output parts[k], the last member having
+ * read the replica's h_copy. Replaces p2p/replica.py:81-85 (_member's combine). */
+int p2p_combine(const void* const* parts, int n, const void* h, const void* h_copy, void* out, int dtype,
+                int64_t n_elem, void* stream);
+
+/* out = dtype(sum_k float(parts[k])) in member order (fp32). Replaces p2p/route.py:825-831 (_summed). */
+int p2p_sum_parts(const void* const* parts, int n, void* out, int dtype, int64_t n_elem, void* stream);
+
+/* out = dtype(float(y) - float(x)): a middle or last member's part of a spread step.
+ * Replaces p2p/route.py:1268-1274 (_member's part). */
+int p2p_member_part(const void* y, const void* x, void* out, int dtype, int64_t n_elem, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* P2P_B200_H */

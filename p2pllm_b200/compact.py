@@ -1,0 +1,180 @@
+"""Pruned weights stored and multiplied compactly on B200: the operator API of p2p/compact.py.
+
+A replica's projection keeps the same number k of weights in every row (Wanda). The reference stores each row's kept
+values plus a 1-bit-per-weight mask and multiplies 8 x 8 pieces on mma.sync tensor cores; here each row keeps its
+values plus their column indices (int16 while cols <= 32767), and the GEMM y[t, r] = sum_j v[r, j] * x[t, idx[r, j]]
+runs as hand-written sm_100a kernels (libp2p_b200.so). The reference's block lists and mask words are accepted as they
+are and converted on the GPU at load.
+
+Block list (p2p/compact.py:88-97, prepare.py:201-203), in row order:
+    ("dense", W [rows, cols])                                  kept whole
+    ("sparse", values [rows, k], words [rows, ceil(cols/32)], cols)   the reference's packed form
+    ("compact", values [rows, k], idx [rows, k], cols)          this package's form (values + column indices)
+each with an optional leading expert dimension for routed experts.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import kernels
+from ._lib import P2PError, idx_dtype
+
+__all__ = ["pack", "unpack", "expand", "to_compact", "Tiles", "Compact", "CompactMoE"]
+
+
+def pack(w: torch.Tensor, mask: torch.Tensor) -> tuple:
+    """(values [rows, k], words [rows, ceil(cols / 32)] int32) of w where mask, which keeps the same k in every row.
+    p2p/compact.py:36-45."""
+    return kernels.pack_mask(w, mask)
+
+
+def unpack(values: torch.Tensor, words: torch.Tensor, cols: int) -> torch.Tensor:
+    """The dense matrix pack stored. p2p/compact.py:48-61 (its Triton kernel _unpack, 64-85, is replaced by a CUDA one)."""
+    return kernels.unpack(values, cols, words=words)
+
+
+def _cols(block: tuple) -> int:
+    return block[3] if block[0] in ("sparse", "compact") else block[1].shape[-1]
+
+
+def expand(block: tuple, experts=None) -> torch.Tensor:
+    """A stored row block as a dense matrix, each with a leading expert dimension for routed experts; of those, only
+    `experts` (ids), if given. p2p/compact.py:88-97."""
+    if block[0] == "dense":
+        return block[1] if experts is None else block[1][experts]
+    kind, values, meta, cols = block
+    if experts is not None:
+        values, meta = values[experts], meta[experts]
+    lead = values.shape[:-1]
+    v2 = values.reshape(-1, values.shape[-1])
+    m2 = meta.reshape(-1, meta.shape[-1])
+    dense = kernels.unpack(v2, cols, words=m2) if kind == "sparse" else kernels.unpack(v2, cols, idx=m2)
+    return dense.view(*lead, cols)
+
+
+def to_compact(block: tuple) -> tuple:
+    """A block as ("dense", W) or ("compact", values, idx, cols): mask words become column indices (on the GPU,
+    checking that every row keeps k); column indices are range-checked once here, so the GEMMs need not."""
+    if block[0] == "dense":
+        return block
+    kind, values, meta, cols = block
+    if kind == "sparse":
+        k = values.shape[-1]
+        idx = kernels.words_to_idx(meta.reshape(-1, meta.shape[-1]), cols, k).view(*values.shape[:-1], k)
+        return ("compact", values, idx, cols)
+    if kind == "compact":
+        kernels.check_idx(meta, cols)
+        return block
+    raise P2PError(f"unknown block kind {kind!r}")
+
+
+def _nbytes(blocks) -> int:
+    return sum(t.numel() * t.element_size() for b in blocks for t in b[1:] if torch.is_tensor(t))
+
+
+class Tiles:
+    """A module's row blocks on the GPU, as the compact GEMM reads them; calling it multiplies tokens by them.
+    The B200 counterpart of p2p/compact.py:113-202 (Tiles): no re-tiling into 8 x 8 pieces and no load-time tuning
+    run; rows keep values + column indices, dense blocks keep their weights."""
+
+    @staticmethod
+    def usable(blocks: list) -> bool:
+        """CUDA tensors of bf16, f16 or f32, 2-D blocks (p2p/compact.py:117-122 asks for the same, less fp32, plus
+        columns in multiples of 8, which this kernel does not need)."""
+        t = blocks[0][1]
+        return t.is_cuda and t.dtype in (torch.bfloat16, torch.float16, torch.float32) and t.dim() == 2
+
+    def __init__(self, blocks: list):
+        if not blocks:
+            raise P2PError("a module needs at least one row block")
+        blocks = [to_compact(b) for b in blocks]
+        self.cols = _cols(blocks[0])
+        self.dtype = blocks[0][1].dtype
+        self.device = blocks[0][1].device
+        self.blocks, row0 = [], 0
+        kinds = set()
+        for b in blocks:
+            if _cols(b) != self.cols:
+                raise P2PError("every block of a module has the same columns")
+            if b[1].dtype != self.dtype or b[1].dim() != 2:
+                raise P2PError("blocks share one dtype and are 2-D")
+            values = b[1].contiguous()
+            idx = b[2].contiguous() if b[0] == "compact" else None
+            if idx is not None:
+                kinds.add(idx.dtype)
+            self.blocks.append((row0, values, idx))
+            row0 += values.shape[0]
+        if len(kinds) > 1:                        # one index width for the whole module
+            want = idx_dtype(self.cols)
+            self.blocks = [(r, v, None if i is None else i.to(want)) for r, v, i in self.blocks]
+        self.rows = row0
+
+    def __call__(self, x: torch.Tensor) -> torch.Tensor:
+        """x [T, cols] @ W.T: [T, rows]. Any T (the reference launches at most 64 tokens at a time)."""
+        if x.dtype != self.dtype:
+            raise P2PError(f"x is {x.dtype}, the weights {self.dtype}")
+        return kernels.spmm_rows(x, self.blocks, self.cols, self.rows)
+
+    def nbytes(self) -> int:
+        return sum(t.numel() * t.element_size() for _, v, i in self.blocks for t in (v, i) if t is not None)
+
+
+class Compact:
+    """A linear module's quant_method for a replica: its row blocks as Tiles. SGLang's linear layers call
+    quant_method.apply(layer, x, bias). p2p/compact.py:205-224."""
+
+    def __init__(self, blocks: list):
+        assert Tiles.usable(blocks), ("a compact replica needs CUDA tensors of bfloat16, float16 or float32 and "
+                                      "libp2p_b200.so")
+        self.tiles = Tiles(blocks)
+
+    def apply(self, layer, x: torch.Tensor, bias=None) -> torch.Tensor:
+        out = self.tiles(x.reshape(-1, x.shape[-1]))
+        if bias is not None:
+            out = out + bias
+        return out.reshape(*x.shape[:-1], out.shape[-1])
+
+    def process_weights_after_loading(self, layer) -> None:
+        pass
+
+    def nbytes(self) -> int:
+        return self.tiles.nbytes()
+
+
+class CompactMoE(torch.nn.Module):
+    """A FusedMoE's quant_method for compact routed experts ({weight name: row blocks with a leading expert
+    dimension}): each pass expands only the experts in use, and the layer's own method runs them.
+    p2p/compact.py:227-262, with the expansion on this package's CUDA kernel instead of Triton."""
+
+    def __init__(self, method, weights: dict):
+        super().__init__()
+        self.method, self.weights = method, weights
+
+    def __getattr__(self, name):
+        try:
+            return super().__getattr__(name)
+        except AttributeError:
+            return getattr(super().__getattr__("method"), name)
+
+    def apply(self, layer, dispatch_output):
+        topk = dispatch_output.topk_output
+        ids = topk.topk_ids
+        used = torch.unique(ids[ids >= 0])                     # sorted ids of the experts this pass reaches
+        # Each routed id becomes its position among the used experts; -1 (no expert) stays -1.
+        local = torch.searchsorted(used, ids.clamp(min=0)).to(ids.dtype)
+        local = torch.where(ids >= 0, local, ids)
+        swapped = {name: torch.nn.Parameter(torch.cat([expand(b, used) for b in blocks], dim=-2), requires_grad=False)
+                   for name, blocks in self.weights.items()}
+        saved = {name: layer._parameters[name] for name in swapped}
+        layer._parameters.update(swapped)
+        try:
+            routed = dispatch_output._replace(topk_output=topk._replace(topk_ids=local))
+            return self.method.apply(layer, routed)
+        finally:
+            layer._parameters.update(saved)              # the layer's own (empty) weights are back
+
+    def process_weights_after_loading(self, layer) -> None:
+        pass
+
+    def nbytes(self) -> int:
+        return sum(_nbytes(blocks) for blocks in self.weights.values())

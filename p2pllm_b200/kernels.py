@@ -1,0 +1,236 @@
+"""Tensor-level wrappers of the C ABI: shape and device checks, outputs allocated with torch, launches on the current
+stream of the inputs' device. Each function names the reference interface it serves."""
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from . import _lib
+from ._lib import P2PError, call, dtype_code, ptr, require_cuda, stream_of
+
+_workspaces: dict = {}
+
+
+def _workspace(device: torch.device, nbytes: int) -> torch.Tensor:
+    """A zeroed per-device scratch buffer of at least nbytes (the kernels leave it zeroed again)."""
+    key = (device.type, device.index)
+    ws = _workspaces.get(key)
+    if ws is None or ws.numel() < nbytes:
+        ws = torch.zeros(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
+        _workspaces[key] = ws
+    return ws
+
+
+def _rows2d(x: torch.Tensor) -> torch.Tensor:
+    x = x.reshape(-1, x.shape[-1])
+    if x.stride(-1) != 1:
+        x = x.contiguous()
+    return x
+
+
+def sumsq_cols(x: torch.Tensor, sums: torch.Tensor) -> torch.Tensor:
+    """sums += x.float().pow(2).sum(0).double() over x [..., cols] (p2p/wanda.py:37-40). sums: float64 [cols]."""
+    require_cuda(x, sums)
+    x = _rows2d(x)
+    if sums.dtype != torch.float64 or sums.numel() != x.shape[1] or not sums.is_contiguous():
+        raise P2PError("sums must be a contiguous float64 vector of x's columns")
+    lib = _lib.load()
+    need = lib.p2p_sumsq_workspace(x.shape[0], x.shape[1], dtype_code(x))
+    ws = _workspace(x.device, need) if need else None
+    call("p2p_sumsq_cols", ptr(x), dtype_code(x), x.shape[0], x.shape[1], x.stride(0), ptr(sums), ptr(ws),
+         0 if ws is None else ws.numel(), stream_of(x))
+    return sums
+
+
+def expert_sumsq(x: torch.Tensor, ids: torch.Tensor, into: torch.Tensor) -> torch.Tensor:
+    """into[e] += fp32 sum of x[t]^2 over the tokens routed to e, each once (the `into` half of p2p/wanda.py:10-20).
+    ids: [tokens, topk] expert ids (negative = none)."""
+    require_cuda(x, ids, into)
+    x = _rows2d(x)
+    n_exp = into.shape[0]
+    if into.dtype != torch.float64 or into.shape[-1] != x.shape[1] or not into.is_contiguous():
+        raise P2PError("into must be contiguous float64 [experts, cols]")
+    topk = ids.shape[-1]
+    flat = ids.reshape(-1).to(torch.int64)
+    flat = torch.where((flat >= 0) & (flat < n_exp), flat, torch.full_like(flat, n_exp))
+    # (token, slot) pairs grouped by expert, tokens ascending inside an expert: a stable sort of the expert ids.
+    order = torch.sort(flat, stable=True).indices
+    counts = torch.bincount(flat, minlength=n_exp + 1)[:n_exp]
+    seg = torch.zeros(n_exp + 1, dtype=torch.int64, device=x.device)
+    seg[1:] = counts.cumsum(0)
+    call("p2p_expert_sumsq", ptr(x), dtype_code(x), x.shape[0], x.shape[1], x.stride(0), ptr(order), ptr(seg), topk,
+         n_exp, ptr(into), stream_of(x))
+    return into
+
+
+def channel_norms(sums: torch.Tensor) -> torch.Tensor:
+    """sums.sqrt().float(); for [experts, cols] sums a row of zeros gives ones, shaped [experts, 1, cols]
+    (p2p/wanda.py:63-73)."""
+    require_cuda(sums)
+    sums = sums.to(torch.float64).contiguous()
+    experts = sums.dim() == 2
+    groups = sums.shape[0] if experts else 1
+    norms = torch.empty(sums.shape, dtype=torch.float32, device=sums.device)
+    call("p2p_channel_norms", ptr(sums), groups, sums.shape[-1], int(experts), ptr(norms), stream_of(sums))
+    return norms[:, None, :] if experts else norms
+
+
+def wanda_select(w: torch.Tensor, norms: torch.Tensor, k: int, *, values: bool = True, idx: bool = True,
+                 words: bool = False, mask: bool = False, pruned: bool = False, idx_dtype=None) -> dict:
+    """Per-row top-k of |w| * norms, ties to the lower column (p2p/wanda.py:76-87 + p2p/compact.py:36-45).
+    w: [rows, cols] or [experts, rows, cols] with norms [experts, 1, cols]. Returns the requested outputs among
+    values [.., k], idx [.., k] (int16 while cols <= 32767), words [.., ceil(cols/32)] int32, mask (bool) and pruned."""
+    require_cuda(w, norms)
+    lead, cols = w.shape[:-1], w.shape[-1]
+    w2 = w.reshape(-1, cols)
+    if w2.stride(-1) != 1:
+        w2 = w2.contiguous()
+    rows = w2.shape[0]
+    norms = norms.to(torch.float32).contiguous()
+    if norms.numel() == cols:
+        group_rows = 0
+    elif w.dim() == 3 and norms.numel() == w.shape[0] * cols:
+        group_rows = w.shape[1]
+    else:
+        raise P2PError(f"norms of {tuple(norms.shape)} do not fit w of {tuple(w.shape)}")
+    dev = w.device
+    idt = idx_dtype or _lib.idx_dtype(cols)
+    out = {}
+    v = torch.empty(rows, k, dtype=w.dtype, device=dev) if values else None
+    ix = torch.empty(rows, k, dtype=idt, device=dev) if idx else None
+    wd = torch.empty(rows, (cols + 31) // 32, dtype=torch.int32, device=dev) if words else None
+    m = torch.empty(rows, cols, dtype=torch.bool, device=dev) if mask else None
+    p = torch.empty(rows, cols, dtype=w.dtype, device=dev) if pruned else None
+    call("p2p_wanda_select", ptr(w2), dtype_code(w2), rows, cols, w2.stride(0), ptr(norms), group_rows, k,
+         ptr(v), ptr(ix), _lib.IDX_BYTES[idt], k, ptr(wd), 0 if wd is None else wd.shape[1],
+         ptr(m), cols, ptr(p), cols, stream_of(w2))
+    for name, t in (("values", v), ("idx", ix), ("words", wd), ("mask", m), ("pruned", p)):
+        if t is not None:
+            out[name] = t.view(*lead, *t.shape[1:])
+    return out
+
+
+def words_to_idx(words: torch.Tensor, cols: int, k: int, idx_dtype=None) -> torch.Tensor:
+    """Column indices [rows, k] of the reference's mask words (p2p/compact.py:36-45); raises if a row keeps another
+    number of columns."""
+    require_cuda(words)
+    words = words.reshape(-1, words.shape[-1]).contiguous()
+    idt = idx_dtype or _lib.idx_dtype(cols)
+    idx = torch.empty(words.shape[0], k, dtype=idt, device=words.device)
+    call("p2p_words_to_idx", ptr(words), words.shape[0], cols, words.stride(0), k, ptr(idx), _lib.IDX_BYTES[idt], k,
+         stream_of(words))
+    return idx
+
+
+def pack_mask(w: torch.Tensor, mask: torch.Tensor):
+    """(values [rows, k], words) from w and a bool mask that keeps the same k in every row (p2p/compact.py:36-45)."""
+    require_cuda(w, mask)
+    rows, cols = w.shape
+    w = w.contiguous()
+    m = mask.contiguous().view(torch.uint8)
+    k = int(mask[0].sum()) if rows else 0
+    values = torch.empty(rows, k, dtype=w.dtype, device=w.device)
+    words = torch.empty(rows, (cols + 31) // 32, dtype=torch.int32, device=w.device)
+    try:
+        call("p2p_pack_mask", ptr(w), dtype_code(w), rows, cols, w.stride(0), ptr(m), m.stride(0), k, ptr(values),
+             k, ptr(words), words.shape[1], stream_of(w))
+    except P2PError as e:
+        raise AssertionError("every row must keep the same number of weights") from e
+    return values, words
+
+
+def unpack(values: torch.Tensor, cols: int, words: torch.Tensor | None = None,
+           idx: torch.Tensor | None = None) -> torch.Tensor:
+    """Dense [rows, cols] from values [rows, k] and mask words or column indices (p2p/compact.py:48-85)."""
+    require_cuda(values, words, idx)
+    rows, k = values.shape
+    values = values.contiguous()
+    dense = torch.empty(rows, cols, dtype=values.dtype, device=values.device)
+    if words is not None:
+        words = words.contiguous()
+        call("p2p_unpack", ptr(values), dtype_code(values), rows, k, values.stride(0), ptr(words), words.stride(0),
+             None, 0, 0, cols, ptr(dense), cols, stream_of(values))
+    else:
+        idx = idx.contiguous()
+        call("p2p_unpack", ptr(values), dtype_code(values), rows, k, values.stride(0), None, 0, ptr(idx),
+             _lib.IDX_BYTES[idx.dtype], idx.stride(0), cols, ptr(dense), cols, stream_of(values))
+    return dense
+
+
+def check_idx(idx: torch.Tensor, cols: int) -> None:
+    """Raises unless every column index lies in [0, cols)."""
+    require_cuda(idx)
+    idx = idx.reshape(-1, idx.shape[-1]).contiguous()
+    call("p2p_check_idx", ptr(idx), _lib.IDX_BYTES[idx.dtype], idx.shape[0], idx.shape[1], idx.stride(0), cols,
+         stream_of(idx))
+
+
+def spmm_rows(x: torch.Tensor, blocks: list, cols: int, out_rows: int, out: torch.Tensor | None = None) -> torch.Tensor:
+    """y [tokens, out_rows] = x [tokens, cols] times row blocks (CUDA cores). blocks: (row0, values, idx | None) with
+    values [rows, k] (k == cols when idx is None: a dense block). Replaces p2p/compact.cu:265-278 for row layouts."""
+    require_cuda(x)
+    if x.dim() != 2 or x.shape[1] != cols:
+        raise P2PError(f"x of {tuple(x.shape)} does not have {cols} columns")
+    if x.stride(1) != 1:
+        x = x.contiguous()
+    if out is None:
+        out = torch.empty(x.shape[0], out_rows, dtype=x.dtype, device=x.device)
+    table = (_lib.RowBlock * len(blocks))()
+    idx_bytes = 2
+    for i, (row0, v, ix) in enumerate(blocks):
+        if v.dtype != x.dtype:
+            raise P2PError(f"values {v.dtype} differ from x {x.dtype}")
+        if ix is not None:
+            idx_bytes = _lib.IDX_BYTES[ix.dtype]
+        table[i] = _lib.RowBlock(v.data_ptr(), None if ix is None else ix.data_ptr(), row0, v.shape[0], v.shape[1],
+                                 v.stride(0))
+    kinds = {_lib.IDX_BYTES[ix.dtype] for _, _, ix in blocks if ix is not None}
+    if len(kinds) > 1:
+        raise P2PError("all row blocks of a module use one index type")
+    call("p2p_spmm_rows", ptr(x), dtype_code(x), x.shape[0], cols, x.stride(0), table, len(blocks), idx_bytes,
+         ptr(out), out.stride(0), stream_of(x))
+    return out
+
+
+def _ptr_array(ts) -> ctypes.Array:
+    arr = (ctypes.c_void_p * len(ts))()
+    for i, t in enumerate(ts):
+        arr[i] = t.data_ptr()
+    return arr
+
+
+def _same(ts, ref: torch.Tensor) -> list:
+    out = []
+    for t in ts:
+        require_cuda(t)
+        if t.shape != ref.shape or t.dtype != ref.dtype:
+            raise P2PError(f"part of {tuple(t.shape)} {t.dtype} differs from {tuple(ref.shape)} {ref.dtype}")
+        out.append(t.contiguous())
+    return out
+
+
+def combine(parts: list, h: torch.Tensor, h_copy: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """h' = l_0(h) + sum_mid dtype(l_k(h) - h) + dtype(l_last(h~) - h~), fp32 sums (p2p/replica.py:81-85)."""
+    parts = _same(parts, h)
+    h, h_copy = _same([h, h_copy], h)
+    out = torch.empty_like(h) if out is None else out
+    call("p2p_combine", _ptr_array(parts), len(parts), ptr(h), ptr(h_copy), ptr(out), dtype_code(h), h.numel(),
+         stream_of(h))
+    return out
+
+
+def sum_parts(parts: list, out: torch.Tensor | None = None) -> torch.Tensor:
+    """dtype(sum of the parts in fp32, member order) (p2p/route.py:825-831)."""
+    parts = _same(parts, parts[0])
+    out = torch.empty_like(parts[0]) if out is None else out
+    call("p2p_sum_parts", _ptr_array(parts), len(parts), ptr(out), dtype_code(out), out.numel(), stream_of(out))
+    return out
+
+
+def member_part(y: torch.Tensor, x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """dtype(float(y) - float(x)) (p2p/route.py:1268-1274)."""
+    y, x = _same([y, x], y)
+    out = torch.empty_like(y) if out is None else out
+    call("p2p_member_part", ptr(y), ptr(x), ptr(out), dtype_code(y), y.numel(), stream_of(y))
+    return out

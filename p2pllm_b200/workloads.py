@@ -1,0 +1,80 @@
+"""Seeded synthetic workloads with the shapes and value distributions of the five benchmark configurations.
+
+No checkpoints or datasets are used: weights are N(0, 0.02), calibration and forward activations are N(0, 1) scaled
+per input channel by lognormal(0, 1), generated from fixed seeds, on the CPU generator (reproducible on any machine
+with the same torch) or on the device for the large configurations.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+
+
+@dataclass(frozen=True)
+class Projection:
+    name: str
+    rows: int
+    cols: int
+    keep: float
+
+
+# Llama-3-8B: q, o 4096x4096; k, v 1024x4096 (GQA, 8 KV heads); gate, up 14336x4096; down 4096x14336.
+LLAMA3_8B = (
+    Projection("q", 4096, 4096, 33), Projection("k", 1024, 4096, 33), Projection("v", 1024, 4096, 33),
+    Projection("o", 4096, 4096, 33), Projection("gate", 14336, 4096, 36), Projection("up", 14336, 4096, 36),
+    Projection("down", 4096, 14336, 36),
+)
+
+# Qwen2.5-32B: hidden 5120, intermediate 27648, 40 query / 8 KV heads of 128.
+QWEN25_32B = (
+    Projection("q", 5120, 5120, 40), Projection("k", 1024, 5120, 40), Projection("v", 1024, 5120, 40),
+    Projection("o", 5120, 5120, 40), Projection("gate", 27648, 5120, 40), Projection("up", 27648, 5120, 40),
+    Projection("down", 5120, 27648, 40),
+)
+
+
+def channel_scale(cols: int, generator: torch.Generator, device="cpu") -> torch.Tensor:
+    """lognormal(0, 1) per input channel."""
+    return torch.exp(torch.randn(cols, generator=generator, device=device))
+
+
+@dataclass
+class Config1:
+    """CPU-runnable single projection: W [2048, 2048] fp32 ~ N(0, 0.02), keep 40, a 17-token forward batch, calibration
+    from 128 x 512 tokens in 16 calls of 4096 tokens; seed 0."""
+    w: torch.Tensor
+    scale: torch.Tensor
+    x: torch.Tensor
+    seed: int
+    keep: float = 40.0
+    calib_tokens: int = 128 * 512
+    calib_call: int = 4096
+
+    def calib_chunks(self, device="cpu"):
+        """The calibration activations, one hook call at a time."""
+        g = torch.Generator().manual_seed(self.seed + 1)
+        for _ in range(self.calib_tokens // self.calib_call):
+            yield (torch.randn(self.calib_call, self.w.shape[1], generator=g) * self.scale).to(device)
+
+
+def config1(seed: int = 0, rows: int = 2048, cols: int = 2048, tokens: int = 17) -> Config1:
+    g = torch.Generator().manual_seed(seed)
+    w = torch.randn(rows, cols, generator=g) * 0.02
+    scale = channel_scale(cols, g)
+    x = torch.randn(tokens, cols, generator=g) * scale
+    return Config1(w=w, scale=scale, x=x, seed=seed)
+
+
+def projection_weights(p: Projection, seed: int, device, dtype=torch.bfloat16) -> torch.Tensor:
+    """W [rows, cols] ~ N(0, 0.02) in dtype, generated on `device`."""
+    g = torch.Generator(device=device).manual_seed(seed)
+    return (torch.randn(p.rows, p.cols, generator=g, device=device) * 0.02).to(dtype)
+
+
+def activations(cols: int, tokens: int, seed: int, device, dtype=torch.bfloat16, scale=None) -> torch.Tensor:
+    """x [tokens, cols] ~ N(0, 1) times a per-channel lognormal scale (its own, from `seed`, unless given)."""
+    g = torch.Generator(device=device).manual_seed(seed)
+    if scale is None:
+        scale = channel_scale(cols, g, device)
+    return (torch.randn(tokens, cols, generator=g, device=device) * scale).to(dtype)

@@ -1,0 +1,68 @@
+"""The C ABI without a GPU: the library loads, exports every function include/p2p_b200.h declares, and rejects bad
+arguments with a status and a message before touching the device."""
+import ctypes
+import os
+import re
+
+import pytest
+
+from p2pllm_b200 import _lib
+
+HEADER = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "include", "p2p_b200.h")
+
+
+def declared() -> set:
+    text = re.sub(r"/\*.*?\*/", "", open(HEADER).read(), flags=re.S)
+    return set(re.findall(r"\b(p2p_[a-z0-9_]+)\s*\(", text))
+
+
+@pytest.fixture(scope="module")
+def lib():
+    if not os.path.exists(_lib.LIB_PATH):
+        from p2pllm_b200 import build
+        build.build()
+    return _lib.load()
+
+
+def test_every_declared_symbol_is_exported(lib):
+    names = declared()
+    assert len(names) >= 15
+    missing = [n for n in names if not hasattr(lib, n)]
+    assert not missing, missing
+
+
+def test_every_declared_symbol_has_a_binding():
+    assert declared() <= set(_lib.SIGNATURES)
+
+
+def test_abi_version(lib):
+    assert lib.p2p_abi_version() == 1
+
+
+def test_bad_arguments_give_a_status_and_a_message(lib):
+    st = lib.p2p_spmm_rows(None, 0, 4, 8, 8, None, 0, 2, None, 4, None)
+    assert st == -1 and b"row blocks" in lib.p2p_last_error()
+    st = lib.p2p_wanda_select(None, 0, 4, 8, 8, None, 0, 9, None, None, 2, 9, None, 0, None, 0, None, 0, None)
+    assert st == -1 and b"k=9" in lib.p2p_last_error()
+    st = lib.p2p_combine(None, 1, None, None, None, 0, 4, None)
+    assert st == -1 and b"at least 2" in lib.p2p_last_error()
+    st = lib.p2p_wanda_select(None, 0, 4, 60000, 60000, None, 0, 9, None, None, 4, 9, None, 0, None, 0, None, 0, None)
+    assert st == -2 and b"at most" in lib.p2p_last_error()
+
+
+def test_empty_work_is_a_no_op(lib):
+    assert lib.p2p_sumsq_cols(None, 0, 0, 16, 16, None, None, 0, None) == 0
+    assert lib.p2p_member_part(None, None, None, 0, 0, None) == 0
+
+
+def test_workspace_query_is_host_only(lib):
+    assert lib.p2p_sumsq_workspace(0, 10, 0) == 0
+    assert lib.p2p_sumsq_workspace(262144, 4096, 0) > 0
+    assert lib.p2p_sumsq_workspace(100, 4096, 9) == 0
+
+
+def test_cpu_tensors_are_refused():
+    import torch
+    from p2pllm_b200 import P2PError, kernels
+    with pytest.raises(P2PError, match="CUDA"):
+        kernels.combine([torch.zeros(4), torch.zeros(4)], torch.zeros(4), torch.zeros(4))
