@@ -3,8 +3,9 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference] [--tokens T]
 
-A step is one forward pass of the replica layer's seven compact projections (q, k, v, o at keep 33; gate, up, down at
-keep 36; values bf16 + int16 column indices) over a batch of T = 272 tokens (16 sequences x 17 draft-pass tokens).
+A step is one forward pass of the replica layer's compact projections (q, k, v, o at keep 33; gate, up, down at keep
+36; 4 bytes a kept weight) over a batch of T = 272 tokens (16 sequences x 17 draft-pass tokens), module by module as
+SGLang holds them: qkv_proj, o_proj, gate_up_proj, down_proj, each one Compact (one kernel launch).
 Weights are N(0, 0.02), activations N(0, 1) times a lognormal per-channel scale, all seeded and synthetic; the
 calibration sums come from 128 x 2048 synthetic tokens per projection input through the package's own calibration
 kernel, and the selection from its Wanda top-k kernel.
@@ -37,9 +38,10 @@ from p2pllm_b200 import workloads  # noqa: E402
 
 METRIC = "replica sparse-GEMM tokens/s (Llama-3-8B replica layer, keep 33/36, T=272)"
 UNIT = "tokens/s"
-# Which synthetic activation each projection reads: q/k/v share the attention input, gate/up the MLP input.
-INPUT_OF = {"q": "attn_in", "k": "attn_in", "v": "attn_in", "o": "attn_out", "gate": "mlp_in", "up": "mlp_in",
-            "down": "mlp_mid"}
+# The layer's linear modules as SGLang holds them (fused q/k/v and gate/up), the input each reads, and their blocks.
+MODULES = {"qkv_proj": ("attn_in", ("q", "k", "v")), "o_proj": ("attn_out", ("o",)),
+           "gate_up_proj": ("mlp_in", ("gate", "up")), "down_proj": ("mlp_mid", ("down",))}
+INPUT_OF = {n: group for group, names in MODULES.values() for n in names}
 L2_BYTES = 126 * 1024 * 1024
 
 
@@ -127,25 +129,23 @@ class ClockSampler:
 # ------------------------------------------------------------------------------------------------------- the layer --
 
 class ReplicaLayer:
-    """Seven compact projections of a Llama-3-8B replica layer, calibrated and selected on the GPU."""
+    """A Llama-3-8B replica layer's four linear modules, each a Compact over its projections' blocks, calibrated and
+    selected on the GPU."""
 
     def __init__(self, seed: int, tokens: int, calib_tokens: int, device: torch.device):
         from p2pllm_b200 import compact, kernels, wanda
         self.device, self.tokens = device, tokens
         self.proj = {p.name: p for p in workloads.LLAMA3_8B}
-        self.inputs, self.tiles, self.methods, self.k = {}, {}, {}, {}
-        self.host_rows = {}
-        calib_ms, select_ms = 0.0, 0.0
+        self.inputs, self.methods, self.k = {}, {}, {}
+        calib_ms, select_ms, calib_bytes = 0.0, 0.0, 0
         ev = lambda: torch.cuda.Event(enable_timing=True)
-        for gi, group in enumerate(("attn_in", "attn_out", "mlp_in", "mlp_mid")):
-            names = [n for n, g in INPUT_OF.items() if g == group]
+        for gi, (module, (group, names)) in enumerate(MODULES.items()):
             cols = self.proj[names[0]].cols
             g = torch.Generator(device=device).manual_seed(seed * 1000 + gi)
             scale = workloads.channel_scale(cols, g, device)
-            # Calibration: the hook's reduction over 128 x 2048 synthetic tokens, 16 calls.
+            # Calibration: the hook's reduction over 128 x 2048 synthetic tokens, in 16 calls.
             sums = torch.zeros(cols, dtype=torch.float64, device=device)
             chunk = max(1, calib_tokens // 16)
-            t_cal = 0.0
             for _ in range(max(1, calib_tokens // chunk)):
                 xc = (torch.randn(chunk, cols, generator=g, device=device) * scale).bfloat16()
                 a, b = ev(), ev()
@@ -153,11 +153,12 @@ class ReplicaLayer:
                 kernels.sumsq_cols(xc, sums)
                 b.record()
                 b.synchronize()
-                t_cal += a.elapsed_time(b)
+                calib_ms += a.elapsed_time(b)
+                calib_bytes += xc.numel() * 2
                 del xc
-            calib_ms += t_cal
             norms = kernels.channel_norms(sums)
             self.inputs[group] = (torch.randn(tokens, cols, generator=g, device=device) * scale).bfloat16()
+            blocks = []
             for n in names:
                 p = self.proj[n]
                 w = workloads.projection_weights(p, seed * 1000 + 17 * (list(self.proj).index(n) + 1), device)
@@ -169,28 +170,37 @@ class ReplicaLayer:
                 select_ms += a.elapsed_time(b)
                 del w
                 self.k[n] = values.shape[1]
-                self.tiles[n] = compact.Tiles([("compact", values, idx, p.cols)])
-                self.methods[n] = compact.Compact.__new__(compact.Compact)
-                self.methods[n].tiles = self.tiles[n]
-        self.calib_ms, self.select_ms = calib_ms, select_ms
+                blocks.append(("compact", values, idx, p.cols))
+            self.methods[module] = compact.Compact(blocks)
+        self.calib_ms, self.select_ms, self.calib_bytes = calib_ms, select_ms, calib_bytes
         torch.cuda.synchronize(device)
 
-    def algorithmic_bytes(self, n: str, tokens: int) -> int:
-        p = self.proj[n]
-        return p.rows * self.k[n] * (2 + 2) + tokens * p.cols * 2 + tokens * p.rows * 2
+    def rows(self, module: str) -> int:
+        return sum(self.proj[n].rows for n in MODULES[module][1])
 
-    def mask_format_bytes(self, n: str) -> int:
-        p = self.proj[n]
-        return p.rows * self.k[n] * 2 + p.rows * ((p.cols + 31) // 32) * 4
+    def cols(self, module: str) -> int:
+        return self.proj[MODULES[module][1][0]].cols
+
+    def algorithmic_bytes(self, module: str, tokens: int) -> int:
+        """Values + indices (2 + 2 bytes a kept weight), x and y, each once."""
+        weights = sum(self.proj[n].rows * self.k[n] * 4 for n in MODULES[module][1])
+        return weights + tokens * self.cols(module) * 2 + tokens * self.rows(module) * 2
+
+    def flops(self, module: str, tokens: int) -> int:
+        return sum(2 * self.proj[n].rows * self.k[n] * tokens for n in MODULES[module][1])
+
+    def mask_format_bytes(self, module: str) -> int:
+        return sum(self.proj[n].rows * self.k[n] * 2 + self.proj[n].rows * ((self.proj[n].cols + 31) // 32) * 4
+                   for n in MODULES[module][1])
 
     def step(self, events=None, x=None):
-        """One pass of the layer; with events, records (start, end) around each projection's launch."""
+        """One pass of the layer; with events, records (start, end) around each module's launch."""
         x = x or self.inputs
         outs = {}
-        for i, n in enumerate(self.tiles):
+        for i, (module, (group, _)) in enumerate(MODULES.items()):
             if events is not None:
                 events[i][0].record()
-            outs[n] = self.tiles[n](x[INPUT_OF[n]])
+            outs[module] = self.methods[module].apply(None, x[group])
             if events is not None:
                 events[i][1].record()
         return outs
@@ -201,27 +211,28 @@ def cpu_layer_time(layer: ReplicaLayer, budget_s: float) -> tuple:
     a sample of each projection's rows scaled to all of them. Returns (seconds per layer pass, sample description)."""
     from oracle import cpu_ref
     torch.set_num_threads(os.cpu_count() or 1)
-    per = {}
-    first = True
+    g = torch.Generator().manual_seed(0)
+    total = 0.0
     frac = 1.0 / 16
-    for n, tiles in layer.tiles.items():
-        _, values, idx = tiles.blocks[0]
-        rows = max(64, int(values.shape[0] * frac))
-        dense = cpu_ref.unpack_rows(values[:rows].cpu(), idx[:rows].cpu(), tiles.cols)
-        x = layer.inputs[INPUT_OF[n]].cpu()
-        cpu_ref.forward(x, dense)                                  # warm-up
-        reps, times = 0, []
-        t_start = time.perf_counter()
-        while reps < 3 or (time.perf_counter() - t_start < budget_s / 7 and reps < 20):
-            t0 = time.perf_counter()
-            cpu_ref.forward(x, dense)
-            times.append(time.perf_counter() - t0)
-            reps += 1
-        per[n] = statistics.median(times) * values.shape[0] / rows
-        first = False
+    for module, (group, names) in MODULES.items():
+        x = layer.inputs[group].cpu()
+        for n in names:
+            p = layer.proj[n]
+            rows = max(64, int(p.rows * frac))
+            k = layer.k[n]
+            w = (torch.randn(rows, p.cols, generator=g) * 0.02).bfloat16()
+            idx = torch.rand(rows, p.cols, generator=g).topk(k, dim=1).indices.sort(dim=1).values
+            dense = cpu_ref.unpack_rows(torch.gather(w, 1, idx), idx, p.cols)
+            cpu_ref.forward(x, dense)                                  # warm-up
+            times, t_start = [], time.perf_counter()
+            while len(times) < 3 or (time.perf_counter() - t_start < budget_s / 7 and len(times) < 20):
+                t0 = time.perf_counter()
+                cpu_ref.forward(x, dense)
+                times.append(time.perf_counter() - t0)
+            total += statistics.median(times) * p.rows / rows
     sample = (f"rows 1/16 of each projection (>= 64), {layer.tokens} tokens, bf16 F.linear of the unpacked rows, "
               f"median of >= 3 runs per projection, scaled to all rows")
-    return sum(per.values()), sample
+    return total, sample
 
 
 # ---------------------------------------------------------------------------------------------------------- driver --
@@ -303,7 +314,8 @@ def run_b200(args, rank, world, local):
     peaks = measured_peaks()
     layer = ReplicaLayer(seed=rank, tokens=args.tokens, calib_tokens=args.calib_tokens, device=device)
     stream = torch.cuda.current_stream(device)
-    n_proj = len(layer.tiles)
+    names = list(MODULES)
+    n_proj = len(names)
 
     # warm-up
     for _ in range(args.warmup):
@@ -329,12 +341,11 @@ def run_b200(args, rank, world, local):
     ms_per_step = total_ms / args.steps
     value = args.tokens * world * args.steps / (total_ms / 1e3)
 
-    names = list(layer.tiles)
     launch_ms = {n: statistics.mean(events[s][i][0].elapsed_time(events[s][i][1]) for s in range(args.steps))
                  for i, n in enumerate(names)}
     alg = {n: layer.algorithmic_bytes(n, args.tokens) for n in names}
     achieved = sum(alg.values()) / (sum(launch_ms.values()) / 1e3) / 1e9
-    flops = sum(2 * layer.proj[n].rows * layer.k[n] * args.tokens for n in names)
+    flops = sum(layer.flops(n, args.tokens) for n in names)
     traffic = None
     tpath = os.path.join(ROOT, "profiles", "spmm_traffic.json")
     if os.path.exists(tpath):
@@ -344,7 +355,7 @@ def run_b200(args, rank, world, local):
     # e2e through the public API: pinned host inputs in, outputs back to pinned host memory, every step
     host_x = {g: t.cpu().pin_memory() for g, t in layer.inputs.items()}
     dev_x = {g: torch.empty_like(t) for g, t in layer.inputs.items()}
-    host_y = {n: torch.empty(args.tokens, layer.proj[n].rows, dtype=torch.bfloat16).pin_memory() for n in names}
+    host_y = {n: torch.empty(args.tokens, layer.rows(n), dtype=torch.bfloat16).pin_memory() for n in names}
     h2d = sum(t.numel() * t.element_size() for t in host_x.values())
     d2h = sum(t.numel() * t.element_size() for t in host_y.values())
 
@@ -352,7 +363,7 @@ def run_b200(args, rank, world, local):
         for g in host_x:
             dev_x[g].copy_(host_x[g], non_blocking=True)
         for n in names:
-            y = layer.methods[n].apply(None, dev_x[INPUT_OF[n]])
+            y = layer.methods[n].apply(None, dev_x[MODULES[n][0]])
             host_y[n].copy_(y, non_blocking=True)
 
     for _ in range(max(3, args.warmup)):
@@ -391,7 +402,7 @@ def run_b200(args, rank, world, local):
                "sample": sample}
 
     if rank == 0:
-        weights = sum(layer.proj[n].rows * layer.k[n] * 4 for n in names)
+        weights = sum(layer.proj[n].rows * layer.k[n] * 4 for n in layer.proj)
         out = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
@@ -405,16 +416,16 @@ def run_b200(args, rank, world, local):
                        "parallelism": f"{world} independent replica layers (one per GPU)"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                          "frac": achieved / peaks["hbm_gbs"], "traffic": traffic,
-                         "peak_source": peaks["source"], "kernel": "spmm (7 launches a step)",
+                         "peak_source": peaks["source"], "kernel": "spmm_tc (one launch per module, 4 a step)",
                          "algorithmic_bytes_per_step": sum(alg.values()),
                          "algorithmic_flops_per_step": flops,
                          "achieved_tflops": flops / (sum(launch_ms.values()) / 1e3) / 1e12},
-            "per_projection_us": {n: launch_ms[n] * 1e3 for n in names},
+            "per_module_us": {n: launch_ms[n] * 1e3 for n in names},
             "t17": {"ms_per_pass": ms17, "tokens_per_s": 17 / (ms17 / 1e3), "hbm_gbs": alg17 / (ms17 / 1e3) / 1e9,
                     "frac": alg17 / (ms17 / 1e3) / 1e9 / peaks["hbm_gbs"],
-                    "per_projection_us": {n: t17[n] * 1e3 for n in names}},
+                    "per_module_us": {n: t17[n] * 1e3 for n in names}},
             "setup": {"calib_ms": layer.calib_ms, "select_ms": layer.select_ms,
-                      "calib_gbs": None},
+                      "calib_gbs": layer.calib_bytes / (layer.calib_ms / 1e3) / 1e9},
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
             "gpu_launches": args.steps * n_proj,
             "clocks": clocks.summary(),

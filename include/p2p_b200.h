@@ -104,9 +104,9 @@ int p2p_unpack(const void* vals, int dtype, int64_t rows, int64_t k, int64_t ldv
                int64_t ldwords, const void* idx, int idx_bytes, int64_t ldi, int64_t cols, void* dense, int64_t ldd,
                void* stream);
 
-/* P2P_OK if every column index of idx [rows, k] (row stride ldi) lies in [0, cols), else P2P_EDATA (reads one status
- * word back, so it syncs the stream). The GEMMs clamp indices instead of checking them; the host checks once, at
- * load. Guards what p2p/compact.py:113-166 (Tiles.__init__) assumes of the blocks it is given. */
+/* P2P_OK if every row of idx [rows, k] (row stride ldi) holds strictly ascending columns in [0, cols), else P2P_EDATA
+ * (reads one status word back, so it syncs the stream). The GEMMs clamp indices instead of checking them; the host
+ * checks once, at load. Guards what p2p/compact.py:113-166 (Tiles.__init__) assumes of the blocks it is given. */
 int p2p_check_idx(const void* idx, int idx_bytes, int64_t rows, int64_t k, int64_t ldi, int64_t cols, void* stream);
 
 /* ------------------------------------------------------------------------------------------------------------------
@@ -130,6 +130,36 @@ typedef struct {
  * Replaces p2p/compact.cu:265-278 (spmm) for row-layout weights; p2p/compact.py:192-199 (Tiles.__call__). */
 int p2p_spmm_rows(const void* x, int dtype, int64_t tokens, int64_t cols, int64_t ldx, const p2p_row_block* blocks,
                   int nblocks, int idx_bytes, void* y, int64_t ldy, void* stream);
+
+/* The tensor-core layout of a module (bf16 / f16 weights): rows in tiles of 128, columns in tiles of 64; each
+ * (row tile, column tile) segment holds its kept weights as 32-bit words (value bits << 16 | row << 6 | column, bit 13
+ * marking fillers), padded to a multiple of 4 words; seg [row_tiles * col_tiles + 1] holds where each starts.
+ * Same 4 bytes per kept weight as values + int16 indices. The B200 counterpart of p2p/compact.py:124-166
+ * (Tiles.__init__ re-tiling a module into 8 x 8 pieces), run once at load:
+ *   p2p_tiles_workspace: bytes of scratch both calls need;
+ *   p2p_tiles_plan: fills seg and returns the total words through *total_words (reads it back: syncs the stream);
+ *   p2p_tiles_fill: writes the words [total_words]. Row blocks as for p2p_spmm_rows, column indices ascending. */
+size_t p2p_tiles_workspace(const p2p_row_block* blocks, int nblocks, int64_t cols);
+int p2p_tiles_plan(const p2p_row_block* blocks, int nblocks, int idx_bytes, int64_t cols, int64_t* seg,
+                   int64_t* total_words, void* workspace, size_t workspace_bytes, void* stream);
+int p2p_tiles_fill(const p2p_row_block* blocks, int nblocks, int idx_bytes, int64_t cols, int dtype, const int64_t* seg,
+                   uint32_t* words, int64_t n_words, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Bytes of workspace p2p_spmm_tc needs for this shape (0 if it does not split the columns). */
+size_t p2p_spmm_tc_workspace(int64_t rows, int64_t cols, int64_t tokens);
+
+/* y [tokens, ldy] = x [tokens, cols] (row stride ldx, 16-byte aligned rows) times the module in the tensor-core
+ * layout, on tcgen05 tensor cores (fp32 accumulation in TMEM, x staged by TMA). bf16 or f16; cols a multiple of 8;
+ * seg_cap_words: the largest segment's word count. Any token count (512 a launch). workspace: zeroed once before its
+ * first use (left zeroed again); calls sharing it must not overlap on the GPU.
+ * Replaces p2p/compact.cu:82-278 (spmm_kernel, sum_parts, spmm) and p2p/compact.py:192-199 (Tiles.__call__). */
+int p2p_spmm_tc(const void* x, int dtype, int64_t tokens, int64_t cols, int64_t ldx, const uint32_t* words,
+                const int64_t* seg, int64_t rows, int64_t seg_cap_words, void* y, int64_t ldy, void* workspace,
+                size_t workspace_bytes, void* stream);
+
+/* P2P_OK unless a p2p_spmm_tc launch since the last reset gave up waiting on its pipeline (then P2P_ECUDA, naming
+ * the site); reset != 0 clears the flag. Syncs the stream. */
+int p2p_spmm_tc_status(int reset, void* stream);
 
 /* ------------------------------------------------------------------------------------------------------------------
  * (3) Group combine epilogue

@@ -74,24 +74,25 @@ def _nbytes(blocks) -> int:
 
 class Tiles:
     """A module's row blocks on the GPU, as the compact GEMM reads them; calling it multiplies tokens by them.
-    The B200 counterpart of p2p/compact.py:113-202 (Tiles): no re-tiling into 8 x 8 pieces and no load-time tuning
-    run; rows keep values + column indices, dense blocks keep their weights."""
+    The B200 counterpart of p2p/compact.py:113-202 (Tiles). bf16 / f16 modules whose columns are a multiple of 8 are
+    re-laid once into (128-row x 64-column) segments of packed (value, row, column) words and multiplied on tcgen05
+    tensor cores; fp32 modules (and others) keep rows of values + column indices for the CUDA-core kernel."""
 
     @staticmethod
     def usable(blocks: list) -> bool:
         """CUDA tensors of bf16, f16 or f32, 2-D blocks (p2p/compact.py:117-122 asks for the same, less fp32, plus
-        columns in multiples of 8, which this kernel does not need)."""
+        columns in multiples of 8, which only the tensor-core layout needs)."""
         t = blocks[0][1]
         return t.is_cuda and t.dtype in (torch.bfloat16, torch.float16, torch.float32) and t.dim() == 2
 
-    def __init__(self, blocks: list):
+    def __init__(self, blocks: list, layout: str | None = None):
         if not blocks:
             raise P2PError("a module needs at least one row block")
         blocks = [to_compact(b) for b in blocks]
         self.cols = _cols(blocks[0])
         self.dtype = blocks[0][1].dtype
         self.device = blocks[0][1].device
-        self.blocks, row0 = [], 0
+        rows_blocks, row0 = [], 0
         kinds = set()
         for b in blocks:
             if _cols(b) != self.cols:
@@ -102,20 +103,35 @@ class Tiles:
             idx = b[2].contiguous() if b[0] == "compact" else None
             if idx is not None:
                 kinds.add(idx.dtype)
-            self.blocks.append((row0, values, idx))
+            rows_blocks.append((row0, values, idx))
             row0 += values.shape[0]
         if len(kinds) > 1:                        # one index width for the whole module
             want = idx_dtype(self.cols)
-            self.blocks = [(r, v, None if i is None else i.to(want)) for r, v, i in self.blocks]
+            rows_blocks = [(r, v, None if i is None else i.to(want)) for r, v, i in rows_blocks]
         self.rows = row0
+        tc_ok = self.dtype in (torch.bfloat16, torch.float16) and self.cols % 8 == 0
+        self.layout = layout or ("tc" if tc_ok else "rows")
+        if self.layout == "tc":
+            if not tc_ok:
+                raise P2PError("the tensor-core layout holds bf16 / f16 modules with columns in multiples of 8")
+            self.words, self.seg, self.seg_cap = kernels.tiles_build(rows_blocks, self.cols)
+            self.blocks = None
+        elif self.layout == "rows":
+            self.blocks = rows_blocks
+        else:
+            raise P2PError(f"unknown layout {self.layout!r}")
 
-    def __call__(self, x: torch.Tensor) -> torch.Tensor:
+    def __call__(self, x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
         """x [T, cols] @ W.T: [T, rows]. Any T (the reference launches at most 64 tokens at a time)."""
         if x.dtype != self.dtype:
             raise P2PError(f"x is {x.dtype}, the weights {self.dtype}")
-        return kernels.spmm_rows(x, self.blocks, self.cols, self.rows)
+        if self.layout == "tc":
+            return kernels.spmm_tc(x, self.words, self.seg, self.rows, self.cols, self.seg_cap, out=out)
+        return kernels.spmm_rows(x, self.blocks, self.cols, self.rows, out=out)
 
     def nbytes(self) -> int:
+        if self.layout == "tc":
+            return self.words.numel() * 4 + self.seg.numel() * 8
         return sum(t.numel() * t.element_size() for _, v, i in self.blocks for t in (v, i) if t is not None)
 
 

@@ -297,7 +297,7 @@ __global__ void __launch_bounds__(kSelBlock) unpack_kernel(const T* __restrict__
     }
 }
 
-// ---- column indices in range ---------------------------------------------------------------------------------------
+// ---- column indices in range and strictly ascending in each row ----------------------------------------------------
 
 template <typename I>
 __global__ void check_idx_kernel(const I* __restrict__ idx, int64_t rows, int64_t k, int64_t ldi, int64_t cols) {
@@ -307,6 +307,7 @@ __global__ void check_idx_kernel(const I* __restrict__ idx, int64_t rows, int64_
         const int64_t r = i / k, j = i - r * k;
         const int64_t c = (int64_t)idx[r * ldi + j];
         bad |= (c < 0 || c >= cols);
+        if (j > 0) bad |= (int64_t)idx[r * ldi + j - 1] >= c;
     }
     if (__any_sync(0xffffffffu, bad) && (threadIdx.x & 31) == 0) atomicAdd(&g_bad_rows, 1);
 }
@@ -465,6 +466,6 @@ extern "C" int p2p_check_idx(const void* idx, int idx_bytes, int64_t rows, int64
     if (int e = launch_status("p2p_check_idx")) return e;
     int bad = 0;
     if (int e = read_status(s, &bad)) return e;
-    if (bad) return fail(P2P_EDATA, "p2p_check_idx: column indices outside [0, %lld)", (long long)cols);
+    if (bad) return fail(P2P_EDATA, "p2p_check_idx: column indices outside [0, %lld) or not ascending", (long long)cols);
     return P2P_OK;
 }

@@ -1,0 +1,255 @@
+// Builds the tiled layout of tc_layout.cuh from a module's row blocks (values + ascending column indices, or dense
+// rows). The B200 counterpart of p2p/compact.py:124-166 (Tiles.__init__, which re-tiles a module into 8 x 8 pieces):
+// run once when a replica is loaded.
+//
+//   p2p_tiles_plan: per (row, column tile) counts -> per segment prefix of rows -> padded segment sizes -> seg[]
+//   p2p_tiles_fill: every kept weight to seg[segment] + (rows above it in the segment) + (its rank in its row's part)
+#include "common.cuh"
+#include "tc_layout.cuh"
+
+namespace p2p {
+namespace {
+
+constexpr int kMaxBlocks = 8;
+constexpr int kBuildBlock = 256;
+constexpr int64_t kMaxColTiles = 4096;   // columns up to 262,144
+
+struct Blocks {
+    p2p_row_block b[kMaxBlocks];
+    int n;
+};
+
+struct Shape {
+    int64_t rows, cols, row_tiles, col_tiles, n_seg;
+};
+
+Shape shape_of(const p2p_row_block* blocks, int n, int64_t cols) {
+    Shape s;
+    s.rows = 0;
+    for (int i = 0; i < n; ++i) s.rows = s.rows > blocks[i].row0 + blocks[i].rows ? s.rows : blocks[i].row0 + blocks[i].rows;
+    s.cols = cols;
+    s.row_tiles = (s.rows + tc::kTileRows - 1) / tc::kTileRows;
+    s.col_tiles = (cols + tc::kTileCols - 1) / tc::kTileCols;
+    s.n_seg = s.row_tiles * s.col_tiles;
+    return s;
+}
+
+// The block holding output row `row`, or -1.
+__device__ __forceinline__ int block_of(const Blocks& bl, int64_t row) {
+    for (int i = 0; i < bl.n; ++i)
+        if (row >= bl.b[i].row0 && row < bl.b[i].row0 + bl.b[i].rows) return i;
+    return -1;
+}
+
+template <typename I>
+__device__ __forceinline__ int col_at(const p2p_row_block& b, int64_t lr, int64_t j) {
+    return b.idx ? (int)reinterpret_cast<const I*>(b.idx)[lr * b.ld + j] : (int)j;
+}
+
+// cnt[row, ct] = kept weights of `row` in column tile ct.
+template <typename I>
+__global__ void __launch_bounds__(kBuildBlock) count_kernel(Blocks bl, int64_t rows, int n_ct, int* __restrict__ cnt) {
+    extern __shared__ int hist[];
+    for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
+        for (int c = threadIdx.x; c < n_ct; c += kBuildBlock) hist[c] = 0;
+        __syncthreads();
+        const int bi = block_of(bl, row);
+        if (bi >= 0) {
+            const p2p_row_block& b = bl.b[bi];
+            const int64_t lr = row - b.row0;
+            for (int64_t j = threadIdx.x; j < b.k; j += kBuildBlock) atomicAdd(&hist[col_at<I>(b, lr, j) >> 6], 1);
+        }
+        __syncthreads();
+        for (int c = threadIdx.x; c < n_ct; c += kBuildBlock) cnt[row * n_ct + c] = hist[c];
+        __syncthreads();
+    }
+}
+
+// Within each segment, cnt[row, ct] becomes the words of the rows above `row`; segcnt = the padded segment size.
+__global__ void __launch_bounds__(kBuildBlock) prefix_kernel(int64_t rows, int n_ct, int* __restrict__ cnt,
+                                                              int64_t* __restrict__ segcnt) {
+    const int64_t rt = blockIdx.x;
+    for (int ct = threadIdx.x; ct < n_ct; ct += kBuildBlock) {
+        int64_t run = 0;
+        for (int rl = 0; rl < tc::kTileRows; ++rl) {
+            const int64_t row = rt * tc::kTileRows + rl;
+            if (row >= rows) break;
+            const int c = cnt[row * n_ct + ct];
+            cnt[row * n_ct + ct] = (int)run;
+            run += c;
+        }
+        segcnt[rt * n_ct + ct] = (run + 3) & ~(int64_t)3;
+    }
+}
+
+// seg[i] = sum of segcnt[< i], seg[n] = the total: one block, each thread a contiguous chunk.
+__global__ void __launch_bounds__(1024) scan_kernel(const int64_t* __restrict__ segcnt, int64_t n,
+                                                     int64_t* __restrict__ seg) {
+    __shared__ int64_t part[1024];
+    const int t = threadIdx.x;
+    const int64_t chunk = (n + 1023) / 1024;
+    const int64_t a = min(n, t * chunk), b = min(n, a + chunk);
+    int64_t s = 0;
+    for (int64_t i = a; i < b; ++i) s += segcnt[i];
+    part[t] = s;
+    __syncthreads();
+    if (t == 0) {
+        int64_t run = 0;
+        for (int i = 0; i < 1024; ++i) {
+            const int64_t v = part[i];
+            part[i] = run;
+            run += v;
+        }
+        seg[n] = run;
+    }
+    __syncthreads();
+    int64_t run = part[t];
+    for (int64_t i = a; i < b; ++i) {
+        seg[i] = run;
+        run += segcnt[i];
+    }
+}
+
+__global__ void fill_pad_kernel(uint32_t* __restrict__ words, int64_t n) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+        words[i] = tc::kPadWord;
+}
+
+__device__ int g_fill_errors;
+
+template <typename I>
+__global__ void __launch_bounds__(kBuildBlock) fill_kernel(Blocks bl, int64_t rows, int n_ct, const int* __restrict__ cnt,
+                                                            const int64_t* __restrict__ seg, uint32_t* __restrict__ words,
+                                                            int64_t n_words) {
+    extern __shared__ int sm[];
+    int* hist = sm;            // [n_ct]: this row's count per column tile
+    int* first = sm + n_ct;    // [n_ct]: this row's first entry in each column tile
+    for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
+        const int bi = block_of(bl, row);
+        if (bi < 0) continue;                                   // uniform over the block
+        const p2p_row_block& b = bl.b[bi];
+        const int64_t lr = row - b.row0;
+        for (int c = threadIdx.x; c < n_ct; c += kBuildBlock) hist[c] = 0;
+        __syncthreads();
+        for (int64_t j = threadIdx.x; j < b.k; j += kBuildBlock) atomicAdd(&hist[col_at<I>(b, lr, j) >> 6], 1);
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            int run = 0;
+            for (int c = 0; c < n_ct; ++c) {
+                first[c] = run;
+                run += hist[c];
+            }
+        }
+        __syncthreads();
+        const int64_t rt = row / tc::kTileRows;
+        const int rl = (int)(row % tc::kTileRows);
+        const uint16_t* vals = reinterpret_cast<const uint16_t*>(b.vals);
+        for (int64_t j = threadIdx.x; j < b.k; j += kBuildBlock) {
+            const int col = col_at<I>(b, lr, j);
+            const int ct = col >> 6;
+            const int64_t rank = j - first[ct];
+            const int64_t pos = seg[rt * n_ct + ct] + cnt[row * n_ct + ct] + rank;
+            if (rank < 0 || rank >= hist[ct] || pos >= n_words) {   // indices not ascending: refuse, never write
+                atomicAdd(&g_fill_errors, 1);
+                continue;
+            }
+            words[pos] = tc::pack_word(vals[lr * b.ld + j], rl, col & 63);
+        }
+        __syncthreads();
+    }
+}
+
+int check_blocks(const p2p_row_block* blocks, int nblocks, int idx_bytes, int64_t cols, Blocks& bl, const char* who) {
+    if (!blocks || nblocks < 1 || nblocks > kMaxBlocks) return fail(P2P_EINVAL, "%s: 1 to %d row blocks", who, kMaxBlocks);
+    if (idx_bytes != 2 && idx_bytes != 4) return fail(P2P_EINVAL, "%s: idx_bytes %d", who, idx_bytes);
+    if (cols < 1 || (cols + 63) / 64 > kMaxColTiles) return fail(P2P_EUNSUPPORTED, "%s: %lld columns", who, (long long)cols);
+    bl.n = nblocks;
+    for (int i = 0; i < nblocks; ++i) {
+        const p2p_row_block& b = blocks[i];
+        if (b.rows < 0 || b.row0 < 0 || b.k < 0 || (b.rows > 0 && !b.vals) || (b.rows > 0 && b.k > 0 && b.ld < b.k))
+            return fail(P2P_EINVAL, "%s: block %d", who, i);
+        if (!b.idx && b.k != cols) return fail(P2P_EINVAL, "%s: dense block %d needs k == cols", who, i);
+        bl.b[i] = b;
+    }
+    return P2P_OK;
+}
+
+}  // namespace
+}  // namespace p2p
+
+using namespace p2p;
+
+extern "C" size_t p2p_tiles_workspace(const p2p_row_block* blocks, int nblocks, int64_t cols) {
+    if (!blocks || nblocks < 1 || cols < 1) return 0;
+    const Shape s = shape_of(blocks, nblocks, cols);
+    const size_t cnt_bytes = (size_t)s.row_tiles * tc::kTileRows * s.col_tiles * sizeof(int);
+    return (cnt_bytes + 255) / 256 * 256 + (size_t)s.n_seg * sizeof(int64_t);
+}
+
+extern "C" int p2p_tiles_plan(const p2p_row_block* blocks, int nblocks, int idx_bytes, int64_t cols, int64_t* seg,
+                              int64_t* total_words, void* workspace, size_t workspace_bytes, void* stream) {
+    Blocks bl;
+    if (int e = check_blocks(blocks, nblocks, idx_bytes, cols, bl, "p2p_tiles_plan")) return e;
+    P2P_REQUIRE(seg && total_words && workspace, "p2p_tiles_plan: null seg, total or workspace");
+    const Shape s = shape_of(blocks, nblocks, cols);
+    P2P_REQUIRE(workspace_bytes >= p2p_tiles_workspace(blocks, nblocks, cols), "p2p_tiles_plan: workspace too small");
+    cudaStream_t st = as_stream(stream);
+    int* cnt = reinterpret_cast<int*>(workspace);
+    const size_t cnt_bytes = (size_t)s.row_tiles * tc::kTileRows * s.col_tiles * sizeof(int);
+    int64_t* segcnt = reinterpret_cast<int64_t*>(reinterpret_cast<char*>(workspace) + (cnt_bytes + 255) / 256 * 256);
+    if (cudaMemsetAsync(cnt, 0, cnt_bytes, st) != cudaSuccess) return launch_status("p2p_tiles_plan memset");
+    const int smem = (int)(s.col_tiles * sizeof(int));
+    const int grid = (int)(s.rows < sm_count() * 8 ? s.rows : sm_count() * 8);
+    if (s.rows > 0) {
+        if (idx_bytes == 2) {
+            if (int e = allow_smem((const void*)count_kernel<int16_t>, smem, "p2p_tiles_plan")) return e;
+            count_kernel<int16_t><<<grid, kBuildBlock, smem, st>>>(bl, s.rows, (int)s.col_tiles, cnt);
+        } else {
+            if (int e = allow_smem((const void*)count_kernel<int32_t>, smem, "p2p_tiles_plan")) return e;
+            count_kernel<int32_t><<<grid, kBuildBlock, smem, st>>>(bl, s.rows, (int)s.col_tiles, cnt);
+        }
+        prefix_kernel<<<(unsigned)s.row_tiles, kBuildBlock, 0, st>>>(s.rows, (int)s.col_tiles, cnt, segcnt);
+    }
+    scan_kernel<<<1, 1024, 0, st>>>(segcnt, s.n_seg, seg);
+    if (int e = launch_status("p2p_tiles_plan")) return e;
+    if (cudaMemcpyAsync(total_words, seg + s.n_seg, sizeof(int64_t), cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+        cudaStreamSynchronize(st) != cudaSuccess)
+        return launch_status("p2p_tiles_plan read-back");
+    return P2P_OK;
+}
+
+extern "C" int p2p_tiles_fill(const p2p_row_block* blocks, int nblocks, int idx_bytes, int64_t cols, int dtype,
+                              const int64_t* seg, uint32_t* words, int64_t n_words, void* workspace,
+                              size_t workspace_bytes, void* stream) {
+    Blocks bl;
+    if (int e = check_blocks(blocks, nblocks, idx_bytes, cols, bl, "p2p_tiles_fill")) return e;
+    if (dtype != P2P_BF16 && dtype != P2P_F16)
+        return fail(P2P_EUNSUPPORTED, "p2p_tiles_fill: the tensor-core layout holds bf16 or f16 values");
+    P2P_REQUIRE(seg && words && workspace, "p2p_tiles_fill: null pointer");
+    P2P_REQUIRE(workspace_bytes >= p2p_tiles_workspace(blocks, nblocks, cols), "p2p_tiles_fill: workspace too small");
+    const Shape s = shape_of(blocks, nblocks, cols);
+    cudaStream_t st = as_stream(stream);
+    const int* cnt = reinterpret_cast<const int*>(workspace);
+    const int zero = 0;
+    if (cudaMemcpyToSymbolAsync(g_fill_errors, &zero, sizeof(int), 0, cudaMemcpyHostToDevice, st) != cudaSuccess)
+        return launch_status("p2p_tiles_fill reset");
+    if (n_words > 0) fill_pad_kernel<<<sm_count() * 4, 256, 0, st>>>(words, n_words);
+    const int smem = (int)(2 * s.col_tiles * sizeof(int));
+    const int grid = (int)(s.rows < sm_count() * 8 ? s.rows : sm_count() * 8);
+    if (s.rows > 0) {
+        if (idx_bytes == 2) {
+            if (int e = allow_smem((const void*)fill_kernel<int16_t>, smem, "p2p_tiles_fill")) return e;
+            fill_kernel<int16_t><<<grid, kBuildBlock, smem, st>>>(bl, s.rows, (int)s.col_tiles, cnt, seg, words, n_words);
+        } else {
+            if (int e = allow_smem((const void*)fill_kernel<int32_t>, smem, "p2p_tiles_fill")) return e;
+            fill_kernel<int32_t><<<grid, kBuildBlock, smem, st>>>(bl, s.rows, (int)s.col_tiles, cnt, seg, words, n_words);
+        }
+    }
+    if (int e = launch_status("p2p_tiles_fill")) return e;
+    int bad = 0;
+    if (cudaMemcpyFromSymbolAsync(&bad, g_fill_errors, sizeof(int), 0, cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+        cudaStreamSynchronize(st) != cudaSuccess)
+        return launch_status("p2p_tiles_fill read-back");
+    if (bad) return fail(P2P_EDATA, "p2p_tiles_fill: %d column indices out of ascending order", bad);
+    return P2P_OK;
+}

@@ -12,9 +12,9 @@ from ._lib import P2PError, call, dtype_code, ptr, require_cuda, stream_of
 _workspaces: dict = {}
 
 
-def _workspace(device: torch.device, nbytes: int) -> torch.Tensor:
-    """A zeroed per-device scratch buffer of at least nbytes (the kernels leave it zeroed again)."""
-    key = (device.type, device.index)
+def _workspace(device: torch.device, nbytes: int, purpose: str = "sumsq") -> torch.Tensor:
+    """A zeroed scratch buffer of at least nbytes per device and purpose (the kernels leave it zeroed again)."""
+    key = (device.type, device.index, purpose)
     ws = _workspaces.get(key)
     if ws is None or ws.numel() < nbytes:
         ws = torch.zeros(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
@@ -191,6 +191,65 @@ def spmm_rows(x: torch.Tensor, blocks: list, cols: int, out_rows: int, out: torc
     call("p2p_spmm_rows", ptr(x), dtype_code(x), x.shape[0], cols, x.stride(0), table, len(blocks), idx_bytes,
          ptr(out), out.stride(0), stream_of(x))
     return out
+
+
+def _row_table(blocks: list):
+    table = (_lib.RowBlock * len(blocks))()
+    idx_bytes = 2
+    for i, (row0, v, ix) in enumerate(blocks):
+        if ix is not None:
+            idx_bytes = _lib.IDX_BYTES[ix.dtype]
+        table[i] = _lib.RowBlock(v.data_ptr(), None if ix is None else ix.data_ptr(), row0, v.shape[0], v.shape[1],
+                                 v.stride(0))
+    return table, idx_bytes
+
+
+def tiles_build(blocks: list, cols: int) -> tuple:
+    """The tensor-core layout (words uint32, seg int64, largest segment in words) of a module's row blocks
+    [(row0, values, idx | None)], bf16 or f16 values, ascending column indices. Load time; syncs."""
+    dev = blocks[0][1].device
+    table, idx_bytes = _row_table(blocks)
+    lib = _lib.load()
+    need = lib.p2p_tiles_workspace(table, len(blocks), cols)
+    ws = torch.empty(max(need, 1), dtype=torch.uint8, device=dev)
+    rows = max(r0 + v.shape[0] for r0, v, _ in blocks)
+    n_seg = -(-rows // 128) * -(-cols // 64)
+    seg = torch.empty(n_seg + 1, dtype=torch.int64, device=dev)
+    total = ctypes.c_int64(0)
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    call("p2p_tiles_plan", table, len(blocks), idx_bytes, cols, ptr(seg), ctypes.byref(total), ptr(ws), ws.numel(),
+         stream)
+    words = torch.empty(max(total.value, 4), dtype=torch.int32, device=dev)
+    call("p2p_tiles_fill", table, len(blocks), idx_bytes, cols, dtype_code(blocks[0][1]), ptr(seg), ptr(words),
+         total.value, ptr(ws), ws.numel(), stream)
+    seg_cap = int((seg[1:] - seg[:-1]).max().item()) if n_seg else 0
+    return words, seg, seg_cap
+
+
+def spmm_tc(x: torch.Tensor, words: torch.Tensor, seg: torch.Tensor, rows: int, cols: int, seg_cap: int,
+            out: torch.Tensor | None = None) -> torch.Tensor:
+    """y [tokens, rows] = x [tokens, cols] times a module in the tensor-core layout (tcgen05, bf16/f16)."""
+    require_cuda(x)
+    if x.dim() != 2 or x.shape[1] != cols:
+        raise P2PError(f"x of {tuple(x.shape)} does not have {cols} columns")
+    if x.stride(1) != 1 or x.stride(0) % 8 or x.data_ptr() % 16:
+        x = x.contiguous()
+        if x.data_ptr() % 16:
+            x = x.clone()
+    if out is None:
+        out = torch.empty(x.shape[0], rows, dtype=x.dtype, device=x.device)
+    lib = _lib.load()
+    need = lib.p2p_spmm_tc_workspace(rows, cols, x.shape[0])
+    ws = _workspace(x.device, need, "spmm_tc") if need else None
+    call("p2p_spmm_tc", ptr(x), dtype_code(x), x.shape[0], cols, x.stride(0), ptr(words), ptr(seg), rows, seg_cap,
+         ptr(out), out.stride(0), ptr(ws), 0 if ws is None else ws.numel(), stream_of(x))
+    return out
+
+
+def spmm_tc_status(device=None, reset: bool = True) -> None:
+    """Raises if a tensor-core GEMM launch gave up waiting on its pipeline since the last reset. Syncs."""
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    call("p2p_spmm_tc_status", int(reset), torch.cuda.current_stream(dev).cuda_stream)
 
 
 def _ptr_array(ts) -> ctypes.Array:

@@ -70,16 +70,20 @@ def _compact_forward(method, bias, x):
     return method.apply(None, x, bias)
 
 
+def _run(module: nn.Module, x: torch.Tensor) -> torch.Tensor:
+    """A layer's own forward, past any forward installed on the instance."""
+    return type(module).forward(module, x)
+
+
 def _member(group: list, replica: nn.Module, k: int, h: torch.Tensor, mode: str = "decode"):
     """Member k of a group on one pass (p2p/replica.py:69-85): on decode / verify passes member 0 runs the whole group
     and combines, the others pass h on; prefill runs each layer alone."""
-    layer = group[k]
     if mode not in ("decode", "verify"):
-        return layer(h)
+        return _run(group[k], h)
     if k:
         return h
-    h_copy = replica(h)
-    outs = [group[0](h)] + [m(h) for m in group[1:-1]] + [group[-1](h_copy)]
+    h_copy = _run(replica, h)
+    outs = [_run(group[0], h)] + [_run(m, h) for m in group[1:-1]] + [_run(group[-1], h_copy)]
     return combine(outs, h, h_copy)
 
 

@@ -54,14 +54,17 @@ def test_compact_method_puts_blocks_in_row_order():
     assert got.shape == (2, 5, 80) and (got - want).abs().max() <= 1e-2 * want.abs().max()
 
 
+@pytest.mark.parametrize("layout", [None, "rows"])
 @pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16, torch.float32])
 @pytest.mark.parametrize("t", [1, 3, 17, 32, 64, 100, 272])
 @pytest.mark.parametrize("rows,cols,keep", [(512, 5120, 40), (300, 1000, 7), (96, 80, 90), (1024, 2048, 25), (17, 8, 50)])
-def test_tiles_match_a_dense_matmul(dtype, t, rows, cols, keep):
+def test_tiles_match_a_dense_matmul(layout, dtype, t, rows, cols, keep):
     """tests/test_compact.py:44-56 (its tolerance max|d| <= 1e-2 max|want|), plus rel-L2 <= 1e-2 for bf16/f16 and
-    <= 1e-5 for fp32, any shape and any token count."""
+    <= 1e-5 for fp32, any shape and any token count, in either layout (bf16/f16 default to the tensor-core one)."""
+    if layout is not None and dtype == torch.float32:
+        pytest.skip("fp32 has the row layout only")
     (w, mask), _, _ = _pruned(rows, cols, keep, dtype)
-    tiles = compact.Tiles([("sparse", *compact.pack(w, mask), cols)])
+    tiles = compact.Tiles([("sparse", *compact.pack(w, mask), cols)], layout=layout)
     x = torch.randn(t, cols, device="cuda").to(dtype)
     want = x.double() @ w.double().T
     got = tiles(x)

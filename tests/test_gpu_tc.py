@@ -1,0 +1,133 @@
+"""The tensor-core layout and the tcgen05 compact GEMM on the GPU: the layout decodes back to the oracle's selection
+bit for bit, and the GEMM matches the oracle's dense masked matmul (rel-L2 <= 1e-2 for bf16/f16, the reference's
+max|d| <= 1e-2 max|want| too) over token counts 1..600, odd shapes, mixed dense/compact blocks and split columns."""
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from p2pllm_b200 import compact, kernels, wanda
+
+pytestmark = pytest.mark.gpu
+
+
+def _bits(t):
+    return t.cpu().view(torch.int16).numpy().view(np.uint16)
+
+
+def _module(rows, cols, keep, dtype=torch.bfloat16, seed=0):
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    w = (torch.randn(rows, cols, generator=g, device="cuda") * 0.02).to(dtype)
+    norms = torch.rand(cols, generator=g, device="cuda") + 0.1
+    values, idx = wanda.select(w, keep, norms)
+    return values, idx
+
+
+def _check(got, want, dtype):
+    got = got.double().cpu().numpy() if torch.is_tensor(got) else got
+    rel = np.linalg.norm(got - want) / max(np.linalg.norm(want), 1e-30)
+    assert rel <= 1e-2, rel
+    assert np.abs(got - want).max() <= 1e-2 * np.abs(want).max()
+
+
+@pytest.mark.parametrize("rows,cols,keep", [(128, 64, 36), (300, 1000, 7), (1024, 4096, 33), (17, 8, 50),
+                                            (200, 5120, 90)])
+def test_layout_decodes_to_the_selection(rows, cols, keep):
+    values, idx = _module(rows, cols, keep)
+    words, seg, cap = kernels.tiles_build([(0, values, idx)], cols)
+    w = words.cpu().numpy().view(np.uint32)
+    s = seg.cpu().numpy()
+    n_ct = -(-cols // 64)
+    got = np.zeros((rows, cols), np.uint16)
+    seen = np.zeros((rows, cols), np.int32)
+    for i in range(len(s) - 1):
+        assert s[i] % 4 == 0 and s[i + 1] >= s[i]
+        rt, ct = divmod(i, n_ct)
+        for word in w[s[i]:s[i + 1]]:
+            if word & (1 << 13):
+                continue
+            r, c = rt * 128 + ((word >> 6) & 127), ct * 64 + (word & 63)
+            got[r, c] = word >> 16
+            seen[r, c] += 1
+    assert cap == int(np.diff(s).max())
+    want = np.zeros((rows, cols), np.uint16)
+    np.put_along_axis(want, idx.cpu().numpy().astype(np.int64), _bits(values), axis=1)
+    mask = np.zeros((rows, cols), bool)
+    np.put_along_axis(mask, idx.cpu().numpy().astype(np.int64), True, axis=1)
+    assert np.array_equal(seen, mask.astype(np.int32))
+    assert np.array_equal(got, want)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("t", [1, 3, 16, 17, 31, 64, 100, 255, 256, 257, 272, 512, 513, 600])
+@pytest.mark.parametrize("rows,cols,keep", [(512, 5120, 40), (300, 1000, 7), (1024, 2048, 25), (17, 8, 50)])
+def test_tc_matches_the_dense_matmul(dtype, t, rows, cols, keep):
+    values, idx = _module(rows, cols, keep, dtype, seed=t)
+    tiles = compact.Tiles([("compact", values, idx, cols)])
+    assert tiles.layout == "tc"
+    x = torch.randn(t, cols, device="cuda").to(dtype)
+    y = tiles(x)
+    kernels.spmm_tc_status()
+    assert y.shape == (t, rows) and y.dtype == dtype
+    dt = "bf16" if dtype == torch.bfloat16 else "f16"
+    want = oracle.forward(_bits(x), _bits(values), idx.cpu().numpy(), cols, dt)
+    _check(y, want, dtype)
+
+
+def test_tc_and_rows_layouts_agree_and_repeat_bit_for_bit():
+    values, idx = _module(4096, 4096, 33, seed=11)
+    tc = compact.Tiles([("compact", values, idx, 4096)])
+    rows = compact.Tiles([("compact", values, idx, 4096)], layout="rows")
+    for t in (17, 272):
+        x = torch.randn(t, 4096, device="cuda").bfloat16()
+        a, b = tc(x), tc(x)
+        kernels.spmm_tc_status()
+        assert torch.equal(a, b)                                   # split partials are added in a fixed order
+        r = rows(x)
+        assert ((a.float() - r.float()).norm() / r.float().norm()).item() <= 1e-2
+
+
+def test_tc_mixed_dense_and_compact_blocks_in_row_order():
+    """A fused qkv-like module: compact, dense and compact blocks of different k (tests/test_compact.py:27-36)."""
+    cols = 1024
+    g = torch.Generator(device="cuda").manual_seed(3)
+    norms = torch.rand(cols, generator=g, device="cuda") + 0.1
+    ws = [torch.randn(r, cols, generator=g, device="cuda").bfloat16() for r in (200, 72, 130)]
+    blocks = [("compact", *wanda.select(ws[0], 33, norms), cols), ("dense", ws[1]),
+              ("compact", *wanda.select(ws[2], 60, norms), cols)]
+    tiles = compact.Tiles(blocks)
+    assert tiles.layout == "tc" and tiles.rows == 402
+    x = torch.randn(40, cols, device="cuda").bfloat16()
+    dense = torch.cat([compact.expand(b) for b in blocks])
+    want = x.double().cpu().numpy() @ dense.double().cpu().numpy().T
+    _check(tiles(x), want, torch.bfloat16)
+    kernels.spmm_tc_status()
+
+
+def test_tc_reference_blocks_and_strided_x():
+    """The reference's ("sparse", values, words, cols) blocks load into the tensor-core layout; x may be a strided view."""
+    (w, mask) = wanda.prune(torch.randn(256, 2048, device="cuda").bfloat16(), 36,
+                            torch.rand(2048, device="cuda") + 0.1, with_mask=True)
+    values, words = compact.pack(w, mask)
+    tiles = compact.Tiles([("sparse", values, words, 2048)])
+    base = torch.randn(17, 4096, device="cuda").bfloat16()
+    x = base[:, 1024:3072]                                         # row stride 4096
+    want = x.double().cpu().numpy() @ w.double().cpu().numpy().T
+    _check(tiles(x), want, torch.bfloat16)
+    kernels.spmm_tc_status()
+
+
+def test_llama_shapes_at_17_and_272_tokens():
+    """The configuration the bench runs: each Llama-3-8B projection shape at keep 33/36, against the oracle on a
+    sample of rows (every token)."""
+    from p2pllm_b200 import workloads
+    for p in workloads.LLAMA3_8B:
+        values, idx = _module(p.rows, p.cols, p.keep, seed=p.rows + p.cols)
+        tiles = compact.Tiles([("compact", values, idx, p.cols)])
+        for t in (17, 272):
+            x = torch.randn(t, p.cols, device="cuda").bfloat16()
+            y = tiles(x)
+            kernels.spmm_tc_status()
+            sample = torch.arange(0, p.rows, 97, device="cuda")
+            want = oracle.forward(_bits(x), _bits(values[sample]), idx[sample].cpu().numpy(), p.cols, "bf16")
+            _check(y[:, sample], want, torch.bfloat16)
