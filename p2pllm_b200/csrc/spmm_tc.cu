@@ -5,13 +5,15 @@
 // mma.sync fragments and re-reads every weight once per 64 tokens. Here a CTA owns one 128-row tile and a range of
 // 64-column tiles (split-K), and every token of the pass at once (up to 512 in TMEM):
 //
-//   warp 8  (producer)  per column tile: TMA of the x tile [tokens x 64] (128-byte swizzle) into ring 1, and a bulk
+//   warp 16 (producer)  per column tile: TMA of the x tile [tokens x 64] (128-byte swizzle) into ring 1, and a bulk
 //                       copy of the segment's packed words from HBM into ring 1 beside it; one mbarrier, tx-counted.
-//   warps 0-7 (expand)  zero a 128 x 64 bf16 tile in ring 2 and scatter the segment's words into it at their swizzled
-//                       (row, column) places: the dense A operand, built in shared memory, never in HBM.
-//   warp 9  (MMA)       one elected thread issues tcgen05.mma (M = 128, N = tokens rounded to 16, K = 16 a step)
+//   warps 0-15 (expand) two groups of 8 warps take alternate column tiles; in a group each warp owns 16 rows of the
+//                       128 x 64 bf16 tile in ring 2: it zeroes them and writes its rows' values at the swizzled byte
+//                       offsets the words carry (lanes take consecutive words, so a store touches one or two rows and
+//                       few banks clash). No block-wide barrier: a warp's rows are its own.
+//   warp 17 (MMA)       one elected thread issues tcgen05.mma (M = 128, N = tokens rounded to 16, K = 16 a step)
 //                       with the accumulator D[128 x N] fp32 in TMEM; tcgen05.commit frees both rings' slots.
-//   warps 0-7 (epilogue) tcgen05.ld D out of TMEM, round, and write y[t, row] (coalesced along rows), or write fp32
+//   warps 0-15 (epilogue) tcgen05.ld D out of TMEM, round, and write y[t, row] (coalesced along rows), or write fp32
 //                       partials when the columns are split; the last CTA of a row tile adds the partials in split
 //                       order (a ticket per row tile), so results do not depend on scheduling.
 //
@@ -27,15 +29,18 @@
 namespace p2p {
 namespace {
 
-constexpr int kExpWarps = 8;
-constexpr int kExpThreads = kExpWarps * 32;
+constexpr int kGroupWarps = 8;                                     // warps expanding one tile (16 rows each)
+constexpr int kGroups = 2;                                         // groups taking alternate column tiles
+constexpr int kExpWarps = kGroupWarps * kGroups;
 constexpr int kProducerWarp = kExpWarps;
 constexpr int kMmaWarp = kExpWarps + 1;
-constexpr int kTcThreads = kExpThreads + 64;
+constexpr int kTcThreads = kExpWarps * 32 + 64;
 constexpr int kATileBytes = tc::kTileRows * tc::kTileCols * 2;   // 16 KiB
-constexpr int kS2 = 2;                                             // A tiles in flight
+constexpr int kMaxS2 = 4;                                          // A tiles in flight (2 or 4)
 constexpr int kMaxS1 = 8;
-constexpr int kSmemLimit = 227 * 1024 - 1024;          // dynamic shared memory, leaving room for the static
+constexpr int kMaxTilesPerCta = 1024;                              // segment offsets staged in shared memory
+// Dynamic shared memory: the 227 KiB a block may hold, less the static offsets array and a few scalars.
+constexpr int kSmemLimit = 227 * 1024 - (int)sizeof(int64_t) * (kMaxTilesPerCta + 1) - 256;
 constexpr uint64_t kWaitNs = 2000000000ull;
 
 __device__ int g_tc_error;            // first failed wait of the last launches (0: none); read back by the host
@@ -44,7 +49,7 @@ struct TcParams {
     const uint32_t* words;            // the module's packed words
     const int64_t* seg;               // [row_tiles * col_tiles + 1]
     int rows, col_tiles, tokens, n_total, box_rows, n_boxes, tmem_cols;
-    int s1, b_bytes, seg_cap, kt_per_split, n_split;
+    int s1, s2, g, b_bytes, seg_cap, kt_per_split, n_split;   // g: column tiles a stage; seg_cap: a stage's words
     void* y;
     int64_t ldy;
     float* partial;                   // [n_split, tokens, rows_pad] when n_split > 1
@@ -66,28 +71,45 @@ __device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
     asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
 }
 
+// One test of the phase; a thread whose phase is not complete sleeps in hardware (up to the suspend-time hint, in ns)
+// until it completes, instead of spinning on the issue slots its warp scheduler shares with working warps.
 __device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
     uint32_t ok;
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
         "selp.u32 %0, 1, 0, p;\n\t}"
         : "=r"(ok)
-        : "r"(bar), "r"(parity)
+        : "r"(bar), "r"(parity), "r"(1000000u)
         : "memory");
     return ok != 0;
 }
 
-// Waits for the phase of parity `parity`; after kWaitNs (or at once, once another wait has failed) records `where`.
+// Waits for the phase of parity `parity`; past kWaitNs (or at once, once another wait has given up) it records
+// `where` in g_tc_error and returns, so a broken pipeline ends the kernel instead of hanging it.
 __device__ __forceinline__ void mbar_wait(uint32_t bar, uint32_t parity, int where) {
     if (mbar_try(bar, parity)) return;
     const uint64_t t0 = now_ns();
     while (!mbar_try(bar, parity)) {
-        if (*(volatile int*)&g_tc_error != 0 || now_ns() - t0 > kWaitNs) {
+        if (now_ns() - t0 > (*(volatile int*)&g_tc_error ? 0ull : kWaitNs)) {
             atomicCAS(&g_tc_error, 0, where);
             return;
         }
     }
+}
+
+// Ring position of the next item: `step` slots on (step <= n), the phase bit flipping at each wrap. Kept in
+// registers, so the single-thread roles do no divisions by the runtime ring sizes.
+__device__ __forceinline__ void advance(int& slot, uint32_t& phase, int step, int n) {
+    slot += step;
+    if (slot >= n) {
+        slot -= n;
+        phase ^= 1u;
+    }
+}
+
+__device__ __forceinline__ void sts_u16(uint32_t addr, uint32_t v) {
+    asm volatile("st.shared.u16 [%0], %1;" ::"r"(addr), "h"((unsigned short)v) : "memory");
 }
 
 __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
@@ -158,26 +180,30 @@ __global__ void __launch_bounds__(kTcThreads, 1) spmm_tc_kernel(const __grid_con
     extern __shared__ uint8_t smem_raw[];
     __shared__ uint32_t s_tmem;
     __shared__ int s_last;
+    __shared__ int64_t s_offs[kMaxTilesPerCta + 1];                // this CTA's segment offsets
     const uint32_t raw = smem_u32(smem_raw);
     const uint32_t base = (raw + 1023u) & ~1023u;
     uint8_t* gbase = smem_raw + (base - raw);
-    const int S1 = p.s1;
+    const int S1 = p.s1, kS2 = p.s2, G = p.g;
+    const uint32_t a_stage = (uint32_t)G * kATileBytes, b_stage = (uint32_t)G * p.b_bytes;
     const uint32_t a_ring = base;
-    const uint32_t b_ring = a_ring + kS2 * kATileBytes;
-    const uint32_t seg_ring = b_ring + S1 * p.b_bytes;
+    const uint32_t b_ring = a_ring + kS2 * a_stage;
+    const uint32_t seg_ring = b_ring + S1 * b_stage;
     const uint32_t bars = seg_ring + S1 * p.seg_cap;
     auto full1 = [&](int s) { return bars + 8u * s; };
     auto empty1 = [&](int s) { return bars + 8u * (kMaxS1 + s); };
     auto full2 = [&](int s) { return bars + 8u * (2 * kMaxS1 + s); };
-    auto empty2 = [&](int s) { return bars + 8u * (2 * kMaxS1 + kS2 + s); };
-    const uint32_t done = bars + 8u * (2 * kMaxS1 + 2 * kS2);
+    auto empty2 = [&](int s) { return bars + 8u * (2 * kMaxS1 + kMaxS2 + s); };
+    const uint32_t done = bars + 8u * (2 * kMaxS1 + 2 * kMaxS2);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int rt = blockIdx.x, split = blockIdx.y;
     const int kt0 = split * p.kt_per_split;
     const int kt1 = min(p.col_tiles, kt0 + p.kt_per_split);
-    const int nk = kt1 - kt0;
+    const int nk = kt1 - kt0;                                      // column tiles of this CTA
+    const int ns = (nk + G - 1) / G;                               // pipeline stages, G column tiles each
     const int64_t seg0 = (int64_t)rt * p.col_tiles + kt0;
+    for (int j = threadIdx.x; j <= nk; j += blockDim.x) s_offs[j] = p.seg[seg0 + j];
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < S1; ++s) {
@@ -185,7 +211,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) spmm_tc_kernel(const __grid_con
             mbar_init(empty1(s), 1);
         }
         for (int s = 0; s < kS2; ++s) {
-            mbar_init(full2(s), kExpWarps);
+            mbar_init(full2(s), kGroupWarps);
             mbar_init(empty2(s), 1);
         }
         mbar_init(done, 1);
@@ -204,17 +230,26 @@ __global__ void __launch_bounds__(kTcThreads, 1) spmm_tc_kernel(const __grid_con
     const uint32_t tmem = s_tmem;
 
     if (warp == kProducerWarp) {
-        if (lane == 0) {
-            asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmap_x)) : "memory");
-            for (int i = 0; i < nk; ++i) {
-                const int s = i % S1;
-                if (i >= S1) mbar_wait(empty1(s), ((i / S1) - 1) & 1, 1);
-                const int64_t w0 = p.seg[seg0 + i], w1 = p.seg[seg0 + i + 1];
+        // One producer lane per ring-1 slot: lane s fills slot s for stages s, s + S1, ..., so the slots' waits and
+        // copy issues run side by side. A stage is G column tiles: G x tiles by TMA and one bulk copy of their G
+        // segments, which lie back to back in HBM.
+        if (lane == 0) asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmap_x)) : "memory");
+        if (lane < S1) {
+            const int s = lane;
+            uint32_t ph = 0;
+            for (int j = lane; j < ns; j += S1) {
+                if (j >= S1) {
+                    mbar_wait(empty1(s), ph, 1);
+                    ph ^= 1u;
+                }
+                const int c0 = j * G, cn = min(G, nk - c0);
+                const int64_t w0 = s_offs[c0], w1 = s_offs[c0 + cn];
                 const uint32_t seg_bytes = (uint32_t)((w1 - w0) * 4);
-                mbar_expect_tx(full1(s), (uint32_t)p.b_bytes + seg_bytes);
-                for (int b = 0; b < p.n_boxes; ++b)
-                    tma_load_2d(b_ring + s * p.b_bytes + b * p.box_rows * 128, &tmap_x, (kt0 + i) * tc::kTileCols,
-                                b * p.box_rows, full1(s));
+                mbar_expect_tx(full1(s), (uint32_t)(cn * p.b_bytes) + seg_bytes);
+                for (int h = 0; h < cn; ++h)
+                    for (int b = 0; b < p.n_boxes; ++b)
+                        tma_load_2d(b_ring + s * b_stage + h * p.b_bytes + b * p.box_rows * 128, &tmap_x,
+                                    (kt0 + c0 + h) * tc::kTileCols, b * p.box_rows, full1(s));
                 if (seg_bytes) bulk_load(seg_ring + s * p.seg_cap, p.words + w0, seg_bytes, full1(s));
             }
         }
@@ -223,50 +258,72 @@ __global__ void __launch_bounds__(kTcThreads, 1) spmm_tc_kernel(const __grid_con
         if (lane == 0) {
             const uint32_t id0 = idesc_f16<T>(p.n_total <= 256 ? p.n_total : 256);
             const uint32_t id1 = idesc_f16<T>(p.n_total > 256 ? p.n_total - 256 : 16);
-            for (int i = 0; i < nk; ++i) {
-                const int s1 = i % S1, s2 = i % kS2;
-                mbar_wait(full2(s2), (i / kS2) & 1, 2);
-                mbar_wait(full1(s1), (i / S1) & 1, 3);
+            int s1 = 0, s2 = 0;
+            uint32_t ph1 = 0, ph2 = 0;
+            for (int j = 0; j < ns; ++j) {
+                mbar_wait(full2(s2), ph2, 2);
+                mbar_wait(full1(s1), ph1, 3);
                 tc_fence_after();
-                const uint64_t a_desc = sw128_desc(a_ring + s2 * kATileBytes);
-                const uint64_t b_desc = sw128_desc(b_ring + s1 * p.b_bytes);
+                const int cn = min(G, nk - j * G);
+                uint64_t a_desc = sw128_desc(a_ring + s2 * a_stage);
+                uint64_t b_desc = sw128_desc(b_ring + s1 * b_stage);
+                for (int h = 0; h < cn; ++h) {
 #pragma unroll
-                for (int k = 0; k < tc::kTileCols / 16; ++k) {
-                    const uint32_t acc = (i > 0 || k > 0) ? 1u : 0u;
-                    umma_f16(tmem, a_desc + 2 * k, b_desc + 2 * k, id0, acc);     // +32 bytes a K step of 16
-                    if (p.n_total > 256)
-                        umma_f16(tmem + 256, a_desc + 2 * k, b_desc + (uint64_t)((256 * 128) >> 4) + 2 * k, id1, acc);
+                    for (int k = 0; k < tc::kTileCols / 16; ++k) {
+                        const uint32_t acc = (j > 0 || h > 0 || k > 0) ? 1u : 0u;
+                        umma_f16(tmem, a_desc + 2 * k, b_desc + 2 * k, id0, acc);     // +32 bytes a K step of 16
+                        if (p.n_total > 256)
+                            umma_f16(tmem + 256, a_desc + 2 * k, b_desc + (uint64_t)((256 * 128) >> 4) + 2 * k, id1,
+                                     acc);
+                    }
+                    a_desc += kATileBytes >> 4;
+                    b_desc += (uint32_t)p.b_bytes >> 4;
                 }
                 umma_commit(empty2(s2));
                 umma_commit(empty1(s1));
+                advance(s1, ph1, 1, S1);
+                advance(s2, ph2, 1, kS2);
             }
             umma_commit(done);
         }
         __syncwarp();
     } else {
-        // Expanders: the dense 128 x 64 tile of each column tile, built in shared memory.
-        const int tid = threadIdx.x;
-        for (int i = 0; i < nk; ++i) {
-            const int s1 = i % S1, s2 = i % kS2;
-            mbar_wait(full1(s1), (i / S1) & 1, 4);
-            if (i >= kS2) mbar_wait(empty2(s2), ((i / kS2) - 1) & 1, 5);
-            uint4* a = reinterpret_cast<uint4*>(gbase + (size_t)s2 * kATileBytes);
+        // Expanders: group `grp` builds the dense 128 x 64 tiles of every other stage in shared memory; warp `wg` of
+        // the group owns rows 16 wg .. 16 wg + 15 of each (8-row groups 2 wg and 2 wg + 1 of a segment's header).
+        const int grp = warp / kGroupWarps, wg = warp % kGroupWarps;
+        int s1 = grp % S1, s2 = grp % kS2;
+        uint32_t ph1 = 0, ph2 = 0;
+        for (int j = grp; j < ns; j += kGroups, advance(s1, ph1, kGroups, S1), advance(s2, ph2, kGroups, kS2)) {
+            if (lane == 0) {
+                mbar_wait(full1(s1), ph1, 4);
+                if (j >= kS2) mbar_wait(empty2(s2), ph2 ^ 1u, 5);
+            }
+            __syncwarp();
+            const int c0 = j * G, cn = min(G, nk - c0);
+            const int64_t w0 = s_offs[c0];
+            const uint8_t* slot = gbase + (seg_ring - base) + (size_t)s1 * p.seg_cap;
+            for (int h = 0; h < cn; ++h) {
+                const uint32_t* sg = reinterpret_cast<const uint32_t*>(slot) + (s_offs[c0 + h] - w0);
+                const uint32_t hw = sg[wg];
+                const uint32_t begin = wg ? (sg[wg - 1] >> 16) : 0u, end = hw >> 16;
+                const uint32_t a_off = s2 * a_stage + h * kATileBytes;
+                uint4* rows16 = reinterpret_cast<uint4*>(gbase + a_off + wg * 2048);
 #pragma unroll
-            for (int j = tid; j < kATileBytes / 16; j += kExpThreads) a[j] = make_uint4(0, 0, 0, 0);
-            asm volatile("bar.sync 1, %0;" ::"n"(kExpThreads) : "memory");
-            const int64_t w0 = p.seg[seg0 + i], w1 = p.seg[seg0 + i + 1];
-            const int nq = (int)((w1 - w0) >> 2);
-            const uint4* sg = reinterpret_cast<const uint4*>(gbase + (seg_ring - base) + (size_t)s1 * p.seg_cap);
-            const uint32_t a_s = a_ring + s2 * kATileBytes;
-            for (int q = tid; q < nq; q += kExpThreads) {
-                const uint4 v = sg[q];
-                const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    if (w[e] & tc::kPadWord) continue;
-                    const uint32_t r = (w[e] >> 6) & 127u, c = w[e] & 63u;
-                    const uint32_t off = r * 128u + ((c * 2u) ^ ((r & 7u) << 4));
-                    asm volatile("st.shared.u16 [%0], %1;" ::"r"(a_s + off), "h"((unsigned short)(w[e] >> 16)) : "memory");
+                for (int q = 0; q < 4; ++q) rows16[lane + 32 * q] = make_uint4(0, 0, 0, 0);
+                __syncwarp();
+                const uint32_t a_s = a_ring + a_off;
+                const uint32_t* entries = sg + tc::kHeaderWords;
+                uint32_t e = begin + lane;
+                for (; e + 96 < end; e += 128) {            // four words in flight a lane
+                    const uint32_t x0 = entries[e], x1 = entries[e + 32], x2 = entries[e + 64], x3 = entries[e + 96];
+                    sts_u16(a_s + (x0 & 0x3FFEu), x0 >> 16);
+                    sts_u16(a_s + (x1 & 0x3FFEu), x1 >> 16);
+                    sts_u16(a_s + (x2 & 0x3FFEu), x2 >> 16);
+                    sts_u16(a_s + (x3 & 0x3FFEu), x3 >> 16);
+                }
+                for (; e < end; e += 32) {
+                    const uint32_t x0 = entries[e];
+                    sts_u16(a_s + (x0 & 0x3FFEu), x0 >> 16);
                 }
             }
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -275,13 +332,14 @@ __global__ void __launch_bounds__(kTcThreads, 1) spmm_tc_kernel(const __grid_con
         }
 
         // Epilogue: D[row, token] out of TMEM. Warp w reads lanes 32 (w % 4) .. + 31, every other 16-column chunk.
-        mbar_wait(done, 0, 6);
+        if (lane == 0) mbar_wait(done, 0, 6);
+        __syncwarp();
         tc_fence_after();
-        const int quarter = warp & 3, half = warp >> 2;
+        const int quarter = warp & 3, cgroup = warp >> 2;          // 4 column groups of the 16 expander warps
         const int row_local = quarter * 32 + lane;
         const int64_t row = (int64_t)rt * tc::kTileRows + row_local;
         const bool row_ok = row < p.rows;
-        for (int c = half; c < p.n_total / 16; c += 2) {
+        for (int c = cgroup; c < p.n_total / 16; c += kExpWarps / 4) {
             float v[16];
             tmem_ld16(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(c * 16), v);
 #pragma unroll
@@ -341,7 +399,7 @@ EncodeTiledFn encode_fn() {
 }
 
 struct TcPlan {
-    int n_total, box_rows, n_boxes, tmem_cols, s1, b_bytes, seg_cap, n_split, kt_per_split, smem;
+    int n_total, box_rows, n_boxes, tmem_cols, s1, s2, g, b_bytes, seg_cap, n_split, kt_per_split, smem;
 };
 
 int pow2_at_least(int v) {
@@ -370,6 +428,15 @@ int choose_split(int64_t row_tiles, int col_tiles, int tokens, int sms) {
     return best;
 }
 
+// The column split of one launch: (splits, column tiles a split), at most kMaxTilesPerCta tiles a CTA.
+void plan_split(int64_t row_tiles, int col_tiles, int tokens, int sms, int* n_split, int* per) {
+    int s = choose_split(row_tiles, col_tiles, tokens, sms);
+    int k = (col_tiles + s - 1) / s;
+    if (k > kMaxTilesPerCta) k = kMaxTilesPerCta;
+    *per = k;
+    *n_split = (col_tiles + k - 1) / k;
+}
+
 }  // namespace
 }  // namespace p2p
 
@@ -380,11 +447,13 @@ extern "C" size_t p2p_spmm_tc_workspace(int64_t rows, int64_t cols, int64_t toke
     const int64_t row_tiles = (rows + tc::kTileRows - 1) / tc::kTileRows;
     const int col_tiles = (int)((cols + tc::kTileCols - 1) / tc::kTileCols);
     size_t need = 0;
-    const int chunks[2] = {(int)(tokens < 512 ? tokens : 512), (int)(tokens % 512)};
+    // Every token count a launch may take (512 a launch, 256 when a module's segments leave no room for 512).
+    const int chunks[4] = {(int)(tokens < 512 ? tokens : 512), (int)(tokens % 512), (int)(tokens < 256 ? tokens : 256),
+                           (int)(tokens % 256)};
     for (int t : chunks) {
         if (t <= 0) continue;
-        const int s = choose_split(row_tiles, col_tiles, t, sm_count());
-        const int per = (col_tiles + s - 1) / s, n = (col_tiles + per - 1) / per;
+        int n = 1, per = col_tiles;
+        plan_split(row_tiles, col_tiles, t, sm_count(), &n, &per);
         if (n == 1) continue;
         const size_t w = ((size_t)row_tiles * sizeof(unsigned) + 255) / 256 * 256 +
                          (size_t)n * t * row_tiles * tc::kTileRows * sizeof(float);
@@ -404,7 +473,8 @@ extern "C" int p2p_spmm_tc(const void* x, int dtype, int64_t tokens, int64_t col
     P2P_REQUIRE(cols % 8 == 0 && ldx % 8 == 0 && ldx >= cols && aligned16(x),
                 "p2p_spmm_tc: x needs 16-byte aligned rows (cols and ldx multiples of 8)");
     P2P_REQUIRE(ldy >= rows, "p2p_spmm_tc: ldy %lld below rows %lld", (long long)ldy, (long long)rows);
-    P2P_REQUIRE(seg_cap_words >= 0 && seg_cap_words % 4 == 0 && seg_cap_words <= tc::kTileRows * tc::kTileCols + 4,
+    P2P_REQUIRE(seg_cap_words >= 0 && seg_cap_words % 4 == 0 &&
+                    seg_cap_words <= tc::kHeaderWords + tc::kTileRows * tc::kTileCols + 4,
                 "p2p_spmm_tc: segment capacity %lld words", (long long)seg_cap_words);
     P2P_REQUIRE(rows <= 0x7fffffff && cols <= 0x7fffffff, "p2p_spmm_tc: too large");
     EncodeTiledFn encode = encode_fn();
@@ -415,8 +485,17 @@ extern "C" int p2p_spmm_tc(const void* x, int dtype, int64_t tokens, int64_t col
     const int col_tiles = (int)((cols + tc::kTileCols - 1) / tc::kTileCols);
     const int elem = 2;
 
-    for (int64_t t0 = 0; t0 < tokens; t0 += 512) {             // at most 512 tokens (TMEM columns) a launch
-        const int tn = (int)(tokens - t0 < 512 ? tokens - t0 : 512);
+    // Tokens a launch: up to 512 (TMEM columns), fewer when two x stages of that many rows and the module's largest
+    // segment do not fit beside two A tiles.
+    int chunk = 512;
+    while (chunk > 16) {
+        const int fixed2 = 1024 + 2 * kATileBytes + 8 * (2 * kMaxS1 + 2 * kMaxS2 + 1) + 64;
+        const int seg_b = (int)((seg_cap_words * 4 + 127) / 128 * 128);
+        if ((kSmemLimit - fixed2) / (chunk * 128 + (seg_b ? seg_b : 128)) >= 2) break;
+        chunk /= 2;
+    }
+    for (int64_t t0 = 0; t0 < tokens; t0 += chunk) {
+        const int tn = (int)(tokens - t0 < chunk ? tokens - t0 : chunk);
         TcPlan pl;
         pl.n_total = (tn + 15) / 16 * 16;
         pl.n_boxes = pl.n_total <= 256 ? 1 : 2;
@@ -425,15 +504,41 @@ extern "C" int p2p_spmm_tc(const void* x, int dtype, int64_t tokens, int64_t col
         pl.b_bytes = pl.n_total * 128;
         pl.seg_cap = (int)((seg_cap_words * 4 + 127) / 128 * 128);
         if (pl.seg_cap == 0) pl.seg_cap = 128;
-        const int fixed = 1024 + kS2 * kATileBytes + 8 * (2 * kMaxS1 + 2 * kS2 + 1) + 64;
-        pl.s1 = (kSmemLimit - fixed) / (pl.b_bytes + pl.seg_cap);
+        // Column tiles a stage (G): as many as leave three x / segment stages beside two A stages (more work per
+        // synchronisation); four A stages when a stage is a single column tile and they fit.
+        const int seg_one = (int)((seg_cap_words * 4 + 127) / 128 * 128) > 128
+                                ? (int)((seg_cap_words * 4 + 127) / 128 * 128) : 128;
+        int fixed = 0;
+        pl.g = 1;
+        pl.s2 = 2;
+        pl.s1 = 0;
+        for (int g = 4; g >= 1; g >>= 1) {
+            const int s2 = 2;
+            fixed = 1024 + s2 * g * kATileBytes + 8 * (2 * kMaxS1 + 2 * kMaxS2 + 1) + 64;
+            const int s1 = (kSmemLimit - fixed) / (g * pl.b_bytes + g * seg_one);
+            if (s1 >= 3 || g == 1) {
+                pl.g = g;
+                pl.s2 = s2;
+                pl.s1 = s1;
+                break;
+            }
+        }
+        pl.seg_cap = pl.g * seg_one;
+        if (pl.g == 1) {
+            const int fixed4 = 1024 + 4 * kATileBytes + 8 * (2 * kMaxS1 + 2 * kMaxS2 + 1) + 64;
+            const int s1_4 = (kSmemLimit - fixed4) / (pl.b_bytes + pl.seg_cap);
+            if (s1_4 >= 3) {
+                pl.s2 = 4;
+                pl.s1 = s1_4;
+                fixed = fixed4;
+            }
+        }
         if (pl.s1 > kMaxS1) pl.s1 = kMaxS1;
-        if (pl.s1 < 2) return fail(P2P_EUNSUPPORTED, "p2p_spmm_tc: %d tokens and %d-byte segments exceed shared memory",
-                                   tn, pl.seg_cap);
-        pl.smem = fixed + pl.s1 * (pl.b_bytes + pl.seg_cap);
-        pl.n_split = choose_split(row_tiles, col_tiles, tn, sms);
-        pl.kt_per_split = (col_tiles + pl.n_split - 1) / pl.n_split;
-        pl.n_split = (col_tiles + pl.kt_per_split - 1) / pl.kt_per_split;
+        if (pl.s1 < 2)
+            return fail(P2P_EUNSUPPORTED, "p2p_spmm_tc: %d tokens and %d-byte segments exceed shared memory", tn,
+                        seg_one);
+        pl.smem = fixed + pl.s1 * (pl.g * pl.b_bytes + pl.seg_cap);
+        plan_split(row_tiles, col_tiles, tn, sms, &pl.n_split, &pl.kt_per_split);
 
         TcParams prm;
         prm.words = words;
@@ -446,6 +551,8 @@ extern "C" int p2p_spmm_tc(const void* x, int dtype, int64_t tokens, int64_t col
         prm.n_boxes = pl.n_boxes;
         prm.tmem_cols = pl.tmem_cols;
         prm.s1 = pl.s1;
+        prm.s2 = pl.s2;
+        prm.g = pl.g;
         prm.b_bytes = pl.b_bytes;
         prm.seg_cap = pl.seg_cap;
         prm.kt_per_split = pl.kt_per_split;

@@ -65,9 +65,10 @@ __global__ void __launch_bounds__(kBuildBlock) count_kernel(Blocks bl, int64_t r
     }
 }
 
-// Within each segment, cnt[row, ct] becomes the words of the rows above `row`; segcnt = the padded segment size.
+// Within each segment, cnt[row, ct] becomes the entries of the rows above `row`; segraw = the segment's entries,
+// segcnt = its words (header + entries padded to a multiple of 4).
 __global__ void __launch_bounds__(kBuildBlock) prefix_kernel(int64_t rows, int n_ct, int* __restrict__ cnt,
-                                                              int64_t* __restrict__ segcnt) {
+                                                              int64_t* __restrict__ segcnt, int* __restrict__ segraw) {
     const int64_t rt = blockIdx.x;
     for (int ct = threadIdx.x; ct < n_ct; ct += kBuildBlock) {
         int64_t run = 0;
@@ -78,7 +79,23 @@ __global__ void __launch_bounds__(kBuildBlock) prefix_kernel(int64_t rows, int n
             cnt[row * n_ct + ct] = (int)run;
             run += c;
         }
-        segcnt[rt * n_ct + ct] = (run + 3) & ~(int64_t)3;
+        segraw[rt * n_ct + ct] = (int)run;
+        segcnt[rt * n_ct + ct] = tc::kHeaderWords + ((run + 3) & ~(int64_t)3);
+    }
+}
+
+// Each segment's header: the entries of its 8-row groups, cumulative.
+__global__ void header_kernel(int64_t rows, int n_ct, int64_t n_seg, const int* __restrict__ cnt,
+                              const int* __restrict__ segraw, const int64_t* __restrict__ seg,
+                              uint32_t* __restrict__ words) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n_seg; i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t rt = i / n_ct, ct = i % n_ct;
+        uint32_t h[16];
+        for (int j = 0; j < 16; ++j) {
+            const int64_t next = rt * tc::kTileRows + (int64_t)tc::kGroupRows * (j + 1);   // first row past group j
+            h[j] = (j < 15 && next < rows) ? (uint32_t)cnt[next * n_ct + ct] : (uint32_t)segraw[i];
+        }
+        for (int m = 0; m < tc::kHeaderWords; ++m) words[seg[i] + m] = (h[2 * m] & 0xffffu) | (h[2 * m + 1] << 16);
     }
 }
 
@@ -112,7 +129,7 @@ __global__ void __launch_bounds__(1024) scan_kernel(const int64_t* __restrict__ 
 
 __global__ void fill_pad_kernel(uint32_t* __restrict__ words, int64_t n) {
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
-        words[i] = tc::kPadWord;
+        words[i] = tc::kFillWord;
 }
 
 __device__ int g_fill_errors;
@@ -148,7 +165,7 @@ __global__ void __launch_bounds__(kBuildBlock) fill_kernel(Blocks bl, int64_t ro
             const int col = col_at<I>(b, lr, j);
             const int ct = col >> 6;
             const int64_t rank = j - first[ct];
-            const int64_t pos = seg[rt * n_ct + ct] + cnt[row * n_ct + ct] + rank;
+            const int64_t pos = seg[rt * n_ct + ct] + tc::kHeaderWords + cnt[row * n_ct + ct] + rank;
             if (rank < 0 || rank >= hist[ct] || pos >= n_words) {   // indices not ascending: refuse, never write
                 atomicAdd(&g_fill_errors, 1);
                 continue;
@@ -183,8 +200,26 @@ extern "C" size_t p2p_tiles_workspace(const p2p_row_block* blocks, int nblocks, 
     if (!blocks || nblocks < 1 || cols < 1) return 0;
     const Shape s = shape_of(blocks, nblocks, cols);
     const size_t cnt_bytes = (size_t)s.row_tiles * tc::kTileRows * s.col_tiles * sizeof(int);
-    return (cnt_bytes + 255) / 256 * 256 + (size_t)s.n_seg * sizeof(int64_t);
+    return (cnt_bytes + 255) / 256 * 256 + (size_t)s.n_seg * (sizeof(int64_t) + sizeof(int)) + 256;
 }
+
+namespace {
+// Scratch of the builder: cnt [row_tiles * 128, col_tiles] int, segcnt [n_seg] int64, segraw [n_seg] int.
+struct BuildScratch {
+    int* cnt;
+    int64_t* segcnt;
+    int* segraw;
+};
+BuildScratch scratch_of(void* workspace, const Shape& s) {
+    BuildScratch b;
+    const size_t cnt_bytes = (size_t)s.row_tiles * tc::kTileRows * s.col_tiles * sizeof(int);
+    char* w = reinterpret_cast<char*>(workspace);
+    b.cnt = reinterpret_cast<int*>(w);
+    b.segcnt = reinterpret_cast<int64_t*>(w + (cnt_bytes + 255) / 256 * 256);
+    b.segraw = reinterpret_cast<int*>(b.segcnt + s.n_seg);
+    return b;
+}
+}  // namespace
 
 extern "C" int p2p_tiles_plan(const p2p_row_block* blocks, int nblocks, int idx_bytes, int64_t cols, int64_t* seg,
                               int64_t* total_words, void* workspace, size_t workspace_bytes, void* stream) {
@@ -194,9 +229,10 @@ extern "C" int p2p_tiles_plan(const p2p_row_block* blocks, int nblocks, int idx_
     const Shape s = shape_of(blocks, nblocks, cols);
     P2P_REQUIRE(workspace_bytes >= p2p_tiles_workspace(blocks, nblocks, cols), "p2p_tiles_plan: workspace too small");
     cudaStream_t st = as_stream(stream);
-    int* cnt = reinterpret_cast<int*>(workspace);
+    const BuildScratch sc = scratch_of(workspace, s);
+    int* cnt = sc.cnt;
+    int64_t* segcnt = sc.segcnt;
     const size_t cnt_bytes = (size_t)s.row_tiles * tc::kTileRows * s.col_tiles * sizeof(int);
-    int64_t* segcnt = reinterpret_cast<int64_t*>(reinterpret_cast<char*>(workspace) + (cnt_bytes + 255) / 256 * 256);
     if (cudaMemsetAsync(cnt, 0, cnt_bytes, st) != cudaSuccess) return launch_status("p2p_tiles_plan memset");
     const int smem = (int)(s.col_tiles * sizeof(int));
     const int grid = (int)(s.rows < sm_count() * 8 ? s.rows : sm_count() * 8);
@@ -208,7 +244,7 @@ extern "C" int p2p_tiles_plan(const p2p_row_block* blocks, int nblocks, int idx_
             if (int e = allow_smem((const void*)count_kernel<int32_t>, smem, "p2p_tiles_plan")) return e;
             count_kernel<int32_t><<<grid, kBuildBlock, smem, st>>>(bl, s.rows, (int)s.col_tiles, cnt);
         }
-        prefix_kernel<<<(unsigned)s.row_tiles, kBuildBlock, 0, st>>>(s.rows, (int)s.col_tiles, cnt, segcnt);
+        prefix_kernel<<<(unsigned)s.row_tiles, kBuildBlock, 0, st>>>(s.rows, (int)s.col_tiles, cnt, segcnt, sc.segraw);
     }
     scan_kernel<<<1, 1024, 0, st>>>(segcnt, s.n_seg, seg);
     if (int e = launch_status("p2p_tiles_plan")) return e;
@@ -229,11 +265,15 @@ extern "C" int p2p_tiles_fill(const p2p_row_block* blocks, int nblocks, int idx_
     P2P_REQUIRE(workspace_bytes >= p2p_tiles_workspace(blocks, nblocks, cols), "p2p_tiles_fill: workspace too small");
     const Shape s = shape_of(blocks, nblocks, cols);
     cudaStream_t st = as_stream(stream);
-    const int* cnt = reinterpret_cast<const int*>(workspace);
+    const BuildScratch sc = scratch_of(workspace, s);
+    const int* cnt = sc.cnt;
     const int zero = 0;
     if (cudaMemcpyToSymbolAsync(g_fill_errors, &zero, sizeof(int), 0, cudaMemcpyHostToDevice, st) != cudaSuccess)
         return launch_status("p2p_tiles_fill reset");
     if (n_words > 0) fill_pad_kernel<<<sm_count() * 4, 256, 0, st>>>(words, n_words);
+    if (s.n_seg > 0)
+        header_kernel<<<(unsigned)((s.n_seg + 255) / 256), 256, 0, st>>>(s.rows, (int)s.col_tiles, s.n_seg, cnt,
+                                                                          sc.segraw, seg, words);
     const int smem = (int)(2 * s.col_tiles * sizeof(int));
     const int grid = (int)(s.rows < sm_count() * 8 ? s.rows : sm_count() * 8);
     if (s.rows > 0) {

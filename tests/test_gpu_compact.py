@@ -118,7 +118,7 @@ def test_bad_indices_are_refused_at_load():
 
 def test_words_with_the_wrong_count_are_refused():
     values = torch.randn(2, 3, device="cuda")
-    words = torch.tensor([[0b111], [0b1011]], dtype=torch.int32, device="cuda")
+    words = torch.tensor([[0b111], [0b1111]], dtype=torch.int32, device="cuda")   # 3 and 4 bits
     with pytest.raises(P2PError, match="exactly"):
         compact.Tiles([("sparse", values, words, 8)])
 

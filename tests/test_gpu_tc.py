@@ -33,6 +33,8 @@ def _check(got, want, dtype):
 @pytest.mark.parametrize("rows,cols,keep", [(128, 64, 36), (300, 1000, 7), (1024, 4096, 33), (17, 8, 50),
                                             (200, 5120, 90)])
 def test_layout_decodes_to_the_selection(rows, cols, keep):
+    """Every segment: a header of cumulative 8-row-group counts, then one word per kept weight in row order holding
+    its value and its swizzled byte offset in the 128 x 64 tile; decoded, the layout is the selection, bit for bit."""
     values, idx = _module(rows, cols, keep)
     words, seg, cap = kernels.tiles_build([(0, values, idx)], cols)
     w = words.cpu().numpy().view(np.uint32)
@@ -41,14 +43,23 @@ def test_layout_decodes_to_the_selection(rows, cols, keep):
     got = np.zeros((rows, cols), np.uint16)
     seen = np.zeros((rows, cols), np.int32)
     for i in range(len(s) - 1):
-        assert s[i] % 4 == 0 and s[i + 1] >= s[i]
+        assert s[i] % 4 == 0 and s[i + 1] >= s[i] + 8
         rt, ct = divmod(i, n_ct)
-        for word in w[s[i]:s[i + 1]]:
-            if word & (1 << 13):
-                continue
-            r, c = rt * 128 + ((word >> 6) & 127), ct * 64 + (word & 63)
-            got[r, c] = word >> 16
-            seen[r, c] += 1
+        hdr = np.stack([w[s[i]:s[i] + 8] & 0xFFFF, w[s[i]:s[i] + 8] >> 16], axis=1).reshape(16)
+        assert (np.diff(hdr) >= 0).all()
+        count = int(hdr[15])
+        assert s[i + 1] - s[i] == 8 + ((count + 3) & ~3)
+        ents = w[s[i] + 8:s[i] + 8 + count].astype(np.int64)
+        off = ents & 0x3FFF
+        assert (off % 2 == 0).all()
+        r = off >> 7
+        c = ((((off >> 4) & 7) ^ (r & 7)) << 3) | ((off & 15) >> 1)
+        group = r // 8
+        e = np.arange(count)
+        lo = np.where(group > 0, np.concatenate([[0], hdr])[group], 0)
+        assert ((lo <= e) & (e < hdr[group])).all()
+        np.add.at(seen, (rt * 128 + r, ct * 64 + c), 1)
+        got[rt * 128 + r, ct * 64 + c] = (ents >> 16).astype(np.uint16)
     assert cap == int(np.diff(s).max())
     want = np.zeros((rows, cols), np.uint16)
     np.put_along_axis(want, idx.cpu().numpy().astype(np.int64), _bits(values), axis=1)
@@ -60,7 +71,8 @@ def test_layout_decodes_to_the_selection(rows, cols, keep):
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 @pytest.mark.parametrize("t", [1, 3, 16, 17, 31, 64, 100, 255, 256, 257, 272, 512, 513, 600])
-@pytest.mark.parametrize("rows,cols,keep", [(512, 5120, 40), (300, 1000, 7), (1024, 2048, 25), (17, 8, 50)])
+@pytest.mark.parametrize("rows,cols,keep", [(512, 5120, 40), (300, 1000, 7), (1024, 2048, 25), (17, 8, 50),
+                                            (200, 5120, 95)])
 def test_tc_matches_the_dense_matmul(dtype, t, rows, cols, keep):
     values, idx = _module(rows, cols, keep, dtype, seed=t)
     tiles = compact.Tiles([("compact", values, idx, cols)])
