@@ -53,7 +53,7 @@ def build(force: bool = False, verbose: bool = False) -> str:
             sys.stderr.write(r.stderr)
         objs.append(obj)
     tmp = LIB + ".tmp"
-    r = subprocess.run([nvcc(), *ARCH, "-shared", "-o", tmp, *objs, "-lcuda"], capture_output=True, text=True)
+    r = subprocess.run([nvcc(), *ARCH, "-shared", "-o", tmp, *objs], capture_output=True, text=True)
     if r.returncode:
         raise RuntimeError(f"nvcc link failed:\n{r.stderr[-4000:]}")
     os.replace(tmp, LIB)
