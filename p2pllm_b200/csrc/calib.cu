@@ -135,10 +135,14 @@ SumsqShape sumsq_shape(int64_t tokens, int64_t cols, int vec) {
     return s;
 }
 
+// The workspace: a fixed region of ticket counters (so that no call's partials ever overlap another call's
+// counters, whatever the shapes) and the fp64 partials after it.
+constexpr int64_t kMaxStrips = 16384;
+constexpr size_t kTicketRegion = kMaxStrips * sizeof(unsigned);
+
 size_t workspace_for(const SumsqShape& s, int64_t cols) {
     if (s.slabs <= 1) return 0;
-    const size_t ticket_bytes = ((size_t)s.strips * sizeof(unsigned) + 255) / 256 * 256;
-    return ticket_bytes + (size_t)s.slabs * cols * sizeof(double);
+    return kTicketRegion + (size_t)s.slabs * cols * sizeof(double);
 }
 
 // The vectorised kernel needs 16-byte aligned rows; anything else takes the one-element-a-thread variant.
@@ -228,6 +232,7 @@ __global__ void __launch_bounds__(kBlock) norms_kernel(const double* __restrict_
 }
 
 }  // namespace
+
 }  // namespace p2p
 
 using namespace p2p;
@@ -254,9 +259,10 @@ extern "C" int p2p_sumsq_cols(const void* x, int dtype, int64_t tokens, int64_t 
     const size_t need = workspace_for(s, cols);
     P2P_REQUIRE(workspace_bytes >= need && (need == 0 || workspace),
                 "p2p_sumsq_cols: workspace of %zu bytes, %zu needed", workspace_bytes, need);
+    if (s.strips > kMaxStrips)
+        return fail(P2P_EUNSUPPORTED, "p2p_sumsq_cols: %lld columns is too many", (long long)cols);
     unsigned* tickets = reinterpret_cast<unsigned*>(workspace);
-    const size_t ticket_bytes = ((size_t)s.strips * sizeof(unsigned) + 255) / 256 * 256;
-    double* partial = need ? reinterpret_cast<double*>(reinterpret_cast<char*>(workspace) + ticket_bytes) : nullptr;
+    double* partial = need ? reinterpret_cast<double*>(reinterpret_cast<char*>(workspace) + kTicketRegion) : nullptr;
     const dim3 grid((unsigned)s.strips, (unsigned)s.slabs);
     P2P_DISPATCH(dtype, {
         const scalar_t* xp = reinterpret_cast<const scalar_t*>(x);

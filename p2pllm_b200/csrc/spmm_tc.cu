@@ -42,6 +42,10 @@ constexpr int kMaxTilesPerCta = 1024;                              // segment of
 // Dynamic shared memory: the 227 KiB a block may hold, less the static offsets array and a few scalars.
 constexpr int kSmemLimit = 227 * 1024 - (int)sizeof(int64_t) * (kMaxTilesPerCta + 1) - 256;
 constexpr uint64_t kWaitNs = 2000000000ull;
+// The workspace: a fixed region of per-row-tile ticket counters, then the fp32 partials; no call's partials can
+// overlap another call's counters, whatever the shapes.
+constexpr int64_t kMaxRowTiles = 16384;
+constexpr size_t kTicketRegion = kMaxRowTiles * sizeof(unsigned);
 
 __device__ int g_tc_error;            // first failed wait of the last launches (0: none); read back by the host
 
@@ -455,8 +459,7 @@ extern "C" size_t p2p_spmm_tc_workspace(int64_t rows, int64_t cols, int64_t toke
         int n = 1, per = col_tiles;
         plan_split(row_tiles, col_tiles, t, sm_count(), &n, &per);
         if (n == 1) continue;
-        const size_t w = ((size_t)row_tiles * sizeof(unsigned) + 255) / 256 * 256 +
-                         (size_t)n * t * row_tiles * tc::kTileRows * sizeof(float);
+        const size_t w = kTicketRegion + (size_t)n * t * row_tiles * tc::kTileRows * sizeof(float);
         need = need > w ? need : w;
     }
     return need;
@@ -563,13 +566,12 @@ extern "C" int p2p_spmm_tc(const void* x, int dtype, int64_t tokens, int64_t col
         prm.partial = nullptr;
         prm.tickets = nullptr;
         if (pl.n_split > 1) {
-            const size_t need = ((size_t)row_tiles * sizeof(unsigned) + 255) / 256 * 256 +
-                                (size_t)pl.n_split * tn * prm.rows_pad * sizeof(float);
+            const size_t need = kTicketRegion + (size_t)pl.n_split * tn * prm.rows_pad * sizeof(float);
             P2P_REQUIRE(workspace && workspace_bytes >= need, "p2p_spmm_tc: workspace of %zu bytes, %zu needed",
                         workspace_bytes, need);
+            if (row_tiles > kMaxRowTiles) return fail(P2P_EUNSUPPORTED, "p2p_spmm_tc: %lld rows is too many", (long long)rows);
             prm.tickets = reinterpret_cast<unsigned*>(workspace);
-            const size_t tb = ((size_t)row_tiles * sizeof(unsigned) + 255) / 256 * 256;
-            prm.partial = reinterpret_cast<float*>(reinterpret_cast<char*>(workspace) + tb);
+            prm.partial = reinterpret_cast<float*>(reinterpret_cast<char*>(workspace) + kTicketRegion);
         }
 
         CUtensorMap map;

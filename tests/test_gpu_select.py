@@ -140,6 +140,19 @@ def test_sumsq_strided_and_misaligned_rows():
     assert np.allclose(sums.cpu().numpy(), oracle.sumsq_cols(x.cpu().numpy()), rtol=1e-6)
 
 
+def test_sumsq_calls_of_different_shapes_share_a_workspace():
+    """A call with more column strips after one with fewer must find its counters zero (they live apart from the
+    partials)."""
+    shapes = [(100000, 4096, torch.bfloat16), (30000, 16384, torch.float32), (50000, 1024, torch.float16),
+              (30000, 16384, torch.float32)]
+    for rows, cols, dt in shapes:
+        x = torch.randn(rows, cols, device="cuda").to(dt)
+        sums = torch.zeros(cols, dtype=torch.float64, device="cuda")
+        kernels.sumsq_cols(x, sums)
+        want = x.double().pow(2).sum(0)
+        assert torch.allclose(sums, want, rtol=1e-5, atol=0), (rows, cols, dt)
+
+
 def test_sumsq_is_deterministic():
     x = torch.randn(100000, 1024, device="cuda").bfloat16()
     a = torch.zeros(1024, dtype=torch.float64, device="cuda")

@@ -143,3 +143,16 @@ def test_llama_shapes_at_17_and_272_tokens():
             sample = torch.arange(0, p.rows, 97, device="cuda")
             want = oracle.forward(_bits(x), _bits(values[sample]), idx[sample].cpu().numpy(), p.cols, "bf16")
             _check(y[:, sample], want, torch.bfloat16)
+
+
+def test_split_launches_of_different_shapes_share_a_workspace():
+    """Column-split launches with few row tiles, then many: each finds its ticket counters zero."""
+    for rows, cols in ((256, 4096), (14336, 4096), (512, 14336), (28672, 4096)):
+        values, idx = _module(rows, cols, 36, seed=rows)
+        tiles = compact.Tiles([("compact", values, idx, cols)])
+        x = torch.randn(17, cols, device="cuda").bfloat16()
+        y = tiles(x)
+        kernels.spmm_tc_status()
+        sample = torch.arange(0, rows, 61, device="cuda")
+        want = oracle.forward(_bits(x), _bits(values[sample]), idx[sample].cpu().numpy(), cols, "bf16")
+        _check(y[:, sample], want, torch.bfloat16)
