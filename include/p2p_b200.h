@@ -54,6 +54,17 @@ size_t p2p_sumsq_workspace(int64_t tokens, int64_t cols, int dtype);
 int p2p_sumsq_cols(const void* x, int dtype, int64_t tokens, int64_t cols, int64_t ldx, double* sums,
                    void* workspace, size_t workspace_bytes, void* stream);
 
+/* p2p_sumsq_cols for callers that cannot allocate device memory: the same reduction (same rounding, deterministic),
+ * with its scratch held inside the library in one fixed device array of 4 MiB + 4 KiB per GPU (kept until the process
+ * exits) instead of a caller-provided workspace. It allocates nothing. For a calibration hook running inside a serving
+ * engine that has already reserved its share of GPU memory (SGLang's static fraction for weights and the KV pool),
+ * where a fresh allocation can fail or fragment what is left. cols <= 16,384 (P2P_EUNSUPPORTED above). The first call
+ * on each device looks up the array's device address; make that first call before any stream capture. Every call
+ * uses the same array: calls that overlap on the GPU (other streams, other host threads) race and must be ordered by
+ * the caller. No counterpart in the reference (p2pLLM allocates through torch). */
+int p2p_sumsq_cols_noalloc(const void* x, int dtype, int64_t tokens, int64_t cols, int64_t ldx, double* sums,
+                           void* stream);
+
 /* Per-expert sums of squares of the tokens routed to each expert: into[e, c] += (double)(float)sum over the tokens t
  * whose ids row holds e (each token once per expert) of x[t, c]^2. order: the `tokens * topk` (token, slot) pairs
  * sorted by expert and then token (order[i] = token * topk + slot), seg: [n_experts + 1] offsets into order per expert.

@@ -31,6 +31,7 @@ SIGNATURES = {
     "p2p_abi_version": ([], _int),
     "p2p_sumsq_workspace": ([_i64, _i64, _int], _sz),
     "p2p_sumsq_cols": ([_vp, _int, _i64, _i64, _i64, _vp, _vp, _sz, _vp], _int),
+    "p2p_sumsq_cols_noalloc": ([_vp, _int, _i64, _i64, _i64, _vp, _vp], _int),
     "p2p_expert_sumsq": ([_vp, _int, _i64, _i64, _i64, _vp, _vp, _i64, _i64, _vp, _vp], _int),
     "p2p_channel_norms": ([_vp, _i64, _i64, _int, _vp, _vp], _int),
     "p2p_wanda_select": ([_vp, _int, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _vp, _int, _i64, _vp, _i64, _vp, _i64,

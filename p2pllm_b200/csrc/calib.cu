@@ -7,6 +7,8 @@
 // meet in the workspace: each writes its fp64 partial there, and the last slab to finish (a ticket counter per strip)
 // adds the partials in slab order, rounds the column total to fp32 as the reference's fp32 sum does, and adds it to
 // the caller's fp64 sums. The result therefore does not depend on which block finishes first.
+#include <mutex>
+
 #include "common.cuh"
 
 namespace p2p {
@@ -233,9 +235,83 @@ __global__ void __launch_bounds__(kBlock) norms_kernel(const double* __restrict_
 
 }  // namespace
 
+// ---- the reduction with its scratch inside the library ----------------------------------------------------------
+//
+// Some callers cannot allocate device memory: the calibration hook runs inside an SGLang forward pass, after SGLang
+// has reserved its static share of the GPU for weights and the KV pool, where an extra allocation can fail or
+// fragment what is left. For them the scratch lives in this fixed array: 4 MiB of fp64 partials plus 4 KiB of ticket
+// counters, enough for up to 16,384 columns. Every GPU that loads the library holds one copy until the process exits.
+constexpr int64_t kNoAllocMaxCols = 16384;
+constexpr size_t kNoAllocTicketBytes = 4096;                      // 1024 strips' counters (16,384 columns need 512)
+constexpr size_t kNoAllocPartialBytes = 4u << 20;
+static __device__ __align__(256) unsigned char g_sumsq_scratch[kNoAllocTicketBytes + kNoAllocPartialBytes];
+
+namespace {
+std::mutex g_scratch_mutex;
+void* g_scratch_addr[64] = {nullptr};
+
+// The device address of g_sumsq_scratch on the current device, looked up once per device (the host-side name of a
+// __device__ array is only a stand-in, not an address a kernel may use).
+int scratch_address(void** out) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return fail(P2P_ECUDA, "no current CUDA device");
+    std::lock_guard<std::mutex> lock(g_scratch_mutex);
+    if (!g_scratch_addr[dev]) {
+        void* ptr = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&ptr, g_sumsq_scratch);
+        if (e != cudaSuccess || !ptr)
+            return fail(P2P_ECUDA, "p2p_sumsq_cols_noalloc: scratch address lookup failed: %s", cudaGetErrorString(e));
+        g_scratch_addr[dev] = ptr;
+    }
+    *out = g_scratch_addr[dev];
+    return P2P_OK;
+}
+}  // namespace
+
 }  // namespace p2p
 
 using namespace p2p;
+
+extern "C" int p2p_sumsq_cols_noalloc(const void* x, int dtype, int64_t tokens, int64_t cols, int64_t ldx,
+                                      double* sums, void* stream) {
+    P2P_REQUIRE(tokens >= 0 && cols >= 0, "p2p_sumsq_cols_noalloc: negative shape [%lld, %lld]", (long long)tokens,
+                (long long)cols);
+    if (tokens == 0 || cols == 0) return P2P_OK;
+    P2P_REQUIRE(x && sums, "p2p_sumsq_cols_noalloc: null x or sums");
+    P2P_REQUIRE(ldx >= cols, "p2p_sumsq_cols_noalloc: row stride %lld below %lld columns", (long long)ldx,
+                (long long)cols);
+    if (!dtype_ok(dtype)) return fail(P2P_EUNSUPPORTED, "p2p_sumsq_cols_noalloc: dtype %d", dtype);
+    if (cols > kNoAllocMaxCols)
+        return fail(P2P_EUNSUPPORTED, "p2p_sumsq_cols_noalloc: %lld columns; its built-in scratch holds at most %lld "
+                    "(use p2p_sumsq_cols with a workspace)", (long long)cols, (long long)kNoAllocMaxCols);
+    const int vec = pick_vec(x, dtype, cols, ldx);
+    SumsqShape s = sumsq_shape(tokens, cols, vec);
+    // Fewer, taller slabs when the usual split would not fit the fixed scratch.
+    const int64_t max_slabs = (int64_t)(kNoAllocPartialBytes / ((size_t)cols * sizeof(double)));
+    if (s.slabs > max_slabs) {
+        s.rows_per_slab = (tokens + max_slabs - 1) / max_slabs;
+        s.slabs = (tokens + s.rows_per_slab - 1) / s.rows_per_slab;
+    }
+    void* scratch = nullptr;
+    if (int e = scratch_address(&scratch)) return e;
+    unsigned* tickets = reinterpret_cast<unsigned*>(scratch);
+    double* partial = reinterpret_cast<double*>(reinterpret_cast<char*>(scratch) + kNoAllocTicketBytes);
+    cudaStream_t st = as_stream(stream);
+    // The array keeps whatever the last call left: the counters must start at zero.
+    if (s.slabs > 1 && cudaMemsetAsync(tickets, 0, (size_t)s.strips * sizeof(unsigned), st) != cudaSuccess)
+        return launch_status("p2p_sumsq_cols_noalloc: clearing the counters");
+    const dim3 grid((unsigned)s.strips, (unsigned)s.slabs);
+    P2P_DISPATCH(dtype, {
+        const scalar_t* xp = reinterpret_cast<const scalar_t*>(x);
+        if (vec == 1)
+            sumsq_kernel<scalar_t, 1><<<grid, kBlock, 0, st>>>(xp, tokens, cols, ldx, s.rows_per_slab, sums, partial,
+                                                               tickets);
+        else
+            sumsq_kernel<scalar_t, Vec<scalar_t>::n><<<grid, kBlock, 0, st>>>(xp, tokens, cols, ldx, s.rows_per_slab,
+                                                                              sums, partial, tickets);
+    });
+    return launch_status("p2p_sumsq_cols_noalloc");
+}
 
 extern "C" size_t p2p_sumsq_workspace(int64_t tokens, int64_t cols, int dtype) {
     if (tokens <= 0 || cols <= 0 || !dtype_ok(dtype)) return 0;
