@@ -5,12 +5,12 @@
 // mma.sync fragments and re-reads every weight once per 64 tokens. Here a CTA owns one 128-row tile and a range of
 // 64-column tiles (split-K), and every token of the pass at once (up to 512 in TMEM):
 //
-//   warp 16 (producer)  per column tile: TMA of the x tile [tokens x 64] (128-byte swizzle) into ring 1, and a bulk
-//                       copy of the segment's packed words from HBM into ring 1 beside it; one mbarrier, tx-counted.
-//   warps 0-15 (expand) two groups of 8 warps take alternate column tiles; in a group each warp owns 16 rows of the
-//                       128 x 64 bf16 tile in ring 2: it zeroes them and writes its rows' values at the swizzled byte
-//                       offsets the words carry (lanes take consecutive words, so a store touches one or two rows and
-//                       few banks clash). No block-wide barrier: a warp's rows are its own.
+//   warp 16 (producer)  per column tile: TMA of the x tile [tokens x 64] (128-byte swizzle) into the x ring, one
+//                       producer lane per ring slot.
+//   warps 0-15 (expand) two groups of 8 warps take alternate column tiles. A group zeroes a 128 x 64 bf16 tile in the
+//                       A ring (each warp 16 rows), meets at a named barrier, and each warp writes its piece of the
+//                       segment's words at the swizzled byte offsets they carry. The words come straight from HBM into
+//                       registers (coalesced, read one tile ahead), never through shared memory.
 //   warp 17 (MMA)       one elected thread issues tcgen05.mma (M = 128, N = tokens rounded to 16, K = 16 a step)
 //                       with the accumulator D[128 x N] fp32 in TMEM; tcgen05.commit frees both rings' slots.
 //   warps 0-15 (epilogue) tcgen05.ld D out of TMEM, round, and write y[t, row] (coalesced along rows), or write fp32
@@ -36,8 +36,10 @@ constexpr int kProducerWarp = kExpWarps;
 constexpr int kMmaWarp = kExpWarps + 1;
 constexpr int kTcThreads = kExpWarps * 32 + 64;
 constexpr int kATileBytes = tc::kTileRows * tc::kTileCols * 2;   // 16 KiB
-constexpr int kMaxS2 = 4;                                          // A tiles in flight (2 or 4)
-constexpr int kMaxS1 = 8;
+constexpr int kASlotBytes = kATileBytes + 1024;                    // + the pad filler words write into; 1 KiB aligned
+constexpr int kMaxStages = 8;                                      // (A tile, x tile) slots in flight (even)
+constexpr int kPrefetch = 14;                                      // segment words a lane holds in registers a tile
+constexpr uint32_t kOffsetMask = 0x7FFEu;
 constexpr int kMaxTilesPerCta = 1024;                              // segment offsets staged in shared memory
 // Dynamic shared memory: the 227 KiB a block may hold, less the static offsets array and a few scalars.
 constexpr int kSmemLimit = 227 * 1024 - (int)sizeof(int64_t) * (kMaxTilesPerCta + 1) - 256;
@@ -53,7 +55,7 @@ struct TcParams {
     const uint32_t* words;            // the module's packed words
     const int64_t* seg;               // [row_tiles * col_tiles + 1]
     int rows, col_tiles, tokens, n_total, box_rows, n_boxes, tmem_cols;
-    int s1, s2, g, b_bytes, seg_cap, kt_per_split, n_split;   // g: column tiles a stage; seg_cap: a stage's words
+    int stages, b_bytes, kt_per_split, n_split;
     void* y;
     int64_t ldy;
     float* partial;                   // [n_split, tokens, rows_pad] when n_split > 1
@@ -131,12 +133,6 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map
         : "memory");
 }
 
-__device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
-    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
-                 "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(bar)
-                 : "memory");
-}
-
 // Shared-memory matrix descriptor of a K-major tile in the 128-byte swizzle layout: rows of 128 bytes, 8-row atoms of
 // 1024 bytes (stride byte offset), version 1, swizzle mode 2 (128B).
 __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
@@ -179,6 +175,32 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
     for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// A warp's share of one segment's words: [lo, hi) in the module's word array. The segment's words after its header
+// are cut into kGroupWarps contiguous pieces; any piece will do, since every word carries its own place in the tile.
+__device__ __forceinline__ void warp_piece(const int64_t* offs, int i, int wg, int64_t& lo, int64_t& hi) {
+    const int64_t s0 = offs[i], s1 = offs[i + 1];
+    const int64_t body = s1 - s0 - tc::kHeaderWords;
+    const int64_t per = (body + kGroupWarps - 1) / kGroupWarps;
+    lo = s0 + tc::kHeaderWords + (int64_t)wg * per;
+    hi = lo + per < s1 ? lo + per : s1;
+}
+
+__device__ __forceinline__ uint32_t ldg_stream(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.global.nc.L1::no_allocate.b32 %0, [%1];" : "=r"(v) : "l"(p));
+    return v;
+}
+
+// The first kPrefetch * 32 words of a warp's piece, one lane every 32nd word (coalesced); filler past the end.
+__device__ __forceinline__ void load_piece(const uint32_t* words, int64_t lo, int64_t hi, int lane,
+                                           uint32_t (&buf)[kPrefetch]) {
+#pragma unroll
+    for (int k = 0; k < kPrefetch; ++k) {
+        const int64_t e = lo + lane + 32 * k;
+        buf[k] = e < hi ? ldg_stream(words + e) : tc::kFillWord;
+    }
+}
+
 template <typename T>
 __global__ void __launch_bounds__(kTcThreads, 1) spmm_tc_kernel(const __grid_constant__ CUtensorMap tmap_x, TcParams p) {
     extern __shared__ uint8_t smem_raw[];
@@ -188,35 +210,28 @@ __global__ void __launch_bounds__(kTcThreads, 1) spmm_tc_kernel(const __grid_con
     const uint32_t raw = smem_u32(smem_raw);
     const uint32_t base = (raw + 1023u) & ~1023u;
     uint8_t* gbase = smem_raw + (base - raw);
-    const int S1 = p.s1, kS2 = p.s2, G = p.g;
-    const uint32_t a_stage = (uint32_t)G * kATileBytes, b_stage = (uint32_t)G * p.b_bytes;
-    const uint32_t a_ring = base;
-    const uint32_t b_ring = a_ring + kS2 * a_stage;
-    const uint32_t seg_ring = b_ring + S1 * b_stage;
-    const uint32_t bars = seg_ring + S1 * p.seg_cap;
-    auto full1 = [&](int s) { return bars + 8u * s; };
-    auto empty1 = [&](int s) { return bars + 8u * (kMaxS1 + s); };
-    auto full2 = [&](int s) { return bars + 8u * (2 * kMaxS1 + s); };
-    auto empty2 = [&](int s) { return bars + 8u * (2 * kMaxS1 + kMaxS2 + s); };
-    const uint32_t done = bars + 8u * (2 * kMaxS1 + 2 * kMaxS2);
+    const int S = p.stages;
+    const uint32_t a_ring = base;                                  // S slots of kASlotBytes
+    const uint32_t x_ring = a_ring + S * kASlotBytes;              // S slots of b_bytes
+    const uint32_t bars = x_ring + S * p.b_bytes;
+    auto fullx = [&](int s) { return bars + 8u * s; };             // x tile landed (TMA transaction count)
+    auto fulla = [&](int s) { return bars + 8u * (kMaxStages + s); };        // A tile expanded (8 warps)
+    auto empty = [&](int s) { return bars + 8u * (2 * kMaxStages + s); };    // both consumed (MMA commit)
+    const uint32_t done = bars + 8u * (3 * kMaxStages);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int rt = blockIdx.x, split = blockIdx.y;
     const int kt0 = split * p.kt_per_split;
     const int kt1 = min(p.col_tiles, kt0 + p.kt_per_split);
     const int nk = kt1 - kt0;                                      // column tiles of this CTA
-    const int ns = (nk + G - 1) / G;                               // pipeline stages, G column tiles each
     const int64_t seg0 = (int64_t)rt * p.col_tiles + kt0;
     for (int j = threadIdx.x; j <= nk; j += blockDim.x) s_offs[j] = p.seg[seg0 + j];
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < S1; ++s) {
-            mbar_init(full1(s), 1);
-            mbar_init(empty1(s), 1);
-        }
-        for (int s = 0; s < kS2; ++s) {
-            mbar_init(full2(s), kGroupWarps);
-            mbar_init(empty2(s), 1);
+        for (int s = 0; s < S; ++s) {
+            mbar_init(fullx(s), 1);
+            mbar_init(fulla(s), kGroupWarps);
+            mbar_init(empty(s), 1);
         }
         mbar_init(done, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -234,27 +249,20 @@ __global__ void __launch_bounds__(kTcThreads, 1) spmm_tc_kernel(const __grid_con
     const uint32_t tmem = s_tmem;
 
     if (warp == kProducerWarp) {
-        // One producer lane per ring-1 slot: lane s fills slot s for stages s, s + S1, ..., so the slots' waits and
-        // copy issues run side by side. A stage is G column tiles: G x tiles by TMA and one bulk copy of their G
-        // segments, which lie back to back in HBM.
+        // The x tiles (the B operand), one producer lane per slot so the slots' waits and TMA issues run side by side.
         if (lane == 0) asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmap_x)) : "memory");
-        if (lane < S1) {
+        if (lane < S) {
             const int s = lane;
             uint32_t ph = 0;
-            for (int j = lane; j < ns; j += S1) {
-                if (j >= S1) {
-                    mbar_wait(empty1(s), ph, 1);
+            for (int i = lane; i < nk; i += S) {
+                if (i >= S) {
+                    mbar_wait(empty(s), ph, 1);
                     ph ^= 1u;
                 }
-                const int c0 = j * G, cn = min(G, nk - c0);
-                const int64_t w0 = s_offs[c0], w1 = s_offs[c0 + cn];
-                const uint32_t seg_bytes = (uint32_t)((w1 - w0) * 4);
-                mbar_expect_tx(full1(s), (uint32_t)(cn * p.b_bytes) + seg_bytes);
-                for (int h = 0; h < cn; ++h)
-                    for (int b = 0; b < p.n_boxes; ++b)
-                        tma_load_2d(b_ring + s * b_stage + h * p.b_bytes + b * p.box_rows * 128, &tmap_x,
-                                    (kt0 + c0 + h) * tc::kTileCols, b * p.box_rows, full1(s));
-                if (seg_bytes) bulk_load(seg_ring + s * p.seg_cap, p.words + w0, seg_bytes, full1(s));
+                mbar_expect_tx(fullx(s), (uint32_t)p.b_bytes);
+                for (int b = 0; b < p.n_boxes; ++b)
+                    tma_load_2d(x_ring + s * p.b_bytes + b * p.box_rows * 128, &tmap_x, (kt0 + i) * tc::kTileCols,
+                                b * p.box_rows, fullx(s));
             }
         }
         __syncwarp();
@@ -262,77 +270,78 @@ __global__ void __launch_bounds__(kTcThreads, 1) spmm_tc_kernel(const __grid_con
         if (lane == 0) {
             const uint32_t id0 = idesc_f16<T>(p.n_total <= 256 ? p.n_total : 256);
             const uint32_t id1 = idesc_f16<T>(p.n_total > 256 ? p.n_total - 256 : 16);
-            int s1 = 0, s2 = 0;
-            uint32_t ph1 = 0, ph2 = 0;
-            for (int j = 0; j < ns; ++j) {
-                mbar_wait(full2(s2), ph2, 2);
-                mbar_wait(full1(s1), ph1, 3);
+            int s = 0;
+            uint32_t ph = 0;
+            for (int i = 0; i < nk; ++i) {
+                mbar_wait(fulla(s), ph, 2);
+                mbar_wait(fullx(s), ph, 3);
                 tc_fence_after();
-                const int cn = min(G, nk - j * G);
-                uint64_t a_desc = sw128_desc(a_ring + s2 * a_stage);
-                uint64_t b_desc = sw128_desc(b_ring + s1 * b_stage);
-                for (int h = 0; h < cn; ++h) {
+                const uint64_t a_desc = sw128_desc(a_ring + s * kASlotBytes);
+                const uint64_t b_desc = sw128_desc(x_ring + s * p.b_bytes);
 #pragma unroll
-                    for (int k = 0; k < tc::kTileCols / 16; ++k) {
-                        const uint32_t acc = (j > 0 || h > 0 || k > 0) ? 1u : 0u;
-                        umma_f16(tmem, a_desc + 2 * k, b_desc + 2 * k, id0, acc);     // +32 bytes a K step of 16
-                        if (p.n_total > 256)
-                            umma_f16(tmem + 256, a_desc + 2 * k, b_desc + (uint64_t)((256 * 128) >> 4) + 2 * k, id1,
-                                     acc);
-                    }
-                    a_desc += kATileBytes >> 4;
-                    b_desc += (uint32_t)p.b_bytes >> 4;
+                for (int k = 0; k < tc::kTileCols / 16; ++k) {
+                    const uint32_t acc = (i > 0 || k > 0) ? 1u : 0u;
+                    umma_f16(tmem, a_desc + 2 * k, b_desc + 2 * k, id0, acc);     // +32 bytes a K step of 16
+                    if (p.n_total > 256)
+                        umma_f16(tmem + 256, a_desc + 2 * k, b_desc + (uint64_t)((256 * 128) >> 4) + 2 * k, id1, acc);
                 }
-                umma_commit(empty2(s2));
-                umma_commit(empty1(s1));
-                advance(s1, ph1, 1, S1);
-                advance(s2, ph2, 1, kS2);
+                umma_commit(empty(s));                  // frees the slot's A tile and x tile at once
+                advance(s, ph, 1, S);
             }
             umma_commit(done);
         }
         __syncwarp();
     } else {
-        // Expanders: group `grp` builds the dense 128 x 64 tiles of every other stage in shared memory; warp `wg` of
-        // the group owns rows 16 wg .. 16 wg + 15 of each (8-row groups 2 wg and 2 wg + 1 of a segment's header).
+        // Expanders: group `grp` builds the dense 128 x 64 tiles of every other column tile in shared memory. Each of
+        // its warps zeroes 16 rows of the tile, the group meets at a named barrier, and each warp writes its piece of
+        // the segment's words at the offsets they carry. The words come straight from HBM into registers, three of
+        // the group's tiles ahead (a ring of four register buffers), never through shared memory.
         const int grp = warp / kGroupWarps, wg = warp % kGroupWarps;
-        int s1 = grp % S1, s2 = grp % kS2;
-        uint32_t ph1 = 0, ph2 = 0;
-        for (int j = grp; j < ns; j += kGroups, advance(s1, ph1, kGroups, S1), advance(s2, ph2, kGroups, kS2)) {
-            if (lane == 0) {
-                mbar_wait(full1(s1), ph1, 4);
-                if (j >= kS2) mbar_wait(empty2(s2), ph2 ^ 1u, 5);
+        int s = grp % S;
+        uint32_t ph = 0;
+        uint32_t b0[kPrefetch], b1[kPrefetch], b2[kPrefetch], b3[kPrefetch];
+        int64_t l0 = 0, h0 = 0, l1 = 0, h1 = 0, l2 = 0, h2 = 0, l3 = 0, h3 = 0;
+        auto fetch = [&](int i, uint32_t (&b)[kPrefetch], int64_t& lo, int64_t& hi) {
+            if (i < nk) {
+                warp_piece(s_offs, i, wg, lo, hi);
+                load_piece(p.words, lo, hi, lane, b);
             }
+        };
+        auto expand = [&](int i, const uint32_t (&cur)[kPrefetch], int64_t lo, int64_t hi) {
+            if (lane == 0 && i >= S) mbar_wait(empty(s), ph ^ 1u, 5);
             __syncwarp();
-            const int c0 = j * G, cn = min(G, nk - c0);
-            const int64_t w0 = s_offs[c0];
-            const uint8_t* slot = gbase + (seg_ring - base) + (size_t)s1 * p.seg_cap;
-            for (int h = 0; h < cn; ++h) {
-                const uint32_t* sg = reinterpret_cast<const uint32_t*>(slot) + (s_offs[c0 + h] - w0);
-                const uint32_t hw = sg[wg];
-                const uint32_t begin = wg ? (sg[wg - 1] >> 16) : 0u, end = hw >> 16;
-                const uint32_t a_off = s2 * a_stage + h * kATileBytes;
-                uint4* rows16 = reinterpret_cast<uint4*>(gbase + a_off + wg * 2048);
+            const uint32_t a_s = a_ring + s * kASlotBytes;
+            uint4* rows16 = reinterpret_cast<uint4*>(gbase + (size_t)s * kASlotBytes + wg * 2048);
 #pragma unroll
-                for (int q = 0; q < 4; ++q) rows16[lane + 32 * q] = make_uint4(0, 0, 0, 0);
-                __syncwarp();
-                const uint32_t a_s = a_ring + a_off;
-                const uint32_t* entries = sg + tc::kHeaderWords;
-                uint32_t e = begin + lane;
-                for (; e + 96 < end; e += 128) {            // four words in flight a lane
-                    const uint32_t x0 = entries[e], x1 = entries[e + 32], x2 = entries[e + 64], x3 = entries[e + 96];
-                    sts_u16(a_s + (x0 & 0x3FFEu), x0 >> 16);
-                    sts_u16(a_s + (x1 & 0x3FFEu), x1 >> 16);
-                    sts_u16(a_s + (x2 & 0x3FFEu), x2 >> 16);
-                    sts_u16(a_s + (x3 & 0x3FFEu), x3 >> 16);
-                }
-                for (; e < end; e += 32) {
-                    const uint32_t x0 = entries[e];
-                    sts_u16(a_s + (x0 & 0x3FFEu), x0 >> 16);
-                }
+            for (int q = 0; q < 4; ++q) rows16[lane + 32 * q] = make_uint4(0, 0, 0, 0);
+            asm volatile("bar.sync %0, %1;" ::"r"(1 + grp), "n"(kGroupWarps * 32) : "memory");   // tile zeroed
+#pragma unroll
+            for (int k = 0; k < kPrefetch; ++k) sts_u16(a_s + (cur[k] & kOffsetMask), cur[k] >> 16);
+            for (int64_t e = lo + 32 * kPrefetch + lane; e < hi; e += 32) {          // pieces longer than the registers
+                const uint32_t w = ldg_stream(p.words + e);
+                sts_u16(a_s + (w & kOffsetMask), w >> 16);
             }
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
             __syncwarp();
-            if (lane == 0) mbar_arrive(full2(s2));
+            if (lane == 0) mbar_arrive(fulla(s));
+            advance(s, ph, kGroups, S);
+        };
+        constexpr int G = kGroups;
+        fetch(grp, b0, l0, h0);
+        fetch(grp + G, b1, l1, h1);
+        fetch(grp + 2 * G, b2, l2, h2);
+        for (int i = grp; i < nk; i += 4 * G) {
+            fetch(i + 3 * G, b3, l3, h3);
+            expand(i, b0, l0, h0);
+            if (i + G >= nk) break;
+            fetch(i + 4 * G, b0, l0, h0);
+            expand(i + G, b1, l1, h1);
+            if (i + 2 * G >= nk) break;
+            fetch(i + 5 * G, b1, l1, h1);
+            expand(i + 2 * G, b2, l2, h2);
+            if (i + 3 * G >= nk) break;
+            fetch(i + 6 * G, b2, l2, h2);
+            expand(i + 3 * G, b3, l3, h3);
         }
 
         // Epilogue: D[row, token] out of TMEM. Warp w reads lanes 32 (w % 4) .. + 31, every other 16-column chunk.
@@ -403,7 +412,7 @@ EncodeTiledFn encode_fn() {
 }
 
 struct TcPlan {
-    int n_total, box_rows, n_boxes, tmem_cols, s1, s2, g, b_bytes, seg_cap, n_split, kt_per_split, smem;
+    int n_total, box_rows, n_boxes, tmem_cols, stages, b_bytes, n_split, kt_per_split, smem;
 };
 
 int pow2_at_least(int v) {
@@ -422,7 +431,7 @@ int choose_split(int64_t row_tiles, int col_tiles, int tokens, int sms) {
         const int per = (col_tiles + s - 1) / s;
         if ((s - 1) * per >= col_tiles) continue;                     // an empty split
         const double waves = (double)((row_tiles * s + sms - 1) / sms);
-        double cost = waves * (per + 3.0);                            // + pipeline fill and epilogue
+        double cost = waves * (per + 10.0);         // + a CTA's fixed cost (fill, TMEM, epilogue): ~10 tiles' time
         if (s > 1) cost += (double)s * tokens * row_tiles / 12.0 / sms;
         if (cost < best_cost - 1e-9) {
             best_cost = cost;
@@ -451,9 +460,8 @@ extern "C" size_t p2p_spmm_tc_workspace(int64_t rows, int64_t cols, int64_t toke
     const int64_t row_tiles = (rows + tc::kTileRows - 1) / tc::kTileRows;
     const int col_tiles = (int)((cols + tc::kTileCols - 1) / tc::kTileCols);
     size_t need = 0;
-    // Every token count a launch may take (512 a launch, 256 when a module's segments leave no room for 512).
-    const int chunks[4] = {(int)(tokens < 512 ? tokens : 512), (int)(tokens % 512), (int)(tokens < 256 ? tokens : 256),
-                           (int)(tokens % 256)};
+    // Every token count a launch may take (512 a launch).
+    const int chunks[2] = {(int)(tokens < 512 ? tokens : 512), (int)(tokens % 512)};
     for (int t : chunks) {
         if (t <= 0) continue;
         int n = 1, per = col_tiles;
@@ -488,59 +496,21 @@ extern "C" int p2p_spmm_tc(const void* x, int dtype, int64_t tokens, int64_t col
     const int col_tiles = (int)((cols + tc::kTileCols - 1) / tc::kTileCols);
     const int elem = 2;
 
-    // Tokens a launch: up to 512 (TMEM columns), fewer when two x stages of that many rows and the module's largest
-    // segment do not fit beside two A tiles.
-    int chunk = 512;
-    while (chunk > 16) {
-        const int fixed2 = 1024 + 2 * kATileBytes + 8 * (2 * kMaxS1 + 2 * kMaxS2 + 1) + 64;
-        const int seg_b = (int)((seg_cap_words * 4 + 127) / 128 * 128);
-        if ((kSmemLimit - fixed2) / (chunk * 128 + (seg_b ? seg_b : 128)) >= 2) break;
-        chunk /= 2;
-    }
-    for (int64_t t0 = 0; t0 < tokens; t0 += chunk) {
-        const int tn = (int)(tokens - t0 < chunk ? tokens - t0 : chunk);
+    const int fixed = 1024 + 8 * (3 * kMaxStages + 1) + 64;
+    for (int64_t t0 = 0; t0 < tokens; t0 += 512) {             // at most 512 tokens (TMEM columns) a launch
+        const int tn = (int)(tokens - t0 < 512 ? tokens - t0 : 512);
         TcPlan pl;
         pl.n_total = (tn + 15) / 16 * 16;
         pl.n_boxes = pl.n_total <= 256 ? 1 : 2;
         pl.box_rows = pl.n_total / pl.n_boxes;
         pl.tmem_cols = pow2_at_least(pl.n_total);
         pl.b_bytes = pl.n_total * 128;
-        pl.seg_cap = (int)((seg_cap_words * 4 + 127) / 128 * 128);
-        if (pl.seg_cap == 0) pl.seg_cap = 128;
-        // Column tiles a stage (G): as many as leave three x / segment stages beside two A stages (more work per
-        // synchronisation); four A stages when a stage is a single column tile and they fit.
-        const int seg_one = (int)((seg_cap_words * 4 + 127) / 128 * 128) > 128
-                                ? (int)((seg_cap_words * 4 + 127) / 128 * 128) : 128;
-        int fixed = 0;
-        pl.g = 1;
-        pl.s2 = 2;
-        pl.s1 = 0;
-        for (int g = 4; g >= 1; g >>= 1) {
-            const int s2 = 2;
-            fixed = 1024 + s2 * g * kATileBytes + 8 * (2 * kMaxS1 + 2 * kMaxS2 + 1) + 64;
-            const int s1 = (kSmemLimit - fixed) / (g * pl.b_bytes + g * seg_one);
-            if (s1 >= 3 || g == 1) {
-                pl.g = g;
-                pl.s2 = s2;
-                pl.s1 = s1;
-                break;
-            }
-        }
-        pl.seg_cap = pl.g * seg_one;
-        if (pl.g == 1) {
-            const int fixed4 = 1024 + 4 * kATileBytes + 8 * (2 * kMaxS1 + 2 * kMaxS2 + 1) + 64;
-            const int s1_4 = (kSmemLimit - fixed4) / (pl.b_bytes + pl.seg_cap);
-            if (s1_4 >= 3) {
-                pl.s2 = 4;
-                pl.s1 = s1_4;
-                fixed = fixed4;
-            }
-        }
-        if (pl.s1 > kMaxS1) pl.s1 = kMaxS1;
-        if (pl.s1 < 2)
-            return fail(P2P_EUNSUPPORTED, "p2p_spmm_tc: %d tokens and %d-byte segments exceed shared memory", tn,
-                        seg_one);
-        pl.smem = fixed + pl.s1 * (pl.g * pl.b_bytes + pl.seg_cap);
+        // (A tile, x tile) slots: as many as fit, at most kMaxStages, an even number (the groups alternate).
+        pl.stages = (kSmemLimit - fixed) / (kASlotBytes + pl.b_bytes);
+        if (pl.stages > kMaxStages) pl.stages = kMaxStages;
+        pl.stages &= ~1;
+        if (pl.stages < 2) return fail(P2P_EUNSUPPORTED, "p2p_spmm_tc: %d tokens exceed shared memory", tn);
+        pl.smem = fixed + pl.stages * (kASlotBytes + pl.b_bytes);
         plan_split(row_tiles, col_tiles, tn, sms, &pl.n_split, &pl.kt_per_split);
 
         TcParams prm;
@@ -553,11 +523,8 @@ extern "C" int p2p_spmm_tc(const void* x, int dtype, int64_t tokens, int64_t col
         prm.box_rows = pl.box_rows;
         prm.n_boxes = pl.n_boxes;
         prm.tmem_cols = pl.tmem_cols;
-        prm.s1 = pl.s1;
-        prm.s2 = pl.s2;
-        prm.g = pl.g;
+        prm.stages = pl.stages;
         prm.b_bytes = pl.b_bytes;
-        prm.seg_cap = pl.seg_cap;
         prm.kt_per_split = pl.kt_per_split;
         prm.n_split = pl.n_split;
         prm.y = reinterpret_cast<char*>(y) + t0 * ldy * elem;

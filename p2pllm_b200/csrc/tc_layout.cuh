@@ -11,7 +11,8 @@
 //                   bits 31..16  the value (bf16 or f16 bits)
 //                   bits 13..0   the byte offset of that weight in the 128 x 64 tile as the tensor cores read it:
 //                                row * 128 + ((2 * column) ^ ((row % 8) << 4)), the 128-byte swizzle (always even)
-//                 then filler words (bit 0 set) up to a multiple of 4 words
+//                 then filler words (value 0, offset 16384: just past the tile, into a pad the GEMM keeps there)
+//                 up to a multiple of 4 words
 //
 // A segment starts on a 16-byte boundary and seg[rt * n_ct + ct] holds its first word; seg[n_seg] the total. Per
 // kept weight this is the 2 bytes of the value plus 2 bytes of position, the same 4 bytes as values + int16 column
@@ -26,7 +27,7 @@ constexpr int kTileRows = 128;
 constexpr int kTileCols = 64;
 constexpr int kHeaderWords = 8;
 constexpr int kGroupRows = 8;
-constexpr uint32_t kFillWord = 1u;
+constexpr uint32_t kFillWord = 16384u;
 
 __host__ __device__ __forceinline__ uint32_t swizzled_offset(int row_local, int col_local) {
     return (uint32_t)row_local * 128u + (((uint32_t)col_local * 2u) ^ (((uint32_t)row_local & 7u) << 4));
