@@ -38,3 +38,24 @@ def combine_golden():
 @pytest.fixture(scope="session")
 def expert_golden():
     return golden("expert_case.npz")
+
+
+@pytest.fixture(scope="session")
+def tiles_golden():
+    return golden("tiles_cases.npz")
+
+
+def tiles_blocks(cases: dict, name: str):
+    """The block list (p2p/prepare.py:201-206 form) of a tiles_cases.npz module, as torch tensors on the CPU."""
+    import torch
+    n_blocks, cols = int(cases[name + "_meta"][0]), int(cases[name + "_meta"][1])
+    dt = torch.float16 if name == "b" else torch.bfloat16
+    blocks = []
+    for j in range(n_blocks):
+        if f"{name}_b{j}_dense" in cases:
+            w = torch.from_numpy(cases[f"{name}_b{j}_dense"].view(np.int16).copy()).view(dt)
+            blocks.append(("dense", w))
+        else:
+            v = torch.from_numpy(cases[f"{name}_b{j}_values"].view(np.int16).copy()).view(dt)
+            blocks.append(("sparse", v, torch.from_numpy(cases[f"{name}_b{j}_words"]), cols))
+    return blocks

@@ -155,6 +155,39 @@ def expert_case(wanda) -> dict:
             "gated": gated.numpy()}
 
 
+def tiles_cases(wanda, compact) -> dict:
+    """The reference kernel's layout (p2p.compact.Tiles, p2p/compact.py:124-174) of small modules, built on the CPU with
+    compact.cu's default shape (RT 128, KCOLS 64, WARPS 4); Tiles' timing-based split choice needs the GPU and is left
+    out (it does not change the layout)."""
+    compact._EXT = types.SimpleNamespace(RT=128, KCOLS=64, WARPS=4)
+    compact.Tiles._tune = lambda self: {}
+    cases = {"a": (torch.bfloat16, [("sparse", 300, 36)], 200),
+             "b": (torch.float16, [("dense", 64, 0), ("sparse", 100, 20), ("sparse", 40, 50)], 128),
+             "c": (torch.bfloat16, [("sparse", 130, 90)], 64)}
+    out = {}
+    for name, (dtype, spec, cols) in cases.items():
+        g = torch.Generator().manual_seed(len(name) + ord(name))
+        blocks = []
+        for j, (kind, rows, keep) in enumerate(spec):
+            w = torch.randn(rows, cols, generator=g).to(dtype)
+            if kind == "dense":
+                blocks.append(("dense", w))
+                out[f"{name}_b{j}_dense"] = bits(w)
+                continue
+            pruned, mask = wanda.prune(w, keep, torch.rand(cols, generator=g) + 0.1, with_mask=True)
+            values, words = compact.pack(pruned, mask)
+            blocks.append(("sparse", values, words, cols))
+            out[f"{name}_b{j}_values"] = bits(values)
+            out[f"{name}_b{j}_words"] = words.numpy()
+        t = compact.Tiles(blocks)
+        out[f"{name}_meta"] = np.array([len(spec), cols, t.rows, t.vcap, t.tiles, t.chunks], dtype=np.int64)
+        out[f"{name}_vals"] = bits(t.vals)
+        out[f"{name}_masks"] = t.masks.numpy()
+        out[f"{name}_woff"] = t.woff.numpy()
+    compact._EXT = None
+    return out
+
+
 def main() -> None:
     wanda, compact, replica, route = _reference()
     torch.manual_seed(0)
@@ -162,6 +195,7 @@ def main() -> None:
     np.savez_compressed(os.path.join(HERE, "config1.npz"), **config1_case(wanda, compact))
     np.savez_compressed(os.path.join(HERE, "combine_cases.npz"), **combine_cases(replica, route))
     np.savez_compressed(os.path.join(HERE, "expert_case.npz"), **expert_case(wanda))
+    np.savez_compressed(os.path.join(HERE, "tiles_cases.npz"), **tiles_cases(wanda, compact))
     for f in sorted(os.listdir(HERE)):
         if f.endswith(".npz"):
             print(f, os.path.getsize(os.path.join(HERE, f)))
