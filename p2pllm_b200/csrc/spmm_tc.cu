@@ -33,16 +33,17 @@ constexpr int kGroupWarps = 8;                                     // warps expa
 constexpr int kGroups = 2;                                         // groups taking alternate column tiles
 constexpr int kExpWarps = kGroupWarps * kGroups;
 constexpr int kProducerWarp = kExpWarps;
-constexpr int kMmaWarp = kExpWarps + 1;
-constexpr int kTcThreads = kExpWarps * 32 + 64;
+constexpr int kMmaWarp = kExpWarps + 1;                           // and kMmaWarp + 1: two MMA issuers
+constexpr int kTcThreads = kExpWarps * 32 + 96;
 constexpr int kATileBytes = tc::kTileRows * tc::kTileCols * 2;   // 16 KiB
 constexpr int kASlotBytes = kATileBytes + 1024;                    // + the pad filler words write into; 1 KiB aligned
 constexpr int kMaxStages = 8;                                      // (A tile, x tile) slots in flight (even)
 constexpr int kPrefetch = 14;                                      // segment words a lane holds in registers a tile
 constexpr uint32_t kOffsetMask = 0x7FFEu;
-constexpr int kMaxTilesPerCta = 1024;                              // segment offsets staged in shared memory
-// Dynamic shared memory: the 227 KiB a block may hold, less the static offsets array and a few scalars.
-constexpr int kSmemLimit = 227 * 1024 - (int)sizeof(int64_t) * (kMaxTilesPerCta + 1) - 256;
+constexpr int kMaxTilesPerCta = 256;                               // segment offsets and headers staged in smem
+// Dynamic shared memory: the 227 KiB a block may hold, less the static offsets and headers and a few scalars.
+constexpr int kSmemLimit =
+    227 * 1024 - (int)sizeof(int64_t) * (kMaxTilesPerCta + 1) - tc::kHeaderWords * 4 * kMaxTilesPerCta - 256;
 constexpr uint64_t kWaitNs = 2000000000ull;
 // The workspace: a fixed region of per-row-tile ticket counters, then the fp32 partials; no call's partials can
 // overlap another call's counters, whatever the shapes.
@@ -55,6 +56,7 @@ struct TcParams {
     const uint32_t* words;            // the module's packed words
     const int64_t* seg;               // [row_tiles * col_tiles + 1]
     int rows, col_tiles, tokens, n_total, box_rows, n_boxes, tmem_cols;
+    int acc_stride;                   // TMEM columns between the two issuers' accumulators (n_total <= 256), else 0
     int stages, b_bytes, kt_per_split, n_split;
     void* y;
     int64_t ldy;
@@ -175,14 +177,14 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
     for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
-// A warp's share of one segment's words: [lo, hi) in the module's word array. The segment's words after its header
-// are cut into kGroupWarps contiguous pieces; any piece will do, since every word carries its own place in the tile.
-__device__ __forceinline__ void warp_piece(const int64_t* offs, int i, int wg, int64_t& lo, int64_t& hi) {
-    const int64_t s0 = offs[i], s1 = offs[i + 1];
-    const int64_t body = s1 - s0 - tc::kHeaderWords;
-    const int64_t per = (body + kGroupWarps - 1) / kGroupWarps;
-    lo = s0 + tc::kHeaderWords + (int64_t)wg * per;
-    hi = lo + per < s1 ? lo + per : s1;
+// A warp's share of one segment's words: the entries of its 16 rows (8-row groups 2 wg and 2 wg + 1), [lo, hi) in
+// the module's word array, from the segment's header (cumulative counts of its 8-row groups).
+__device__ __forceinline__ void warp_piece(const int64_t* offs, const uint16_t* hdr, int i, int wg, int64_t& lo,
+                                           int64_t& hi) {
+    const uint16_t* h = hdr + i * 2 * tc::kHeaderWords;
+    const int64_t s0 = offs[i] + tc::kHeaderWords;
+    lo = s0 + (wg ? h[2 * wg - 1] : 0);
+    hi = s0 + h[2 * wg + 1];
 }
 
 __device__ __forceinline__ uint32_t ldg_stream(const uint32_t* p) {
@@ -207,6 +209,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) spmm_tc_kernel(const __grid_con
     __shared__ uint32_t s_tmem;
     __shared__ int s_last;
     __shared__ int64_t s_offs[kMaxTilesPerCta + 1];                // this CTA's segment offsets
+    __shared__ uint32_t s_hdr[kMaxTilesPerCta * tc::kHeaderWords];   // and their headers
     const uint32_t raw = smem_u32(smem_raw);
     const uint32_t base = (raw + 1023u) & ~1023u;
     uint8_t* gbase = smem_raw + (base - raw);
@@ -214,9 +217,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) spmm_tc_kernel(const __grid_con
     const uint32_t a_ring = base;                                  // S slots of kASlotBytes
     const uint32_t x_ring = a_ring + S * kASlotBytes;              // S slots of b_bytes
     const uint32_t bars = x_ring + S * p.b_bytes;
-    auto fullx = [&](int s) { return bars + 8u * s; };             // x tile landed (TMA transaction count)
-    auto fulla = [&](int s) { return bars + 8u * (kMaxStages + s); };        // A tile expanded (8 warps)
-    auto empty = [&](int s) { return bars + 8u * (2 * kMaxStages + s); };    // both consumed (MMA commit)
+    // full(s): the slot's A tile expanded (8 warps arrive) and its x tile landed (the producer's arrive with the TMA
+    // transaction count), one barrier so the MMA thread waits once a tile; empty(s): both consumed (MMA commit).
+    auto full = [&](int s) { return bars + 8u * s; };
+    auto empty = [&](int s) { return bars + 8u * (2 * kMaxStages + s); };
     const uint32_t done = bars + 8u * (3 * kMaxStages);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -226,14 +230,15 @@ __global__ void __launch_bounds__(kTcThreads, 1) spmm_tc_kernel(const __grid_con
     const int nk = kt1 - kt0;                                      // column tiles of this CTA
     const int64_t seg0 = (int64_t)rt * p.col_tiles + kt0;
     for (int j = threadIdx.x; j <= nk; j += blockDim.x) s_offs[j] = p.seg[seg0 + j];
+    for (int j = threadIdx.x; j < nk * tc::kHeaderWords; j += blockDim.x)
+        s_hdr[j] = __ldg(p.words + p.seg[seg0 + j / tc::kHeaderWords] + j % tc::kHeaderWords);
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; ++s) {
-            mbar_init(fullx(s), 1);
-            mbar_init(fulla(s), kGroupWarps);
-            mbar_init(empty(s), 1);
+            mbar_init(full(s), kGroupWarps + 1);
+            mbar_init(empty(s), p.acc_stride ? 1 : 2);
         }
-        mbar_init(done, 1);
+        mbar_init(done, 2);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     }
@@ -259,51 +264,60 @@ __global__ void __launch_bounds__(kTcThreads, 1) spmm_tc_kernel(const __grid_con
                     mbar_wait(empty(s), ph, 1);
                     ph ^= 1u;
                 }
-                mbar_expect_tx(fullx(s), (uint32_t)p.b_bytes);
+                mbar_expect_tx(full(s), (uint32_t)p.b_bytes);
                 for (int b = 0; b < p.n_boxes; ++b)
                     tma_load_2d(x_ring + s * p.b_bytes + b * p.box_rows * 128, &tmap_x, (kt0 + i) * tc::kTileCols,
-                                b * p.box_rows, fullx(s));
+                                b * p.box_rows, full(s));
             }
         }
         __syncwarp();
-    } else if (warp == kMmaWarp) {
+    } else if (warp == kMmaWarp || warp == kMmaWarp + 1) {
+        // Two MMA issuers: one thread's tcgen05.mma stream runs one instruction at a time (about 63 ns each, whatever
+        // N up to 256), while two threads' streams overlap. With N <= 256 issuer j takes the tiles of expander group j
+        // into its own accumulator (the epilogue adds the two); with N > 256 both take every tile, issuer 0 the first
+        // n0 token columns and issuer 1 the rest, into one accumulator.
+        const int j = warp - kMmaWarp;
         if (lane == 0) {
-            const uint32_t id0 = idesc_f16<T>(p.n_total <= 256 ? p.n_total : 256);
-            const uint32_t id1 = idesc_f16<T>(p.n_total > 256 ? p.n_total - 256 : 16);
-            int s = 0;
-            uint32_t ph = 0;
-            for (int i = 0; i < nk; ++i) {
-                mbar_wait(fulla(s), ph, 2);
-                mbar_wait(fullx(s), ph, 3);
+            const bool by_tile = p.acc_stride != 0;
+            const int n0 = by_tile ? p.n_total : (p.n_total / 2 + 15) / 16 * 16;
+            const int n_mine = by_tile ? p.n_total : (j ? p.n_total - n0 : n0);
+            const uint32_t id = idesc_f16<T>(n_mine);
+            const uint32_t d = tmem + (by_tile ? (uint32_t)(j * p.acc_stride) : (uint32_t)(j * n0));
+            const uint64_t a0 = sw128_desc(a_ring);
+            const uint64_t b0 = sw128_desc(x_ring) + (by_tile ? 0u : (uint64_t)((j * n0 * 128) >> 4));
+            const int step = by_tile ? 2 : 1;
+            int s = by_tile ? j : 0;
+            uint32_t ph = 0, acc = 0;
+            for (int i = by_tile ? j : 0; i < nk; i += step) {
+                mbar_wait(full(s), ph, 2);
                 tc_fence_after();
-                const uint64_t a_desc = sw128_desc(a_ring + s * kASlotBytes);
-                const uint64_t b_desc = sw128_desc(x_ring + s * p.b_bytes);
+                const uint64_t a_desc = a0 + (uint64_t)((s * kASlotBytes) >> 4);
+                const uint64_t b_desc = b0 + (uint64_t)((s * p.b_bytes) >> 4);
 #pragma unroll
-                for (int k = 0; k < tc::kTileCols / 16; ++k) {
-                    const uint32_t acc = (i > 0 || k > 0) ? 1u : 0u;
-                    umma_f16(tmem, a_desc + 2 * k, b_desc + 2 * k, id0, acc);     // +32 bytes a K step of 16
-                    if (p.n_total > 256)
-                        umma_f16(tmem + 256, a_desc + 2 * k, b_desc + (uint64_t)((256 * 128) >> 4) + 2 * k, id1, acc);
-                }
-                umma_commit(empty(s));                  // frees the slot's A tile and x tile at once
-                advance(s, ph, 1, S);
+                for (int k = 0; k < tc::kTileCols / 16; ++k)
+                    umma_f16(d, a_desc + 2 * k, b_desc + 2 * k, id, acc | k);     // +32 bytes a K step of 16
+                acc = 1u;
+                umma_commit(empty(s));                  // frees the slot's A tile and x tile (with the other issuer)
+                advance(s, ph, step, S);
             }
             umma_commit(done);
         }
         __syncwarp();
     } else {
-        // Expanders: group `grp` builds the dense 128 x 64 tiles of every other column tile in shared memory. Each of
-        // its warps zeroes 16 rows of the tile, the group meets at a named barrier, and each warp writes its piece of
-        // the segment's words at the offsets they carry. The words come straight from HBM into registers, three of
-        // the group's tiles ahead (a ring of four register buffers), never through shared memory.
+        // Expanders: group `grp` builds the dense 128 x 64 tiles of every other column tile in shared memory. Warp wg
+        // owns rows 16 wg .. 16 wg + 15 of the tile: it zeroes them and writes their entries at the offsets the words
+        // carry, apart from the other warps (no barrier between them), then arrives on the slot's barrier. The words
+        // come straight from HBM into registers, three of the group's tiles ahead (a ring of four register buffers),
+        // never through shared memory.
         const int grp = warp / kGroupWarps, wg = warp % kGroupWarps;
+        const uint16_t* hdr = reinterpret_cast<const uint16_t*>(s_hdr);
         int s = grp % S;
         uint32_t ph = 0;
         uint32_t b0[kPrefetch], b1[kPrefetch], b2[kPrefetch], b3[kPrefetch];
         int64_t l0 = 0, h0 = 0, l1 = 0, h1 = 0, l2 = 0, h2 = 0, l3 = 0, h3 = 0;
         auto fetch = [&](int i, uint32_t (&b)[kPrefetch], int64_t& lo, int64_t& hi) {
             if (i < nk) {
-                warp_piece(s_offs, i, wg, lo, hi);
+                warp_piece(s_offs, hdr, i, wg, lo, hi);
                 load_piece(p.words, lo, hi, lane, b);
             }
         };
@@ -314,7 +328,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) spmm_tc_kernel(const __grid_con
             uint4* rows16 = reinterpret_cast<uint4*>(gbase + (size_t)s * kASlotBytes + wg * 2048);
 #pragma unroll
             for (int q = 0; q < 4; ++q) rows16[lane + 32 * q] = make_uint4(0, 0, 0, 0);
-            asm volatile("bar.sync %0, %1;" ::"r"(1 + grp), "n"(kGroupWarps * 32) : "memory");   // tile zeroed
+            __syncwarp();                                                    // the warp's rows zeroed
 #pragma unroll
             for (int k = 0; k < kPrefetch; ++k) sts_u16(a_s + (cur[k] & kOffsetMask), cur[k] >> 16);
             for (int64_t e = lo + 32 * kPrefetch + lane; e < hi; e += 32) {          // pieces longer than the registers
@@ -323,7 +337,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) spmm_tc_kernel(const __grid_con
             }
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
             __syncwarp();
-            if (lane == 0) mbar_arrive(fulla(s));
+            if (lane == 0) mbar_arrive(full(s));
             advance(s, ph, kGroups, S);
         };
         constexpr int G = kGroups;
@@ -352,9 +366,17 @@ __global__ void __launch_bounds__(kTcThreads, 1) spmm_tc_kernel(const __grid_con
         const int row_local = quarter * 32 + lane;
         const int64_t row = (int64_t)rt * tc::kTileRows + row_local;
         const bool row_ok = row < p.rows;
+        const bool two = p.acc_stride != 0 && nk > 1;                // issuer 1 took tiles: add its accumulator
         for (int c = cgroup; c < p.n_total / 16; c += kExpWarps / 4) {
             float v[16];
-            tmem_ld16(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(c * 16), v);
+            const uint32_t ta = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(c * 16);
+            tmem_ld16(ta, v);
+            if (two) {
+                float u[16];
+                tmem_ld16(ta + (uint32_t)p.acc_stride, u);
+#pragma unroll
+                for (int q = 0; q < 16; ++q) v[q] += u[q];
+            }
 #pragma unroll
             for (int j = 0; j < 16; ++j) {
                 const int t = c * 16 + j;
@@ -412,7 +434,7 @@ EncodeTiledFn encode_fn() {
 }
 
 struct TcPlan {
-    int n_total, box_rows, n_boxes, tmem_cols, stages, b_bytes, n_split, kt_per_split, smem;
+    int n_total, box_rows, n_boxes, tmem_cols, acc_stride, stages, b_bytes, n_split, kt_per_split, smem;
 };
 
 int pow2_at_least(int v) {
@@ -503,7 +525,10 @@ extern "C" int p2p_spmm_tc(const void* x, int dtype, int64_t tokens, int64_t col
         pl.n_total = (tn + 15) / 16 * 16;
         pl.n_boxes = pl.n_total <= 256 ? 1 : 2;
         pl.box_rows = pl.n_total / pl.n_boxes;
-        pl.tmem_cols = pow2_at_least(pl.n_total);
+        // N <= 256: an accumulator per issuer, side by side; N > 256: one, the issuers splitting its columns.
+        const int acc_cols = pow2_at_least(pl.n_total);
+        pl.acc_stride = pl.n_total <= 256 ? acc_cols : 0;
+        pl.tmem_cols = pl.n_total <= 256 ? 2 * acc_cols : acc_cols;
         pl.b_bytes = pl.n_total * 128;
         // (A tile, x tile) slots: as many as fit, at most kMaxStages, an even number (the groups alternate).
         pl.stages = (kSmemLimit - fixed) / (kASlotBytes + pl.b_bytes);
@@ -523,6 +548,7 @@ extern "C" int p2p_spmm_tc(const void* x, int dtype, int64_t tokens, int64_t col
         prm.box_rows = pl.box_rows;
         prm.n_boxes = pl.n_boxes;
         prm.tmem_cols = pl.tmem_cols;
+        prm.acc_stride = pl.acc_stride;
         prm.stages = pl.stages;
         prm.b_bytes = pl.b_bytes;
         prm.kt_per_split = pl.kt_per_split;

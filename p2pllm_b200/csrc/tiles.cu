@@ -176,6 +176,72 @@ __global__ void __launch_bounds__(kBuildBlock) fill_kernel(Blocks bl, int64_t ro
     }
 }
 
+// Reorders the entries of every 16-row slice of every segment so that 32 consecutive entries spread over the
+// shared-memory banks (the GEMM's expanding warp stores them 32 at a time, and a store takes one pass per entry on its
+// busiest bank). An entry's bank is bits 2..6 of its byte offset. Entries are ranked within their bank in their current
+// order and sorted by (rank, bank): round r holds one entry of every bank with more than r entries, and a 32-entry
+// window meets a bank only as often as the rounds it spans. One warp a slice (16 rows x 64 columns: at most 32 entries
+// a bank, 1024 in all).
+__global__ void __launch_bounds__(256) bank_order_kernel(const int64_t* __restrict__ seg, int64_t n_seg,
+                                                         uint32_t* __restrict__ words) {
+    constexpr int kSliceMax = 16 * tc::kTileCols;
+    __shared__ uint32_t buf[8][kSliceMax];
+    __shared__ uint8_t rk[8][kSliceMax];
+    __shared__ int cnt[8][32];
+    __shared__ uint32_t rmask[8][32];
+    __shared__ int rpre[8][32];
+    const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const unsigned below = (1u << lane) - 1u;
+    for (int64_t sg = blockIdx.x; sg < n_seg; sg += gridDim.x) {
+        const int64_t s0 = seg[sg];
+        auto hdr = [&](int j) { return (int)((words[s0 + j / 2] >> (16 * (j & 1))) & 0xffffu); };
+        const int lo = w ? hdr(2 * w - 1) : 0, hi = hdr(2 * w + 1);
+        const int n = hi - lo;
+        uint32_t* ent = words + s0 + tc::kHeaderWords + lo;
+        cnt[w][lane] = 0;
+        __syncwarp();
+        if (n > 0 && n <= kSliceMax) {
+            for (int j = 0; j < n; j += 32) {
+                const int e = j + lane;
+                const bool ok = e < n;
+                const uint32_t v = ok ? ent[e] : 0u;
+                const int b = ok ? (int)((v >> 2) & 31u) : 32 + lane;   // lanes past the end: a bank of their own
+                const unsigned peers = __match_any_sync(0xffffffffu, b);
+                const int before = __popc(peers & below);
+                if (ok) {
+                    buf[w][e] = v;
+                    rk[w][e] = (uint8_t)(cnt[w][b] + before);
+                }
+                __syncwarp();
+                if (ok && before == 0) cnt[w][b] += __popc(peers);
+                __syncwarp();
+            }
+            // round r: the banks with more than r entries (a mask), and where the round starts
+            const int cb = cnt[w][lane];
+            uint32_t mine = 0;
+            for (int r = 0; r < 32; ++r) {
+                const uint32_t m = __ballot_sync(0xffffffffu, cb > r);
+                if (lane == r) mine = m;
+            }
+            const int nr = __popc(mine);
+            int incl = nr;
+            for (int d = 1; d < 32; d <<= 1) {
+                const int t = __shfl_up_sync(0xffffffffu, incl, d);
+                if (lane >= d) incl += t;
+            }
+            rmask[w][lane] = mine;
+            rpre[w][lane] = incl - nr;
+            __syncwarp();
+            for (int e = lane; e < n; e += 32) {
+                const uint32_t v = buf[w][e];
+                const int b = (int)((v >> 2) & 31u), r = rk[w][e];
+                ent[rpre[w][r] + __popc(rmask[w][r] & ((1u << b) - 1u))] = v;
+            }
+        }
+        __syncwarp();
+    }
+}
+
 int check_blocks(const p2p_row_block* blocks, int nblocks, int idx_bytes, int64_t cols, Blocks& bl, const char* who) {
     if (!blocks || nblocks < 1 || nblocks > kMaxBlocks) return fail(P2P_EINVAL, "%s: 1 to %d row blocks", who, kMaxBlocks);
     if (idx_bytes != 2 && idx_bytes != 4) return fail(P2P_EINVAL, "%s: idx_bytes %d", who, idx_bytes);
@@ -285,6 +351,9 @@ extern "C" int p2p_tiles_fill(const p2p_row_block* blocks, int nblocks, int idx_
             fill_kernel<int32_t><<<grid, kBuildBlock, smem, st>>>(bl, s.rows, (int)s.col_tiles, cnt, seg, words, n_words);
         }
     }
+    if (s.n_seg > 0)
+        bank_order_kernel<<<(unsigned)(s.n_seg < sm_count() * 8 ? s.n_seg : sm_count() * 8), 256, 0, st>>>(seg, s.n_seg,
+                                                                                                     words);
     if (int e = launch_status("p2p_tiles_fill")) return e;
     int bad = 0;
     if (cudaMemcpyFromSymbolAsync(&bad, g_fill_errors, sizeof(int), 0, cudaMemcpyDeviceToHost, st) != cudaSuccess ||

@@ -33,8 +33,9 @@ def _check(got, want, dtype):
 @pytest.mark.parametrize("rows,cols,keep", [(128, 64, 36), (300, 1000, 7), (1024, 4096, 33), (17, 8, 50),
                                             (200, 5120, 90)])
 def test_layout_decodes_to_the_selection(rows, cols, keep):
-    """Every segment: a header of cumulative 8-row-group counts, then one word per kept weight in row order holding
-    its value and its swizzled byte offset in the 128 x 64 tile; decoded, the layout is the selection, bit for bit."""
+    """Every segment: a header of cumulative 8-row-group counts, then one word per kept weight holding its value and
+    its swizzled byte offset in the 128 x 64 tile, 16-row slice after slice, each slice in bank order (sorted by rank
+    within its shared-memory bank, then bank); decoded, the layout is the selection, bit for bit."""
     values, idx = _module(rows, cols, keep)
     words, seg, cap = kernels.tiles_build([(0, values, idx)], cols)
     w = words.cpu().numpy().view(np.uint32)
@@ -54,10 +55,20 @@ def test_layout_decodes_to_the_selection(rows, cols, keep):
         assert (off % 2 == 0).all()
         r = off >> 7
         c = ((((off >> 4) & 7) ^ (r & 7)) << 3) | ((off & 15) >> 1)
-        group = r // 8
+        sl = r // 16
         e = np.arange(count)
-        lo = np.where(group > 0, np.concatenate([[0], hdr])[group], 0)
-        assert ((lo <= e) & (e < hdr[group])).all()
+        bounds = np.concatenate([[0], hdr[1::2]])                   # slice s: [hdr[2s-1], hdr[2s+1])
+        assert ((bounds[sl] <= e) & (e < bounds[sl + 1])).all()
+        bank = (off >> 2) & 31
+        for q in range(8):                                          # bank order: (rank within bank, bank) ascending
+            b = bank[bounds[q]:bounds[q + 1]]
+            seen_b = np.zeros(32, np.int64)
+            rank = np.zeros(len(b), np.int64)
+            for j, x in enumerate(b):
+                rank[j] = seen_b[x]
+                seen_b[x] += 1
+            key = rank * 32 + b
+            assert (np.diff(key) > 0).all()
         np.add.at(seen, (rt * 128 + r, ct * 64 + c), 1)
         got[rt * 128 + r, ct * 64 + c] = (ents >> 16).astype(np.uint16)
     assert cap == int(np.diff(s).max())
