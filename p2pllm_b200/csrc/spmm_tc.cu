@@ -38,7 +38,7 @@ constexpr int kTcThreads = kExpWarps * 32 + 96;
 constexpr int kATileBytes = tc::kTileRows * tc::kTileCols * 2;   // 16 KiB
 constexpr int kASlotBytes = kATileBytes + 1024;                    // + the pad filler words write into; 1 KiB aligned
 constexpr int kMaxStages = 8;                                      // (A tile, x tile) slots in flight (even)
-constexpr int kPrefetch = 14;                                      // segment words a lane holds in registers a tile
+constexpr int kChunks = 4;                                         // 16-byte loads a lane holds for one tile
 constexpr uint32_t kOffsetMask = 0x7FFEu;
 constexpr int kMaxTilesPerCta = 256;                               // segment offsets and headers staged in smem
 // Dynamic shared memory: the 227 KiB a block may hold, less the static offsets and headers and a few scalars.
@@ -178,11 +178,10 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
 }
 
 // A warp's share of one segment's words: the entries of its 16 rows (8-row groups 2 wg and 2 wg + 1), [lo, hi) in
-// the module's word array, from the segment's header (cumulative counts of its 8-row groups).
-__device__ __forceinline__ void warp_piece(const int64_t* offs, const uint16_t* hdr, int i, int wg, int64_t& lo,
-                                           int64_t& hi) {
+// words from the CTA's first segment, from the segment's header (cumulative counts of its 8-row groups).
+__device__ __forceinline__ void warp_piece(const int64_t* offs, const uint16_t* hdr, int i, int wg, int& lo, int& hi) {
     const uint16_t* h = hdr + i * 2 * tc::kHeaderWords;
-    const int64_t s0 = offs[i] + tc::kHeaderWords;
+    const int s0 = (int)(offs[i] - offs[0]) + tc::kHeaderWords;
     lo = s0 + (wg ? h[2 * wg - 1] : 0);
     hi = s0 + h[2 * wg + 1];
 }
@@ -193,13 +192,23 @@ __device__ __forceinline__ uint32_t ldg_stream(const uint32_t* p) {
     return v;
 }
 
-// The first kPrefetch * 32 words of a warp's piece, one lane every 32nd word (coalesced); filler past the end.
-__device__ __forceinline__ void load_piece(const uint32_t* words, int64_t lo, int64_t hi, int lane,
-                                           uint32_t (&buf)[kPrefetch]) {
+__device__ __forceinline__ uint4 ldg_stream4(const uint32_t* p) {
+    uint4 v;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p));
+    return v;
+}
+
+// A warp's slice [lo, hi) in 16-byte loads from its 4-word-aligned base A = lo & ~3: load c of lane l holds words
+// A + 4 (l + 32 c) .. + 3 (coalesced, and inside the segment, which ends on a 16-byte boundary). Words outside the
+// slice are masked when stored; loads wholly past the slice are skipped.
+__device__ __forceinline__ void load_piece(const uint32_t* words, int lo, int hi, int lane, uint4 (&buf)[kChunks]) {
+    const int a0 = lo & ~3;
 #pragma unroll
-    for (int k = 0; k < kPrefetch; ++k) {
-        const int64_t e = lo + lane + 32 * k;
-        buf[k] = e < hi ? ldg_stream(words + e) : tc::kFillWord;
+    for (int c = 0; c < kChunks; ++c) {
+        const int a = a0 + 4 * (lane + 32 * c);
+        buf[c] = a < hi ? ldg_stream4(words + a) : make_uint4(tc::kFillWord, tc::kFillWord, tc::kFillWord, tc::kFillWord);
     }
 }
 
@@ -307,21 +316,22 @@ __global__ void __launch_bounds__(kTcThreads, 1) spmm_tc_kernel(const __grid_con
         // Expanders: group `grp` builds the dense 128 x 64 tiles of every other column tile in shared memory. Warp wg
         // owns rows 16 wg .. 16 wg + 15 of the tile: it zeroes them and writes their entries at the offsets the words
         // carry, apart from the other warps (no barrier between them), then arrives on the slot's barrier. The words
-        // come straight from HBM into registers, three of the group's tiles ahead (a ring of four register buffers),
-        // never through shared memory.
+        // come straight from HBM into registers in 16-byte loads, two of the group's tiles ahead (a ring of three
+        // register buffers), never through shared memory.
         const int grp = warp / kGroupWarps, wg = warp % kGroupWarps;
         const uint16_t* hdr = reinterpret_cast<const uint16_t*>(s_hdr);
         int s = grp % S;
         uint32_t ph = 0;
-        uint32_t b0[kPrefetch], b1[kPrefetch], b2[kPrefetch], b3[kPrefetch];
-        int64_t l0 = 0, h0 = 0, l1 = 0, h1 = 0, l2 = 0, h2 = 0, l3 = 0, h3 = 0;
-        auto fetch = [&](int i, uint32_t (&b)[kPrefetch], int64_t& lo, int64_t& hi) {
+        const uint32_t* wbase = p.words + s_offs[0];        // 16-byte aligned: segments start on 4-word boundaries
+        uint4 b0[kChunks], b1[kChunks], b2[kChunks];
+        int l0 = 0, h0 = 0, l1 = 0, h1 = 0, l2 = 0, h2 = 0;
+        auto fetch = [&](int i, uint4 (&b)[kChunks], int& lo, int& hi) {
             if (i < nk) {
                 warp_piece(s_offs, hdr, i, wg, lo, hi);
-                load_piece(p.words, lo, hi, lane, b);
+                load_piece(wbase, lo, hi, lane, b);
             }
         };
-        auto expand = [&](int i, const uint32_t (&cur)[kPrefetch], int64_t lo, int64_t hi) {
+        auto expand = [&](int i, const uint4 (&cur)[kChunks], int lo, int hi) {
             if (lane == 0 && i >= S) mbar_wait(empty(s), ph ^ 1u, 5);
             __syncwarp();
             const uint32_t a_s = a_ring + s * kASlotBytes;
@@ -329,10 +339,21 @@ __global__ void __launch_bounds__(kTcThreads, 1) spmm_tc_kernel(const __grid_con
 #pragma unroll
             for (int q = 0; q < 4; ++q) rows16[lane + 32 * q] = make_uint4(0, 0, 0, 0);
             __syncwarp();                                                    // the warp's rows zeroed
+            const int a0 = lo & ~3;
+            const int lo_rel = lo - a0, hi_rel = hi - a0;
 #pragma unroll
-            for (int k = 0; k < kPrefetch; ++k) sts_u16(a_s + (cur[k] & kOffsetMask), cur[k] >> 16);
-            for (int64_t e = lo + 32 * kPrefetch + lane; e < hi; e += 32) {          // pieces longer than the registers
-                const uint32_t w = ldg_stream(p.words + e);
+            for (int c = 0; c < kChunks; ++c) {
+                if (128 * c >= hi_rel) break;                                 // the rest of the loads are filler
+                const uint32_t wv[4] = {cur[c].x, cur[c].y, cur[c].z, cur[c].w};
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const int pr = 4 * (lane + 32 * c) + j;
+                    const uint32_t w = (pr >= lo_rel && pr < hi_rel) ? wv[j] : tc::kFillWord;
+                    sts_u16(a_s + (w & kOffsetMask), w >> 16);
+                }
+            }
+            for (int e = a0 + 128 * kChunks + lane; e < hi; e += 32) {          // slices longer than the registers
+                const uint32_t w = ldg_stream(wbase + e);
                 sts_u16(a_s + (w & kOffsetMask), w >> 16);
             }
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -343,19 +364,15 @@ __global__ void __launch_bounds__(kTcThreads, 1) spmm_tc_kernel(const __grid_con
         constexpr int G = kGroups;
         fetch(grp, b0, l0, h0);
         fetch(grp + G, b1, l1, h1);
-        fetch(grp + 2 * G, b2, l2, h2);
-        for (int i = grp; i < nk; i += 4 * G) {
-            fetch(i + 3 * G, b3, l3, h3);
+        for (int i = grp; i < nk; i += 3 * G) {
+            fetch(i + 2 * G, b2, l2, h2);
             expand(i, b0, l0, h0);
             if (i + G >= nk) break;
-            fetch(i + 4 * G, b0, l0, h0);
+            fetch(i + 3 * G, b0, l0, h0);
             expand(i + G, b1, l1, h1);
             if (i + 2 * G >= nk) break;
-            fetch(i + 5 * G, b1, l1, h1);
+            fetch(i + 4 * G, b1, l1, h1);
             expand(i + 2 * G, b2, l2, h2);
-            if (i + 3 * G >= nk) break;
-            fetch(i + 6 * G, b2, l2, h2);
-            expand(i + 3 * G, b3, l3, h3);
         }
 
         // Epilogue: D[row, token] out of TMEM. Warp w reads lanes 32 (w % 4) .. + 31, every other 16-column chunk.
@@ -503,6 +520,7 @@ extern "C" int p2p_spmm_tc(const void* x, int dtype, int64_t tokens, int64_t col
     if (dtype != P2P_BF16 && dtype != P2P_F16)
         return fail(P2P_EUNSUPPORTED, "p2p_spmm_tc: bf16 or f16 (fp32 weights take p2p_spmm_rows)");
     P2P_REQUIRE(x && words && seg && y, "p2p_spmm_tc: null pointer");
+    P2P_REQUIRE(aligned16(words), "p2p_spmm_tc: words must start on a 16-byte boundary");
     P2P_REQUIRE(cols % 8 == 0 && ldx % 8 == 0 && ldx >= cols && aligned16(x),
                 "p2p_spmm_tc: x needs 16-byte aligned rows (cols and ldx multiples of 8)");
     P2P_REQUIRE(ldy >= rows, "p2p_spmm_tc: ldy %lld below rows %lld", (long long)ldy, (long long)rows);

@@ -7,11 +7,11 @@
 //   words 0..7    header: 16 uint16 (two a word, low half first); header[j] = entries in the segment's rows
 //                 0 .. 8j + 7, so 16-row slice s owns entries [header[2s-1], header[2s+1]) (header[-1] = 0) and
 //                 header[15] is the segment's entry count
-//   words 8..     one word per kept weight, slice after slice. Within a slice the entries are in bank order:
-//                 sorted by (rank among the slice's entries in the same shared-memory bank, bank), bank = bits 2..6
-//                 of the offset: round r holds one entry of each bank with more than r entries, so 32 consecutive
-//                 entries, stored at once, meet each bank only as often as the rounds they span (about 40% fewer
-//                 shared-memory wavefronts than row order at keep 36). Each word:
+//   words 8..     one word per kept weight, slice after slice. Within a slice the order is free (every word
+//                 carries its place); the builder deals the entries, in (rank within their shared-memory bank, bank)
+//                 order, to the GEMM's store rounds (tiles.cu, bank_order_kernel), so the 32 entries one store writes
+//                 mostly differ in bank (about 40% fewer shared-memory wavefronts than row order at keep 36). Each
+//                 word:
 //                   bits 31..16  the value (bf16 or f16 bits)
 //                   bits 13..0   the byte offset of that weight in the 128 x 64 tile as the tensor cores read it:
 //                                row * 128 + ((2 * column) ^ ((row % 8) << 4)), the 128-byte swizzle (always even)

@@ -176,35 +176,62 @@ __global__ void __launch_bounds__(kBuildBlock) fill_kernel(Blocks bl, int64_t ro
     }
 }
 
-// Reorders the entries of every 16-row slice of every segment so that 32 consecutive entries spread over the
-// shared-memory banks (the GEMM's expanding warp stores them 32 at a time, and a store takes one pass per entry on its
-// busiest bank). An entry's bank is bits 2..6 of its byte offset. Entries are ranked within their bank in their current
-// order and sorted by (rank, bank): round r holds one entry of every bank with more than r entries, and a 32-entry
-// window meets a bank only as often as the rounds it spans. One warp a slice (16 rows x 64 columns: at most 32 entries
-// a bank, 1024 in all).
-__global__ void __launch_bounds__(256) bank_order_kernel(const int64_t* __restrict__ seg, int64_t n_seg,
-                                                         uint32_t* __restrict__ words) {
-    constexpr int kSliceMax = 16 * tc::kTileCols;
-    __shared__ uint32_t buf[8][kSliceMax];
-    __shared__ uint8_t rk[8][kSliceMax];
-    __shared__ int cnt[8][32];
-    __shared__ uint32_t rmask[8][32];
-    __shared__ int rpre[8][32];
+// Reorders the entries of every 16-row slice of every segment for the GEMM's stores. The GEMM's warp loads its slice
+// in 16-byte pieces from the 4-word boundary A at or below the slice's start: lane l's load c holds words
+// A + 4 (l + 32 c) .. + 3, and store round 4 c + j writes word j of every lane's load c (rounds 0..15, the first 512
+// words from A); past those, round 16 + m stores words A + 512 + 32 m + l. A store takes one pass per entry on its
+// busiest shared-memory bank (bits 2..6 of the entry's byte offset), so the entries of one round should differ in
+// bank. Entries are ranked within their bank (in their current order), put in (rank, bank) order -- bank round r holds
+// one entry of every bank with more than r entries -- and dealt in that order to the store rounds' positions, round
+// by round, lane by lane. One warp a slice (16 rows x 64 columns: at most 32 entries a bank, 1024 in all).
+constexpr int kOrderWarps = 4;
+constexpr int kSliceMax = 16 * tc::kTileCols;
+constexpr int kStoreRounds = 16 + (kSliceMax + 3 - 512 + 31) / 32;   // rounds over the slice's words from A
+
+__device__ __forceinline__ int ceil_div4(int x) { return (x + 3) >> 2; }   // arithmetic shift: negative x too
+
+// The store round of word A + pr, and its lane.
+__device__ __forceinline__ void store_round(int pr, int& round, int& lane) {
+    if (pr < 512) {
+        round = (pr >> 7) * 4 + (pr & 3);
+        lane = (pr & 127) >> 2;
+    } else {
+        round = 16 + ((pr - 512) >> 5);
+        lane = (pr - 512) & 31;
+    }
+}
+
+__global__ void __launch_bounds__(kOrderWarps * 32) bank_order_kernel(const int64_t* __restrict__ seg, int64_t n_seg,
+                                                                      uint32_t* __restrict__ words) {
+    __shared__ uint32_t buf[kOrderWarps][kSliceMax];
+    __shared__ uint32_t byrank[kOrderWarps][kSliceMax];
+    __shared__ uint8_t rk[kOrderWarps][kSliceMax];
+    __shared__ int cnt[kOrderWarps][32];
+    __shared__ uint32_t rmask[kOrderWarps][32];
+    __shared__ int rpre[kOrderWarps][32];
+    __shared__ int llo[kOrderWarps][kStoreRounds + 1];
+    __shared__ int rstart[kOrderWarps][kStoreRounds + 1];
     const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const unsigned below = (1u << lane) - 1u;
-    for (int64_t sg = blockIdx.x; sg < n_seg; sg += gridDim.x) {
+    const int64_t n_work = n_seg * (8 / kOrderWarps);
+    for (int64_t item = blockIdx.x; item < n_work; item += gridDim.x) {
+        const int64_t sg = item / (8 / kOrderWarps);
+        const int slice = (int)(item % (8 / kOrderWarps)) * kOrderWarps + w;
         const int64_t s0 = seg[sg];
         auto hdr = [&](int j) { return (int)((words[s0 + j / 2] >> (16 * (j & 1))) & 0xffffu); };
-        const int lo = w ? hdr(2 * w - 1) : 0, hi = hdr(2 * w + 1);
+        const int lo = slice ? hdr(2 * slice - 1) : 0, hi = hdr(2 * slice + 1);
         const int n = hi - lo;
-        uint32_t* ent = words + s0 + tc::kHeaderWords + lo;
+        const int64_t first = s0 + tc::kHeaderWords + lo;        // the slice's first word
+        const int lo_rel = (int)(first & 3);                      // its place above the 4-word boundary A
+        uint32_t* base = words + (first - lo_rel);                // A
         cnt[w][lane] = 0;
         __syncwarp();
         if (n > 0 && n <= kSliceMax) {
+            // rank of every entry within its bank
             for (int j = 0; j < n; j += 32) {
                 const int e = j + lane;
                 const bool ok = e < n;
-                const uint32_t v = ok ? ent[e] : 0u;
+                const uint32_t v = ok ? base[lo_rel + e] : 0u;
                 const int b = ok ? (int)((v >> 2) & 31u) : 32 + lane;   // lanes past the end: a bank of their own
                 const unsigned peers = __match_any_sync(0xffffffffu, b);
                 const int before = __popc(peers & below);
@@ -216,7 +243,7 @@ __global__ void __launch_bounds__(256) bank_order_kernel(const int64_t* __restri
                 if (ok && before == 0) cnt[w][b] += __popc(peers);
                 __syncwarp();
             }
-            // round r: the banks with more than r entries (a mask), and where the round starts
+            // bank round r: the banks with more than r entries, and where it starts in (rank, bank) order
             const int cb = cnt[w][lane];
             uint32_t mine = 0;
             for (int r = 0; r < 32; ++r) {
@@ -235,7 +262,32 @@ __global__ void __launch_bounds__(256) bank_order_kernel(const int64_t* __restri
             for (int e = lane; e < n; e += 32) {
                 const uint32_t v = buf[w][e];
                 const int b = (int)((v >> 2) & 31u), r = rk[w][e];
-                ent[rpre[w][r] + __popc(rmask[w][r] & ((1u << b) - 1u))] = v;
+                byrank[w][rpre[w][r] + __popc(rmask[w][r] & ((1u << b) - 1u))] = v;
+            }
+            // the store rounds: the lanes [llo, lhi) of round R that fall in the slice, and where R starts
+            if (lane == 0) {
+                int run = 0;
+                for (int R = 0; R < kStoreRounds; ++R) {
+                    int lo_l, hi_l;
+                    if (R < 16) {
+                        const int c = R >> 2, j = R & 3;
+                        lo_l = max(0, ceil_div4(lo_rel - 128 * c - j));
+                        hi_l = min(32, ceil_div4(lo_rel + n - 128 * c - j));
+                    } else {
+                        const int b0 = 512 + 32 * (R - 16);
+                        lo_l = max(0, lo_rel - b0);
+                        hi_l = min(32, lo_rel + n - b0);
+                    }
+                    llo[w][R] = lo_l;
+                    rstart[w][R] = run;
+                    run += hi_l > lo_l ? hi_l - lo_l : 0;
+                }
+            }
+            __syncwarp();
+            for (int pr = lo_rel + lane; pr < lo_rel + n; pr += 32) {
+                int R, l;
+                store_round(pr, R, l);
+                base[pr] = byrank[w][rstart[w][R] + l - llo[w][R]];
             }
         }
         __syncwarp();
@@ -351,9 +403,11 @@ extern "C" int p2p_tiles_fill(const p2p_row_block* blocks, int nblocks, int idx_
             fill_kernel<int32_t><<<grid, kBuildBlock, smem, st>>>(bl, s.rows, (int)s.col_tiles, cnt, seg, words, n_words);
         }
     }
-    if (s.n_seg > 0)
-        bank_order_kernel<<<(unsigned)(s.n_seg < sm_count() * 8 ? s.n_seg : sm_count() * 8), 256, 0, st>>>(seg, s.n_seg,
-                                                                                                     words);
+    if (s.n_seg > 0) {
+        const int64_t items = s.n_seg * (8 / kOrderWarps);
+        bank_order_kernel<<<(unsigned)(items < sm_count() * 8 ? items : sm_count() * 8), kOrderWarps * 32, 0, st>>>(
+            seg, s.n_seg, words);
+    }
     if (int e = launch_status("p2p_tiles_fill")) return e;
     int bad = 0;
     if (cudaMemcpyFromSymbolAsync(&bad, g_fill_errors, sizeof(int), 0, cudaMemcpyDeviceToHost, st) != cudaSuccess ||

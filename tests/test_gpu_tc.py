@@ -34,8 +34,8 @@ def _check(got, want, dtype):
                                             (200, 5120, 90)])
 def test_layout_decodes_to_the_selection(rows, cols, keep):
     """Every segment: a header of cumulative 8-row-group counts, then one word per kept weight holding its value and
-    its swizzled byte offset in the 128 x 64 tile, 16-row slice after slice, each slice in bank order (sorted by rank
-    within its shared-memory bank, then bank); decoded, the layout is the selection, bit for bit."""
+    its swizzled byte offset in the 128 x 64 tile, 16-row slice after slice, each slice dealt to the GEMM's store rounds
+    in bank order (by rank within its shared-memory bank, then bank); decoded, the layout is the selection, bit for bit."""
     values, idx = _module(rows, cols, keep)
     words, seg, cap = kernels.tiles_build([(0, values, idx)], cols)
     w = words.cpu().numpy().view(np.uint32)
@@ -60,8 +60,12 @@ def test_layout_decodes_to_the_selection(rows, cols, keep):
         bounds = np.concatenate([[0], hdr[1::2]])                   # slice s: [hdr[2s-1], hdr[2s+1])
         assert ((bounds[sl] <= e) & (e < bounds[sl + 1])).all()
         bank = (off >> 2) & 31
-        for q in range(8):                                          # bank order: (rank within bank, bank) ascending
-            b = bank[bounds[q]:bounds[q + 1]]
+        for q in range(8):                                          # read in store-round order, (rank, bank) ascends
+            first = s[i] + 8 + bounds[q]
+            pr = np.arange(bounds[q + 1] - bounds[q]) + (first & 3)  # places above the 4-word boundary
+            rnd = np.where(pr < 512, (pr >> 7) * 4 + (pr & 3), 16 + ((pr - 512) >> 5))
+            ln = np.where(pr < 512, (pr & 127) >> 2, (pr - 512) & 31)
+            b = bank[bounds[q]:bounds[q + 1]][np.lexsort((ln, rnd))]
             seen_b = np.zeros(32, np.int64)
             rank = np.zeros(len(b), np.int64)
             for j, x in enumerate(b):
