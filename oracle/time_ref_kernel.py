@@ -7,7 +7,8 @@ The layer is the bench's: Llama-3-8B projections (q, k, v, o keep 33; gate, up, 
 its own public call per module (the reference: Tiles.__call__, p2p/compact.py:195-201, with its timed split choice;
 this library: Compact.apply). A pass over the four modules moves about 310 MB of weights, more than the 126 MB L2, so
 no pass finds the previous one's weights in cache. Each module's time is the median over passes of its CUDA-event
-duration. The two outputs are compared with each other and must agree within the bf16 tolerance (rel-L2 1e-2).
+duration, with the pass queued ahead of the GPU (a spin kernel first) so that host launch cost is not counted on
+either side. The two outputs are compared with each other and must agree within the bf16 tolerance (rel-L2 1e-2).
 
     python -m oracle.time_ref_kernel [--tokens 17 272] [--passes 30]
 """
@@ -22,6 +23,9 @@ import torch
 from oracle import build_ref, ref_tiles
 
 MODULES = {"qkv_proj": ("q", "k", "v"), "o_proj": ("o",), "gate_up_proj": ("gate", "up"), "down_proj": ("down",)}
+# A spin of a few milliseconds queued ahead of each timed pass: the host enqueues the pass's launches while the GPU
+# spins, so each module's events measure the GPU's time for it, not the host's time to issue it.
+HEAD_START_CYCLES = 8_000_000
 
 
 def words_of(idx: torch.Tensor, cols: int) -> torch.Tensor:
@@ -81,6 +85,7 @@ def main() -> None:
                 outs[s, m] = call(m, xs[m])                              # warm-up and the outputs compared below
             for _ in range(args.passes):
                 evs = []
+                torch.cuda._sleep(HEAD_START_CYCLES)           # the GPU waits while the host queues the whole pass
                 for m in lay:
                     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
                     a.record()
