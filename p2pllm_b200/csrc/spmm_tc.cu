@@ -36,10 +36,10 @@ constexpr int kProducerWarp = kExpWarps;
 constexpr int kMmaWarp = kExpWarps + 1;                           // and kMmaWarp + 1: two MMA issuers
 constexpr int kTcThreads = kExpWarps * 32 + 96;
 constexpr int kATileBytes = tc::kTileRows * tc::kTileCols * 2;   // 16 KiB
-constexpr int kASlotBytes = kATileBytes + 1024;                    // + the pad filler words write into; 1 KiB aligned
-constexpr int kMaxStages = 8;                                      // (A tile, x tile) slots in flight (even)
+constexpr int kASlotBytes = kATileBytes;                           // 1 KiB aligned, as the 128-byte swizzle needs
+constexpr int kMaxStages = 12;                                     // (A tile, x tile) slots in flight (even)
 constexpr int kChunks = 4;                                         // 16-byte loads a lane holds for one tile
-constexpr uint32_t kOffsetMask = 0x7FFEu;
+constexpr uint32_t kOffsetMask = 0x3FFEu;                         // an even byte offset inside the 16 KiB tile
 constexpr int kMaxTilesPerCta = 256;                               // segment offsets and headers staged in smem
 // Dynamic shared memory: the 227 KiB a block may hold, less the static offsets and headers and a few scalars.
 constexpr int kSmemLimit =
@@ -348,8 +348,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) spmm_tc_kernel(const __grid_con
 #pragma unroll
                 for (int j = 0; j < 4; ++j) {
                     const int pr = 4 * (lane + 32 * c) + j;
-                    const uint32_t w = (pr >= lo_rel && pr < hi_rel) ? wv[j] : tc::kFillWord;
-                    sts_u16(a_s + (w & kOffsetMask), w >> 16);
+                    if (pr >= lo_rel && pr < hi_rel) sts_u16(a_s + (wv[j] & kOffsetMask), wv[j] >> 16);
                 }
             }
             for (int e = a0 + 128 * kChunks + lane; e < hi; e += 32) {          // slices longer than the registers

@@ -15,8 +15,8 @@
 //                   bits 31..16  the value (bf16 or f16 bits)
 //                   bits 13..0   the byte offset of that weight in the 128 x 64 tile as the tensor cores read it:
 //                                row * 128 + ((2 * column) ^ ((row % 8) << 4)), the 128-byte swizzle (always even)
-//                 then filler words (value 0, offset 16384: just past the tile, into a pad the GEMM keeps there)
-//                 up to a multiple of 4 words
+//                 then filler words (value 0, offset 16384: past the tile) up to a multiple of 4 words; they lie
+//                 outside every slice, and the GEMM never stores them
 //
 // A segment starts on a 16-byte boundary and seg[rt * n_ct + ct] holds its first word; seg[n_seg] the total. Per
 // kept weight this is the 2 bytes of the value plus 2 bytes of position, the same 4 bytes as values + int16 column
