@@ -59,3 +59,50 @@ def tiles_blocks(cases: dict, name: str):
             v = torch.from_numpy(cases[f"{name}_b{j}_values"].view(np.int16).copy()).view(dt)
             blocks.append(("sparse", v, torch.from_numpy(cases[f"{name}_b{j}_words"]), cols))
     return blocks
+
+
+# --- replica files: the small fake layer of tests/golden/make_golden.py (replica_case), rebuilt from its weights ------
+
+REPLICA_KEEP = {"q": 33, "k": 40, "v": 100, "o": 33, "gate": 36, "up": 95, "down": 36}
+REPLICA_SIZES = {"self_attn.qkv_proj": ((64, 16, 16), 64), "self_attn.o_proj": ((64,), 64),
+                 "mlp.gate_up_proj": ((128, 128), 64), "mlp.down_proj": ((64,), 128)}
+
+
+def _fake_linear(sizes, w):
+    import torch
+
+    class Linear(torch.nn.Module):
+        """A linear module with the attributes SGLang's fused linear layers carry; runs its quant_method once a replica
+        is installed, as SGLang's layers do (p2p/compact.py:205-218)."""
+
+        def __init__(self):
+            super().__init__()
+            self.output_sizes, self.output_partition_sizes = list(sizes), list(sizes)
+            self.output_size, self.input_size = sum(sizes), w.shape[1]
+            self.weight = torch.nn.Parameter(w, requires_grad=False)
+
+        def forward(self, x):
+            if hasattr(self, "quant_method"):
+                return self.quant_method.apply(self, x, None)
+            return torch.nn.functional.linear(x, self.weight)
+
+    return Linear()
+
+
+def replica_model(case: dict, device="cpu"):
+    """A one-layer model (model.layers[0]) with the fake layer's weights from replica_case.npz."""
+    import torch
+    layer = torch.nn.Module()
+    layer.self_attn, layer.mlp = torch.nn.Module(), torch.nn.Module()
+    for path, (sizes, cols) in REPLICA_SIZES.items():
+        w = torch.from_numpy(case[f"w:{path}"].view(np.int16).copy()).view(torch.bfloat16).to(device)
+        parent, name = path.split(".")
+        setattr(getattr(layer, parent), name, _fake_linear(sizes, w))
+    model = torch.nn.Module()
+    model.layers = torch.nn.ModuleList([layer])
+    return model
+
+
+@pytest.fixture(scope="session")
+def replica_golden():
+    return golden("replica_case.npz")

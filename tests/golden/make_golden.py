@@ -188,6 +188,52 @@ def tiles_cases(wanda, compact) -> dict:
     return out
 
 
+class _Linear(torch.nn.Module):
+    """A linear module with the attributes SGLang's fused linear layers carry (output_sizes, output_partition_sizes,
+    input_size), which the reference's family.projections reads."""
+
+    def __init__(self, sizes, cols, g, dtype):
+        super().__init__()
+        self.output_sizes, self.output_size, self.input_size = list(sizes), sum(sizes), cols
+        self.output_partition_sizes = list(sizes)                   # one rank holds them all
+        self.weight = torch.nn.Parameter((torch.randn(sum(sizes), cols, generator=g) * 0.02).to(dtype),
+                                         requires_grad=False)
+
+
+def replica_layer(g, dtype=torch.bfloat16, hidden=64, kv=16, inter=128):
+    layer = torch.nn.Module()
+    layer.self_attn, layer.mlp = torch.nn.Module(), torch.nn.Module()
+    layer.self_attn.qkv_proj = _Linear((hidden, kv, kv), hidden, g, dtype)
+    layer.self_attn.o_proj = _Linear((hidden,), hidden, g, dtype)
+    layer.mlp.gate_up_proj = _Linear((inter, inter), hidden, g, dtype)
+    layer.mlp.down_proj = _Linear((hidden,), inter, g, dtype)
+    return layer
+
+
+# Keeps per projection: compact ones, one kept whole (100) and one where compact would save too little (95).
+REPLICA_KEEP = {"q": 33, "k": 40, "v": 100, "o": 33, "gate": 36, "up": 95, "down": 36}
+
+
+def replica_case(out_dir: str) -> dict:
+    """p2p.prepare.write (p2p/prepare.py:42-73) on one small fake layer: the file it writes goes to
+    tests/golden/replica_layer0.safetensors; its inputs (weights, sums, plan) to replica_case.npz."""
+    import shutil
+    import tempfile
+    sys.modules.setdefault("sglang.srt.plugins", types.ModuleType("sglang.srt.plugins"))
+    from p2p import prepare
+    g = torch.Generator().manual_seed(11)
+    layer = replica_layer(g)
+    keys = {"self_attn.qkv_proj": 64, "self_attn.o_proj": 64, "mlp.gate_up_proj": 64, "mlp.down_proj": 128}
+    sums = {(0, k): (torch.rand(c, generator=g, dtype=torch.float64) * 100 + 1) for k, c in keys.items()}
+    plan = {"keep": {"0": dict(REPLICA_KEEP)}}
+    with tempfile.TemporaryDirectory() as tmp:
+        prepare.write([layer], plan, sums, [0], tmp)
+        shutil.copy(os.path.join(tmp, "layer0.safetensors"), os.path.join(out_dir, "replica_layer0.safetensors"))
+    out = {f"w:{path}": bits(m.weight.data) for path, m in layer.named_modules() if hasattr(m, "weight")}
+    out |= {f"sums:{k}": v.numpy() for (_, k), v in sums.items()}
+    return out
+
+
 def main() -> None:
     wanda, compact, replica, route = _reference()
     torch.manual_seed(0)
@@ -196,6 +242,7 @@ def main() -> None:
     np.savez_compressed(os.path.join(HERE, "combine_cases.npz"), **combine_cases(replica, route))
     np.savez_compressed(os.path.join(HERE, "expert_case.npz"), **expert_case(wanda))
     np.savez_compressed(os.path.join(HERE, "tiles_cases.npz"), **tiles_cases(wanda, compact))
+    np.savez_compressed(os.path.join(HERE, "replica_case.npz"), **replica_case(HERE))
     for f in sorted(os.listdir(HERE)):
         if f.endswith(".npz"):
             print(f, os.path.getsize(os.path.join(HERE, f)))

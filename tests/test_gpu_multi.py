@@ -1,0 +1,102 @@
+"""The multi-GPU paths on GPUs: a row-sharded compact module (shard.ShardedCompact, an NCCL all-gather of y) against
+the single-GPU Compact, and the spread-step hop (route.send_piece / recv_parts over NCCL, summed by the GPU kernel in
+member order) against the oracle's sum. One rank per GPU in child processes; the two-rank cases need two GPUs and are
+skipped on one (the world-size-1 case always runs)."""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _module(seed=0, rows=(1024, 256, 256), cols=2048, keep=33):
+    from p2pllm_b200 import wanda
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    norms = torch.rand(cols, generator=g, device="cuda") + 0.1
+    blocks = []
+    for r in rows:
+        w = (torch.randn(r, cols, generator=g, device="cuda") * 0.02).bfloat16()
+        v, i = wanda.select(w, keep, norms)
+        blocks.append(("compact", v, i, cols))
+    x = torch.randn(17, cols, generator=g, device="cuda").bfloat16()
+    return blocks, x
+
+
+def _sharded(rank, world):
+    from p2pllm_b200 import compact, shard
+    blocks, x = _module()
+    y = shard.ShardedCompact(blocks).apply(None, x)
+    want = compact.Compact(blocks).apply(None, x)
+    return float((y.double() - want.double()).abs().max()), tuple(y.shape)
+
+
+def _hop(rank, world):
+    from p2pllm_b200 import route
+    import oracle
+    g = torch.Generator(device="cuda").manual_seed(rank)
+    piece = torch.randn(17, 4096, generator=g, device="cuda").bfloat16()
+    works = route.send_piece(piece, [r for r in range(world) if r != rank])
+    others = route.recv_parts([r for r in range(world) if r != rank], piece)
+    for w in works:
+        w.wait()
+    parts = [piece if r == rank else others.pop(0) for r in range(world)]
+    got = route.summed(parts)
+    bits = lambda t: t.cpu().view(torch.int16).numpy().view(np.uint16)
+    want = oracle.summed([bits(p) for p in parts], "bf16")
+    return bool(np.array_equal(bits(got), want))
+
+
+def _run(rank, world, port, fn, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    import datetime
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    try:
+        q.put((rank, fn(rank, world)))
+    finally:
+        dist.destroy_process_group()
+
+
+def _spawn(fn, world):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_run, args=(r, world, port, fn, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    out = dict(q.get(timeout=300) for _ in procs)
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    return out
+
+
+def test_sharded_module_on_one_gpu_is_the_module():
+    err, shape = _sharded(0, 1)
+    assert err == 0.0 and shape == (17, 1536)
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_sharded_module_over_two_gpus():
+    out = _spawn(_sharded, 2)
+    for rank in range(2):
+        err, shape = out[rank]
+        assert shape == (17, 1536) and err == 0.0        # each row computed by the same kernel on some rank
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_hop_over_nccl_sums_in_member_order():
+    out = _spawn(_hop, 2)
+    assert out[0] and out[1]
