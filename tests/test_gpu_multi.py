@@ -34,11 +34,15 @@ def _module(seed=0, rows=(1024, 256, 256), cols=2048, keep=33):
 
 
 def _sharded(rank, world):
+    """(rel-L2 of the sharded y against the whole module's, y's shape, a hash of y's bits). The shards may split their
+    columns differently from the whole module, so sums can differ in the last bf16 bit."""
+    import hashlib
     from p2pllm_b200 import compact, shard
     blocks, x = _module()
     y = shard.ShardedCompact(blocks).apply(None, x)
-    want = compact.Compact(blocks).apply(None, x)
-    return float((y.double() - want.double()).abs().max()), tuple(y.shape)
+    want = compact.Compact(blocks).apply(None, x).double()
+    rel = float((y.double() - want).norm() / want.norm())
+    return rel, tuple(y.shape), hashlib.sha256(y.cpu().view(torch.int16).numpy().tobytes()).hexdigest()
 
 
 def _hop(rank, world):
@@ -84,16 +88,17 @@ def _spawn(fn, world):
 
 
 def test_sharded_module_on_one_gpu_is_the_module():
-    err, shape = _sharded(0, 1)
-    assert err == 0.0 and shape == (17, 1536)
+    rel, shape, _ = _sharded(0, 1)
+    assert rel == 0.0 and shape == (17, 1536)
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
 def test_sharded_module_over_two_gpus():
     out = _spawn(_sharded, 2)
     for rank in range(2):
-        err, shape = out[rank]
-        assert shape == (17, 1536) and err == 0.0        # each row computed by the same kernel on some rank
+        rel, shape, _ = out[rank]
+        assert shape == (17, 1536) and rel <= 1e-3
+    assert out[0][2] == out[1][2]                       # the all-gather leaves the same y on every rank
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
