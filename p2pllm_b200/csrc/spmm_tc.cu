@@ -37,7 +37,8 @@ constexpr int kMmaWarp = kExpWarps + 1;                           // and kMmaWar
 constexpr int kTcThreads = kExpWarps * 32 + 96;
 constexpr int kATileBytes = tc::kTileRows * tc::kTileCols * 2;   // 16 KiB
 constexpr int kASlotBytes = kATileBytes;                           // 1 KiB aligned, as the 128-byte swizzle needs
-constexpr int kMaxStages = 12;                                     // (A tile, x tile) slots in flight (even)
+constexpr int kMaxASlots = 12;                                     // A tiles in flight (even: the groups alternate)
+constexpr int kMaxXSlots = 4;                                      // x tiles in flight
 constexpr int kChunks = 4;                                         // 16-byte loads a lane holds for one tile
 constexpr uint32_t kOffsetMask = 0x3FFEu;                         // an even byte offset inside the 16 KiB tile
 constexpr int kMaxTilesPerCta = 256;                               // segment offsets and headers staged in smem
@@ -57,7 +58,7 @@ struct TcParams {
     const int64_t* seg;               // [row_tiles * col_tiles + 1]
     int rows, col_tiles, tokens, n_total, box_rows, n_boxes, tmem_cols;
     int acc_stride;                   // TMEM columns between the two issuers' accumulators (n_total <= 256), else 0
-    int stages, b_bytes, kt_per_split, n_split;
+    int a_slots, x_slots, b_bytes, kt_per_split, n_split;
     void* y;
     int64_t ldy;
     float* partial;                   // [n_split, tokens, rows_pad] when n_split > 1
@@ -222,15 +223,19 @@ __global__ void __launch_bounds__(kTcThreads, 1) spmm_tc_kernel(const __grid_con
     const uint32_t raw = smem_u32(smem_raw);
     const uint32_t base = (raw + 1023u) & ~1023u;
     uint8_t* gbase = smem_raw + (base - raw);
-    const int S = p.stages;
-    const uint32_t a_ring = base;                                  // S slots of kASlotBytes
-    const uint32_t x_ring = a_ring + S * kASlotBytes;              // S slots of b_bytes
-    const uint32_t bars = x_ring + S * p.b_bytes;
-    // full(s): the slot's A tile expanded (8 warps arrive) and its x tile landed (the producer's arrive with the TMA
-    // transaction count), one barrier so the MMA thread waits once a tile; empty(s): both consumed (MMA commit).
-    auto full = [&](int s) { return bars + 8u * s; };
-    auto empty = [&](int s) { return bars + 8u * (2 * kMaxStages + s); };
-    const uint32_t done = bars + 8u * (3 * kMaxStages);
+    // Two rings: A tiles (tile i in slot i % SA) and x tiles (tile i in slot i % SX), sized apart so that large x
+    // tiles (many tokens) do not take the A tiles' depth.
+    const int SA = p.a_slots, SX = p.x_slots;
+    const uint32_t a_ring = base;                                  // SA slots of kASlotBytes
+    const uint32_t x_ring = a_ring + SA * kASlotBytes;             // SX slots of b_bytes
+    const uint32_t bars = x_ring + SX * p.b_bytes;
+    // fulla(s): the A tile expanded (8 warps arrive); fullx(s): the x tile landed (the producer's arrive with the TMA
+    // transaction count); emptya / emptyx: consumed (MMA commits).
+    auto fulla = [&](int s) { return bars + 8u * s; };
+    auto emptya = [&](int s) { return bars + 8u * (kMaxASlots + s); };
+    auto fullx = [&](int s) { return bars + 8u * (2 * kMaxASlots + s); };
+    auto emptyx = [&](int s) { return bars + 8u * (2 * kMaxASlots + kMaxXSlots + s); };
+    const uint32_t done = bars + 8u * (2 * kMaxASlots + 2 * kMaxXSlots);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int rt = blockIdx.x, split = blockIdx.y;
@@ -243,9 +248,14 @@ __global__ void __launch_bounds__(kTcThreads, 1) spmm_tc_kernel(const __grid_con
         s_hdr[j] = __ldg(p.words + p.seg[seg0 + j / tc::kHeaderWords] + j % tc::kHeaderWords);
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < S; ++s) {
-            mbar_init(full(s), kGroupWarps + 1);
-            mbar_init(empty(s), p.acc_stride ? 1 : 2);
+        const uint32_t consumers = p.acc_stride ? 1u : 2u;        // issuers that commit a tile's slots
+        for (int s = 0; s < SA; ++s) {
+            mbar_init(fulla(s), kGroupWarps);
+            mbar_init(emptya(s), consumers);
+        }
+        for (int s = 0; s < SX; ++s) {
+            mbar_init(fullx(s), 1);
+            mbar_init(emptyx(s), consumers);
         }
         mbar_init(done, 2);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -265,18 +275,18 @@ __global__ void __launch_bounds__(kTcThreads, 1) spmm_tc_kernel(const __grid_con
     if (warp == kProducerWarp) {
         // The x tiles (the B operand), one producer lane per slot so the slots' waits and TMA issues run side by side.
         if (lane == 0) asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmap_x)) : "memory");
-        if (lane < S) {
+        if (lane < SX) {
             const int s = lane;
             uint32_t ph = 0;
-            for (int i = lane; i < nk; i += S) {
-                if (i >= S) {
-                    mbar_wait(empty(s), ph, 1);
+            for (int i = lane; i < nk; i += SX) {
+                if (i >= SX) {
+                    mbar_wait(emptyx(s), ph, 1);
                     ph ^= 1u;
                 }
-                mbar_expect_tx(full(s), (uint32_t)p.b_bytes);
+                mbar_expect_tx(fullx(s), (uint32_t)p.b_bytes);
                 for (int b = 0; b < p.n_boxes; ++b)
                     tma_load_2d(x_ring + s * p.b_bytes + b * p.box_rows * 128, &tmap_x, (kt0 + i) * tc::kTileCols,
-                                b * p.box_rows, full(s));
+                                b * p.box_rows, fullx(s));
             }
         }
         __syncwarp();
@@ -295,19 +305,22 @@ __global__ void __launch_bounds__(kTcThreads, 1) spmm_tc_kernel(const __grid_con
             const uint64_t a0 = sw128_desc(a_ring);
             const uint64_t b0 = sw128_desc(x_ring) + (by_tile ? 0u : (uint64_t)((j * n0 * 128) >> 4));
             const int step = by_tile ? 2 : 1;
-            int s = by_tile ? j : 0;
-            uint32_t ph = 0, acc = 0;
+            int sa = by_tile ? j : 0, sx = sa;
+            uint32_t pha = 0, phx = 0, acc = 0;
             for (int i = by_tile ? j : 0; i < nk; i += step) {
-                mbar_wait(full(s), ph, 2);
+                mbar_wait(fulla(sa), pha, 2);
+                mbar_wait(fullx(sx), phx, 3);
                 tc_fence_after();
-                const uint64_t a_desc = a0 + (uint64_t)((s * kASlotBytes) >> 4);
-                const uint64_t b_desc = b0 + (uint64_t)((s * p.b_bytes) >> 4);
+                const uint64_t a_desc = a0 + (uint64_t)((sa * kASlotBytes) >> 4);
+                const uint64_t b_desc = b0 + (uint64_t)((sx * p.b_bytes) >> 4);
 #pragma unroll
                 for (int k = 0; k < tc::kTileCols / 16; ++k)
                     umma_f16(d, a_desc + 2 * k, b_desc + 2 * k, id, acc | k);     // +32 bytes a K step of 16
                 acc = 1u;
-                umma_commit(empty(s));                  // frees the slot's A tile and x tile (with the other issuer)
-                advance(s, ph, step, S);
+                umma_commit(emptya(sa));                // frees the A tile and the x tile (with the other issuer)
+                umma_commit(emptyx(sx));
+                advance(sa, pha, step, SA);
+                advance(sx, phx, step, SX);
             }
             umma_commit(done);
         }
@@ -320,7 +333,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) spmm_tc_kernel(const __grid_con
         // register buffers), never through shared memory.
         const int grp = warp / kGroupWarps, wg = warp % kGroupWarps;
         const uint16_t* hdr = reinterpret_cast<const uint16_t*>(s_hdr);
-        int s = grp % S;
+        int s = grp % SA;
         uint32_t ph = 0;
         const uint32_t* wbase = p.words + s_offs[0];        // 16-byte aligned: segments start on 4-word boundaries
         uint4 b0[kChunks], b1[kChunks], b2[kChunks];
@@ -332,7 +345,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) spmm_tc_kernel(const __grid_con
             }
         };
         auto expand = [&](int i, const uint4 (&cur)[kChunks], int lo, int hi) {
-            if (lane == 0 && i >= S) mbar_wait(empty(s), ph ^ 1u, 5);
+            if (lane == 0 && i >= SA) mbar_wait(emptya(s), ph ^ 1u, 5);
             __syncwarp();
             const uint32_t a_s = a_ring + s * kASlotBytes;
             uint4* rows16 = reinterpret_cast<uint4*>(gbase + (size_t)s * kASlotBytes + wg * 2048);
@@ -357,8 +370,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) spmm_tc_kernel(const __grid_con
             }
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
             __syncwarp();
-            if (lane == 0) mbar_arrive(full(s));
-            advance(s, ph, kGroups, S);
+            if (lane == 0) mbar_arrive(fulla(s));
+            advance(s, ph, kGroups, SA);
         };
         constexpr int G = kGroups;
         fetch(grp, b0, l0, h0);
@@ -450,7 +463,7 @@ EncodeTiledFn encode_fn() {
 }
 
 struct TcPlan {
-    int n_total, box_rows, n_boxes, tmem_cols, acc_stride, stages, b_bytes, n_split, kt_per_split, smem;
+    int n_total, box_rows, n_boxes, tmem_cols, acc_stride, a_slots, x_slots, b_bytes, n_split, kt_per_split, smem;
 };
 
 int pow2_at_least(int v) {
@@ -535,7 +548,7 @@ extern "C" int p2p_spmm_tc(const void* x, int dtype, int64_t tokens, int64_t col
     const int col_tiles = (int)((cols + tc::kTileCols - 1) / tc::kTileCols);
     const int elem = 2;
 
-    const int fixed = 1024 + 8 * (3 * kMaxStages + 1) + 64;
+    const int fixed = 1024 + 8 * (2 * kMaxASlots + 2 * kMaxXSlots + 1) + 64;
     for (int64_t t0 = 0; t0 < tokens; t0 += 512) {             // at most 512 tokens (TMEM columns) a launch
         const int tn = (int)(tokens - t0 < 512 ? tokens - t0 : 512);
         TcPlan pl;
@@ -547,12 +560,19 @@ extern "C" int p2p_spmm_tc(const void* x, int dtype, int64_t tokens, int64_t col
         pl.acc_stride = pl.n_total <= 256 ? acc_cols : 0;
         pl.tmem_cols = pl.n_total <= 256 ? 2 * acc_cols : acc_cols;
         pl.b_bytes = pl.n_total * 128;
-        // (A tile, x tile) slots: as many as fit, at most kMaxStages, an even number (the groups alternate).
-        pl.stages = (kSmemLimit - fixed) / (kASlotBytes + pl.b_bytes);
-        if (pl.stages > kMaxStages) pl.stages = kMaxStages;
-        pl.stages &= ~1;
-        if (pl.stages < 2) return fail(P2P_EUNSUPPORTED, "p2p_spmm_tc: %d tokens exceed shared memory", tn);
-        pl.smem = fixed + pl.stages * (kASlotBytes + pl.b_bytes);
+        // Ring depths: x slots first, then as many A slots as the rest holds (even, at most kMaxASlots): the
+        // expanders' latency needs the A depth. When the issuers split the tiles (N <= 256) the x slots are even, so
+        // every use of a slot belongs to the same issuer -- a parity wait cannot then pass on another issuer's
+        // earlier, unfinished use. When both issuers take every tile, three large x slots are enough.
+        const int step_x = pl.acc_stride ? 2 : 1;
+        pl.x_slots = (pl.b_bytes <= 4096 || pl.acc_stride) ? 4 : 3;
+        while (pl.x_slots - step_x >= 2 && kSmemLimit - fixed - pl.x_slots * pl.b_bytes < 2 * kASlotBytes)
+            pl.x_slots -= step_x;
+        pl.a_slots = (kSmemLimit - fixed - pl.x_slots * pl.b_bytes) / kASlotBytes;
+        if (pl.a_slots > kMaxASlots) pl.a_slots = kMaxASlots;
+        pl.a_slots &= ~1;
+        if (pl.a_slots < 2) return fail(P2P_EUNSUPPORTED, "p2p_spmm_tc: %d tokens exceed shared memory", tn);
+        pl.smem = fixed + pl.a_slots * kASlotBytes + pl.x_slots * pl.b_bytes;
         plan_split(row_tiles, col_tiles, tn, sms, &pl.n_split, &pl.kt_per_split);
 
         TcParams prm;
@@ -566,7 +586,8 @@ extern "C" int p2p_spmm_tc(const void* x, int dtype, int64_t tokens, int64_t col
         prm.n_boxes = pl.n_boxes;
         prm.tmem_cols = pl.tmem_cols;
         prm.acc_stride = pl.acc_stride;
-        prm.stages = pl.stages;
+        prm.a_slots = pl.a_slots;
+        prm.x_slots = pl.x_slots;
         prm.b_bytes = pl.b_bytes;
         prm.kt_per_split = pl.kt_per_split;
         prm.n_split = pl.n_split;
