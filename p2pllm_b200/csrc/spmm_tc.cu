@@ -344,14 +344,39 @@ __global__ void __launch_bounds__(kTcThreads, 1) spmm_tc_kernel(const __grid_con
                 load_piece(wbase, lo, hi, lane, b);
             }
         };
-        auto expand = [&](int i, const uint4 (&cur)[kChunks], int lo, int hi) {
-            if (lane == 0 && i >= SA) mbar_wait(emptya(s), ph ^ 1u, 5);
-            __syncwarp();
-            const uint32_t a_s = a_ring + s * kASlotBytes;
-            uint4* rows16 = reinterpret_cast<uint4*>(gbase + (size_t)s * kASlotBytes + wg * 2048);
+        // Zeroing a slot's rows: with three or more slots a group, the group's next slot is zeroed while this tile is
+        // scattered (its last use is two tiles back, long consumed), which takes the zeroing off the warp's chain of
+        // waits; with two, the slot is zeroed just before its own scatter.
+        const bool zero_ahead = SA / kGroups >= 3;
+        auto zero_rows = [&](int slot) {
+            uint4* rows16 = reinterpret_cast<uint4*>(gbase + (size_t)slot * kASlotBytes + wg * 2048);
 #pragma unroll
-            for (int q = 0; q < 4; ++q) rows16[lane + 32 * q] = make_uint4(0, 0, 0, 0);
-            __syncwarp();                                                    // the warp's rows zeroed
+            for (int z = 0; z < 4; ++z) rows16[lane + 32 * z] = make_uint4(0, 0, 0, 0);
+        };
+        if (zero_ahead && grp < nk) {
+            zero_rows(s);                               // the group's first slot: no earlier use to wait for
+            __syncwarp();
+        }
+        auto expand = [&](int i, const uint4 (&cur)[kChunks], int lo, int hi) {
+            if (zero_ahead) {
+                int sn = s + kGroups;
+                uint32_t pn = ph;
+                if (sn >= SA) {
+                    sn -= SA;
+                    pn ^= 1u;
+                }
+                if (i + kGroups < nk) {
+                    if (lane == 0 && i + kGroups >= SA) mbar_wait(emptya(sn), pn ^ 1u, 5);
+                    __syncwarp();
+                    zero_rows(sn);                      // ordered before its scatter by this tile's fence + sync
+                }
+            } else {
+                if (lane == 0 && i >= SA) mbar_wait(emptya(s), ph ^ 1u, 5);
+                __syncwarp();
+                zero_rows(s);
+                __syncwarp();                                                // the warp's rows zeroed
+            }
+            const uint32_t a_s = a_ring + s * kASlotBytes;
             const int a0 = lo & ~3;
             const int lo_rel = lo - a0, hi_rel = hi - a0;
 #pragma unroll
