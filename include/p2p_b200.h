@@ -168,6 +168,19 @@ int p2p_spmm_tc(const void* x, int dtype, int64_t tokens, int64_t cols, int64_t 
                 const int64_t* seg, int64_t rows, int64_t seg_cap_words, void* y, int64_t ldy, void* workspace,
                 size_t workspace_bytes, void* stream);
 
+/* Routed experts in one launch: y [x_rows, ldy] row x_row0 + t = x row x_row0 + t times its expert's matrix, for every
+ * item {first row tile of the expert in the stacked tensor-core layout, x_row0, tokens (1..256), 0} of items
+ * [n_items][4] (device memory, int32, 16-byte aligned). The layout stacks the experts' matrices, each starting on a
+ * 128-row tile (layout_row_tiles row tiles in all, item_row_tiles = ceil(rows / 128) an expert); x holds each
+ * expert's tokens contiguously (sorted by expert); max_tokens bounds every item's tokens. Items that point past the
+ * layout or x are skipped. No workspace: an item takes whole rows.
+ * Replaces p2p/compact.py:241-256 (CompactMoE.apply, which expands every used expert to dense each pass) for the
+ * routed experts' GEMMs. */
+int p2p_spmm_tc_grouped(const void* x, int dtype, int64_t x_rows, int64_t cols, int64_t ldx, const uint32_t* words,
+                        const int64_t* seg, int64_t layout_row_tiles, int64_t rows, int64_t item_row_tiles,
+                        int64_t seg_cap_words, const int32_t* items, int64_t n_items, int64_t max_tokens, void* y,
+                        int64_t ldy, void* stream);
+
 /* P2P_OK unless a p2p_spmm_tc launch since the last reset gave up waiting on its pipeline (then P2P_ECUDA, naming
  * the site); reset != 0 clears the flag. Syncs the stream. */
 int p2p_spmm_tc_status(int reset, void* stream);

@@ -64,6 +64,11 @@ struct TcParams {
     float* partial;                   // [n_split, tokens, rows_pad] when n_split > 1
     unsigned* tickets;                // [row_tiles]
     int64_t rows_pad;
+    // Grouped launches (routed experts): CTA (x, y) takes row tile x of item y, an item being {first row tile of its
+    // expert in the stacked layout, first row of its tokens in x and y, tokens (at most 256), 0}; rows = an
+    // expert's rows. Null for a plain launch.
+    const int4* items;
+    int64_t item_bound_tiles, item_bound_rows;   // grouped: the layout's row tiles and x's rows (items past them skip)
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -238,7 +243,28 @@ __global__ void __launch_bounds__(kTcThreads, 1) spmm_tc_kernel(const __grid_con
     const uint32_t done = bars + 8u * (2 * kMaxASlots + 2 * kMaxXSlots);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int rt = blockIdx.x, split = blockIdx.y;
+    // This CTA's row tile, column split, tokens, and where its rows start in x and y (a plain launch: every token,
+    // row tile blockIdx.x of the module; a grouped one: its item's tokens, row tile blockIdx.x of its expert).
+    int rt, split, tokens, n_total;
+    int64_t xrow0 = 0, col0;
+    if (p.items) {
+        const int4 it = p.items[blockIdx.y];
+        rt = it.x + (int)blockIdx.x;
+        split = 0;
+        xrow0 = it.y;
+        tokens = it.z;
+        n_total = (tokens + 15) / 16 * 16;
+        col0 = (int64_t)blockIdx.x * tc::kTileRows;
+        if (tokens <= 0 || n_total > p.n_total || it.x < 0 || rt >= p.item_bound_tiles || xrow0 < 0 ||
+            xrow0 + tokens > p.item_bound_rows)
+            return;                                                 // uniform over the CTA, before any barrier
+    } else {
+        rt = blockIdx.x;
+        split = blockIdx.y;
+        tokens = p.tokens;
+        n_total = p.n_total;
+        col0 = (int64_t)rt * tc::kTileRows;
+    }
     const int kt0 = split * p.kt_per_split;
     const int kt1 = min(p.col_tiles, kt0 + p.kt_per_split);
     const int nk = kt1 - kt0;                                      // column tiles of this CTA
@@ -286,7 +312,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) spmm_tc_kernel(const __grid_con
                 mbar_expect_tx(fullx(s), (uint32_t)p.b_bytes);
                 for (int b = 0; b < p.n_boxes; ++b)
                     tma_load_2d(x_ring + s * p.b_bytes + b * p.box_rows * 128, &tmap_x, (kt0 + i) * tc::kTileCols,
-                                b * p.box_rows, fullx(s));
+                                (int)xrow0 + b * p.box_rows, fullx(s));
             }
         }
         __syncwarp();
@@ -298,8 +324,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) spmm_tc_kernel(const __grid_con
         const int j = warp - kMmaWarp;
         if (lane == 0) {
             const bool by_tile = p.acc_stride != 0;
-            const int n0 = by_tile ? p.n_total : (p.n_total / 2 + 15) / 16 * 16;
-            const int n_mine = by_tile ? p.n_total : (j ? p.n_total - n0 : n0);
+            const int n0 = by_tile ? n_total : (n_total / 2 + 15) / 16 * 16;
+            const int n_mine = by_tile ? n_total : (j ? n_total - n0 : n0);
             const uint32_t id = idesc_f16<T>(n_mine);
             const uint32_t d = tmem + (by_tile ? (uint32_t)(j * p.acc_stride) : (uint32_t)(j * n0));
             const uint64_t a0 = sw128_desc(a_ring);
@@ -418,10 +444,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) spmm_tc_kernel(const __grid_con
         tc_fence_after();
         const int quarter = warp & 3, cgroup = warp >> 2;          // 4 column groups of the 16 expander warps
         const int row_local = quarter * 32 + lane;
-        const int64_t row = (int64_t)rt * tc::kTileRows + row_local;
+        const int64_t row = col0 + row_local;                       // y's column: the module's (or expert's) row
         const bool row_ok = row < p.rows;
         const bool two = p.acc_stride != 0 && nk > 1;                // issuer 1 took tiles: add its accumulator
-        for (int c = cgroup; c < p.n_total / 16; c += kExpWarps / 4) {
+        for (int c = cgroup; c < n_total / 16; c += kExpWarps / 4) {
             float v[16];
             const uint32_t ta = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(c * 16);
             tmem_ld16(ta, v);
@@ -434,9 +460,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) spmm_tc_kernel(const __grid_con
 #pragma unroll
             for (int j = 0; j < 16; ++j) {
                 const int t = c * 16 + j;
-                if (t < p.tokens && row_ok) {
+                if (t < tokens && row_ok) {
                     if (p.n_split == 1)
-                        reinterpret_cast<T*>(p.y)[(int64_t)t * p.ldy + row] = from_f32<T>(v[j]);
+                        reinterpret_cast<T*>(p.y)[(xrow0 + t) * p.ldy + row] = from_f32<T>(v[j]);
                     else
                         p.partial[((int64_t)split * p.tokens + t) * p.rows_pad + row] = v[j];
                 }
@@ -495,6 +521,56 @@ int pow2_at_least(int v) {
     int p = 32;
     while (p < v) p <<= 1;
     return p;
+}
+
+// Token-dependent part of a launch plan: MMA N, x boxes, TMEM columns, ring depths, shared memory. Fails when the
+// tokens do not fit shared memory.
+int plan_tokens(int tn, TcPlan& pl) {
+    const int fixed = 1024 + 8 * (2 * kMaxASlots + 2 * kMaxXSlots + 1) + 64;
+    pl.n_total = (tn + 15) / 16 * 16;
+    pl.n_boxes = pl.n_total <= 256 ? 1 : 2;
+    pl.box_rows = pl.n_total / pl.n_boxes;
+    // N <= 256: an accumulator per issuer, side by side; N > 256: one, the issuers splitting its columns.
+    const int acc_cols = pow2_at_least(pl.n_total);
+    pl.acc_stride = pl.n_total <= 256 ? acc_cols : 0;
+    pl.tmem_cols = pl.n_total <= 256 ? 2 * acc_cols : acc_cols;
+    pl.b_bytes = pl.n_total * 128;
+    // Ring depths: x slots first, then as many A slots as the rest holds (even, at most kMaxASlots): the
+    // expanders' latency needs the A depth. When the issuers split the tiles (N <= 256) the x slots are even, so
+    // every use of a slot belongs to the same issuer -- a parity wait cannot then pass on another issuer's
+    // earlier, unfinished use. When both issuers take every tile, three large x slots are enough.
+    const int step_x = pl.acc_stride ? 2 : 1;
+    pl.x_slots = (pl.b_bytes <= 4096 || pl.acc_stride) ? 4 : 3;
+    while (pl.x_slots - step_x >= 2 && kSmemLimit - fixed - pl.x_slots * pl.b_bytes < 2 * kASlotBytes)
+        pl.x_slots -= step_x;
+    pl.a_slots = (kSmemLimit - fixed - pl.x_slots * pl.b_bytes) / kASlotBytes;
+    if (pl.a_slots > kMaxASlots) pl.a_slots = kMaxASlots;
+    pl.a_slots &= ~1;
+    if (pl.a_slots < 2) return fail(P2P_EUNSUPPORTED, "p2p_spmm_tc: %d tokens exceed shared memory", tn);
+    pl.smem = fixed + pl.a_slots * kASlotBytes + pl.x_slots * pl.b_bytes;
+    return P2P_OK;
+}
+
+// The TMA map of x [rows, cols] (row stride ldx elements): boxes of 64 columns x box_rows rows, 128-byte swizzle.
+int encode_x_map(CUtensorMap* map, const void* x, int dtype, int64_t rows, int64_t cols, int64_t ldx, int box_rows) {
+    EncodeTiledFn encode = encode_fn();
+    if (!encode) return fail(P2P_ECUDA, "p2p_spmm_tc: cuTensorMapEncodeTiled unavailable");
+    const cuuint64_t gdim[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    const cuuint64_t gstride[1] = {(cuuint64_t)(ldx * 2)};
+    const cuuint32_t box[2] = {(cuuint32_t)tc::kTileCols, (cuuint32_t)box_rows};
+    const cuuint32_t estride[2] = {1, 1};
+    CUresult r = encode(map, dtype == P2P_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
+                        const_cast<void*>(x), gdim, gstride, box, estride, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(P2P_ECUDA, "p2p_spmm_tc: tensor map encode failed (%d)", (int)r);
+    return P2P_OK;
+}
+
+template <typename T>
+int launch_tc(const CUtensorMap& map, const TcParams& prm, dim3 grid, int smem, cudaStream_t st) {
+    if (int e = allow_smem((const void*)spmm_tc_kernel<T>, smem, "p2p_spmm_tc")) return e;
+    spmm_tc_kernel<T><<<grid, kTcThreads, smem, st>>>(map, prm);
+    return launch_status("p2p_spmm_tc");
 }
 
 // Columns split so that the row tiles fill the SMs: the fewest waves of CTAs a column tile's work, plus the cost of
@@ -565,39 +641,16 @@ extern "C" int p2p_spmm_tc(const void* x, int dtype, int64_t tokens, int64_t col
                     seg_cap_words <= tc::kHeaderWords + tc::kTileRows * tc::kTileCols + 4,
                 "p2p_spmm_tc: segment capacity %lld words", (long long)seg_cap_words);
     P2P_REQUIRE(rows <= 0x7fffffff && cols <= 0x7fffffff, "p2p_spmm_tc: too large");
-    EncodeTiledFn encode = encode_fn();
-    if (!encode) return fail(P2P_ECUDA, "p2p_spmm_tc: cuTensorMapEncodeTiled unavailable");
     cudaStream_t st = as_stream(stream);
     const int sms = sm_count();
     const int64_t row_tiles = (rows + tc::kTileRows - 1) / tc::kTileRows;
     const int col_tiles = (int)((cols + tc::kTileCols - 1) / tc::kTileCols);
     const int elem = 2;
 
-    const int fixed = 1024 + 8 * (2 * kMaxASlots + 2 * kMaxXSlots + 1) + 64;
     for (int64_t t0 = 0; t0 < tokens; t0 += 512) {             // at most 512 tokens (TMEM columns) a launch
         const int tn = (int)(tokens - t0 < 512 ? tokens - t0 : 512);
         TcPlan pl;
-        pl.n_total = (tn + 15) / 16 * 16;
-        pl.n_boxes = pl.n_total <= 256 ? 1 : 2;
-        pl.box_rows = pl.n_total / pl.n_boxes;
-        // N <= 256: an accumulator per issuer, side by side; N > 256: one, the issuers splitting its columns.
-        const int acc_cols = pow2_at_least(pl.n_total);
-        pl.acc_stride = pl.n_total <= 256 ? acc_cols : 0;
-        pl.tmem_cols = pl.n_total <= 256 ? 2 * acc_cols : acc_cols;
-        pl.b_bytes = pl.n_total * 128;
-        // Ring depths: x slots first, then as many A slots as the rest holds (even, at most kMaxASlots): the
-        // expanders' latency needs the A depth. When the issuers split the tiles (N <= 256) the x slots are even, so
-        // every use of a slot belongs to the same issuer -- a parity wait cannot then pass on another issuer's
-        // earlier, unfinished use. When both issuers take every tile, three large x slots are enough.
-        const int step_x = pl.acc_stride ? 2 : 1;
-        pl.x_slots = (pl.b_bytes <= 4096 || pl.acc_stride) ? 4 : 3;
-        while (pl.x_slots - step_x >= 2 && kSmemLimit - fixed - pl.x_slots * pl.b_bytes < 2 * kASlotBytes)
-            pl.x_slots -= step_x;
-        pl.a_slots = (kSmemLimit - fixed - pl.x_slots * pl.b_bytes) / kASlotBytes;
-        if (pl.a_slots > kMaxASlots) pl.a_slots = kMaxASlots;
-        pl.a_slots &= ~1;
-        if (pl.a_slots < 2) return fail(P2P_EUNSUPPORTED, "p2p_spmm_tc: %d tokens exceed shared memory", tn);
-        pl.smem = fixed + pl.a_slots * kASlotBytes + pl.x_slots * pl.b_bytes;
+        if (int e = plan_tokens(tn, pl)) return e;
         plan_split(row_tiles, col_tiles, tn, sms, &pl.n_split, &pl.kt_per_split);
 
         TcParams prm;
@@ -630,29 +683,72 @@ extern "C" int p2p_spmm_tc(const void* x, int dtype, int64_t tokens, int64_t col
             prm.partial = reinterpret_cast<float*>(reinterpret_cast<char*>(workspace) + kTicketRegion);
         }
 
+        prm.items = nullptr;
+        prm.item_bound_tiles = prm.item_bound_rows = 0;
         CUtensorMap map;
-        const cuuint64_t gdim[2] = {(cuuint64_t)cols, (cuuint64_t)tn};
-        const cuuint64_t gstride[1] = {(cuuint64_t)(ldx * elem)};
-        const cuuint32_t box[2] = {(cuuint32_t)tc::kTileCols, (cuuint32_t)pl.box_rows};
-        const cuuint32_t estride[2] = {1, 1};
         const void* xt = reinterpret_cast<const char*>(x) + t0 * ldx * elem;
-        CUresult r = encode(&map, dtype == P2P_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
-                            const_cast<void*>(xt), gdim, gstride, box, estride, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-        if (r != CUDA_SUCCESS) return fail(P2P_ECUDA, "p2p_spmm_tc: tensor map encode failed (%d)", (int)r);
-
+        if (int e = encode_x_map(&map, xt, dtype, tn, cols, ldx, pl.box_rows)) return e;
         const dim3 grid((unsigned)row_tiles, (unsigned)pl.n_split);
-        if (dtype == P2P_BF16) {
-            if (int e = allow_smem((const void*)spmm_tc_kernel<__nv_bfloat16>, pl.smem, "p2p_spmm_tc")) return e;
-            spmm_tc_kernel<__nv_bfloat16><<<grid, kTcThreads, pl.smem, st>>>(map, prm);
-        } else {
-            if (int e = allow_smem((const void*)spmm_tc_kernel<__half>, pl.smem, "p2p_spmm_tc")) return e;
-            spmm_tc_kernel<__half><<<grid, kTcThreads, pl.smem, st>>>(map, prm);
-        }
-        if (int e = launch_status("p2p_spmm_tc")) return e;
+        if (int e = dtype == P2P_BF16 ? launch_tc<__nv_bfloat16>(map, prm, grid, pl.smem, st)
+                                      : launch_tc<__half>(map, prm, grid, pl.smem, st))
+            return e;
     }
     return P2P_OK;
+}
+
+extern "C" int p2p_spmm_tc_grouped(const void* x, int dtype, int64_t x_rows, int64_t cols, int64_t ldx,
+                                   const uint32_t* words, const int64_t* seg, int64_t layout_row_tiles,
+                                   int64_t rows, int64_t item_row_tiles, int64_t seg_cap_words, const int32_t* items,
+                                   int64_t n_items, int64_t max_tokens, void* y, int64_t ldy, void* stream) {
+    P2P_REQUIRE(x_rows >= 0 && rows >= 1 && cols >= 1 && n_items >= 0, "p2p_spmm_tc_grouped: bad shape");
+    if (n_items == 0 || x_rows == 0) return P2P_OK;
+    if (dtype != P2P_BF16 && dtype != P2P_F16) return fail(P2P_EUNSUPPORTED, "p2p_spmm_tc_grouped: bf16 or f16");
+    P2P_REQUIRE(x && words && seg && items && y, "p2p_spmm_tc_grouped: null pointer");
+    P2P_REQUIRE(aligned16(words) && aligned16(items), "p2p_spmm_tc_grouped: words and items need 16-byte alignment");
+    P2P_REQUIRE(cols % 8 == 0 && ldx % 8 == 0 && ldx >= cols && aligned16(x),
+                "p2p_spmm_tc_grouped: x needs 16-byte aligned rows (cols and ldx multiples of 8)");
+    P2P_REQUIRE(ldy >= rows, "p2p_spmm_tc_grouped: ldy %lld below rows %lld", (long long)ldy, (long long)rows);
+    P2P_REQUIRE(item_row_tiles == (rows + tc::kTileRows - 1) / tc::kTileRows,
+                "p2p_spmm_tc_grouped: %lld row tiles an item for %lld rows", (long long)item_row_tiles, (long long)rows);
+    P2P_REQUIRE(max_tokens >= 1 && max_tokens <= 256, "p2p_spmm_tc_grouped: items of 1 to 256 tokens (%lld)",
+                (long long)max_tokens);
+    P2P_REQUIRE(seg_cap_words >= 0 && seg_cap_words % 4 == 0 &&
+                    seg_cap_words <= tc::kHeaderWords + tc::kTileRows * tc::kTileCols + 4,
+                "p2p_spmm_tc_grouped: segment capacity %lld words", (long long)seg_cap_words);
+    P2P_REQUIRE(x_rows <= 0x7fffffff && n_items <= 65535, "p2p_spmm_tc_grouped: too large");
+    cudaStream_t st = as_stream(stream);
+    TcPlan pl;
+    if (int e = plan_tokens((int)max_tokens, pl)) return e;
+    const int col_tiles = (int)((cols + tc::kTileCols - 1) / tc::kTileCols);
+    TcParams prm;
+    prm.words = words;
+    prm.seg = seg;
+    prm.rows = (int)rows;
+    prm.col_tiles = col_tiles;
+    prm.tokens = (int)max_tokens;
+    prm.n_total = pl.n_total;
+    prm.box_rows = pl.box_rows;
+    prm.n_boxes = pl.n_boxes;
+    prm.tmem_cols = pl.tmem_cols;
+    prm.acc_stride = pl.acc_stride;
+    prm.a_slots = pl.a_slots;
+    prm.x_slots = pl.x_slots;
+    prm.b_bytes = pl.b_bytes;
+    prm.kt_per_split = col_tiles;                             // whole rows: items already spread the work
+    prm.n_split = 1;
+    prm.y = y;
+    prm.ldy = ldy;
+    prm.rows_pad = 0;
+    prm.partial = nullptr;
+    prm.tickets = nullptr;
+    prm.items = reinterpret_cast<const int4*>(items);
+    prm.item_bound_tiles = layout_row_tiles;
+    prm.item_bound_rows = x_rows;
+    CUtensorMap map;
+    if (int e = encode_x_map(&map, x, dtype, x_rows, cols, ldx, pl.box_rows)) return e;
+    const dim3 grid((unsigned)item_row_tiles, (unsigned)n_items);
+    return dtype == P2P_BF16 ? launch_tc<__nv_bfloat16>(map, prm, grid, pl.smem, st)
+                             : launch_tc<__half>(map, prm, grid, pl.smem, st);
 }
 
 extern "C" int p2p_spmm_tc_status(int reset, void* stream) {

@@ -1,0 +1,140 @@
+"""Routed experts run compact: a FusedMoE quant_method that multiplies the experts' pruned weights where they lie,
+instead of expanding every used expert to dense on every pass (p2p/compact.py:227-262, CompactMoE).
+
+    ExpertTiles   one routed-expert tensor (row blocks with a leading expert dimension) in one tensor-core layout,
+                  each expert starting on a 128-row tile
+    GroupedMoE    quant_method.apply(layer, dispatch_output): gated-SiLU experts (w13 = gate then up, w2 = down)
+
+A pass: the routed (token, slot) pairs are sorted by expert on the GPU and x's rows gathered in that order; one
+grouped launch of the compact GEMM (p2p_spmm_tc_grouped: a CTA takes one row tile of one expert's run of up to 256
+tokens) gives gate and up for every pair; SiLU(gate) * up in fp32, rounded to x's dtype; a second grouped launch gives
+down; each token's outputs are weighted by its routing weights and added in slot order in fp32 (deterministic). The
+per-expert token counts are read back once a pass (the reference's CompactMoE also syncs, on torch.unique).
+"""
+from __future__ import annotations
+
+import torch
+
+from . import kernels
+from ._lib import P2PError, call, dtype_code, ptr, stream_of
+from .compact import _cols, to_compact
+
+ITEM_TOKENS = 256                       # tokens one grouped CTA takes (an accumulator of at most 256 columns)
+
+
+class ExpertTiles:
+    """A routed-expert tensor [E, rows, cols] from its row blocks (each ("dense", W [E, r, C]) or ("sparse" |
+    "compact", values [E, r, k], words | idx [E, r, ...], C), in row order), laid out for the grouped GEMM: expert
+    e's rows start at row tile e * item_row_tiles. Built once at load (one layout build an expert)."""
+
+    def __init__(self, blocks: list):
+        blocks = [to_compact(b) for b in blocks]
+        self.cols = _cols(blocks[0])
+        self.experts = blocks[0][1].shape[0]
+        self.rows = sum(b[1].shape[-2] for b in blocks)
+        self.dtype, self.device = blocks[0][1].dtype, blocks[0][1].device
+        if self.dtype not in (torch.bfloat16, torch.float16) or self.cols % 8:
+            raise P2PError("grouped experts need bf16 / f16 weights with columns in multiples of 8")
+        self.item_row_tiles = -(-self.rows // 128)
+        words, segs, base = [], [], 0
+        for e in range(self.experts):
+            row_blocks, row0 = [], 0
+            for b in blocks:
+                v = b[1][e].contiguous()
+                idx = b[2][e].contiguous() if b[0] == "compact" else None
+                row_blocks.append((row0, v, idx))
+                row0 += v.shape[0]
+            w, seg, _ = kernels.tiles_build(row_blocks, self.cols)
+            total = int(seg[-1].item())
+            words.append(w[:total])
+            segs.append(seg[:-1] + base)
+            base += total
+        self.words = torch.cat(words) if base else torch.zeros(4, dtype=torch.int32, device=self.device)
+        self.seg = torch.cat(segs + [torch.tensor([base], dtype=torch.int64, device=self.device)])
+        self.seg_cap = int((self.seg[1:] - self.seg[:-1]).max().item())
+        self.layout_row_tiles = self.experts * self.item_row_tiles
+
+    def __call__(self, x: torch.Tensor, items: torch.Tensor, max_tokens: int, out: torch.Tensor) -> torch.Tensor:
+        """out [P, rows] rows s.. of an item = x rows s.. times the item's expert (items: int32 [n, 4] on the GPU)."""
+        call("p2p_spmm_tc_grouped", ptr(x), dtype_code(x), x.shape[0], self.cols, x.stride(0), ptr(self.words),
+             ptr(self.seg), self.layout_row_tiles, self.rows, self.item_row_tiles, self.seg_cap, ptr(items),
+             items.shape[0], max_tokens, ptr(out), out.stride(0), stream_of(x))
+        return out
+
+    def nbytes(self) -> int:
+        return self.words.numel() * 4 + self.seg.numel() * 8
+
+
+def route(ids: torch.Tensor, experts: int) -> tuple:
+    """The pairs (token, slot) with an expert, sorted by expert (stable): (order [P] into ids.flatten(), per-expert
+    counts on the host)."""
+    flat = ids.reshape(-1)
+    key = torch.where(flat >= 0, flat, torch.full_like(flat, experts)).to(torch.int64)
+    order = torch.argsort(key, stable=True)
+    counts = torch.bincount(key, minlength=experts + 1)[:experts].tolist()
+    return order[: sum(counts)], counts
+
+
+def items_of(counts: list, item_row_tiles: int, device) -> tuple:
+    """Items {first row tile of the expert, first row of its tokens, tokens, 0} of at most ITEM_TOKENS tokens."""
+    out, start = [], 0
+    for e, n in enumerate(counts):
+        for s in range(0, n, ITEM_TOKENS):
+            out.append((e * item_row_tiles, start + s, min(ITEM_TOKENS, n - s), 0))
+        start += n
+    t = torch.tensor(out if out else [(0, 0, 0, 0)], dtype=torch.int32).to(device)
+    return t[: len(out)], max((o[2] for o in out), default=0)
+
+
+class GroupedMoE(torch.nn.Module):
+    """A FusedMoE's quant_method for compact routed experts, gated SiLU: weights {"w13_weight": blocks of [E, 2R, H]
+    (gate rows, then up rows), "w2_weight": blocks of [E, H, R]}. apply(layer, dispatch_output) returns the layer's
+    output [T, H] in x's dtype. Other attributes are the layer's own method's."""
+
+    def __init__(self, method, weights: dict):
+        super().__init__()
+        self.method = method
+        self.w13 = ExpertTiles(weights["w13_weight"])
+        self.w2 = ExpertTiles(weights["w2_weight"])
+        if self.w13.rows % 2 or self.w2.cols != self.w13.rows // 2 or self.w2.rows != self.w13.cols:
+            raise P2PError("w13 [E, 2R, H] and w2 [E, H, R] do not match")
+
+    def __getattr__(self, name):
+        try:
+            return super().__getattr__(name)
+        except AttributeError:
+            return getattr(super().__getattr__("method"), name)
+
+    def apply(self, layer, dispatch_output):
+        x = dispatch_output.hidden_states
+        topk = dispatch_output.topk_output
+        ids, weights = topk.topk_ids, topk.topk_weights
+        T, K = ids.shape
+        x2 = x.reshape(-1, x.shape[-1])
+        if x2.dtype != self.w13.dtype:
+            raise P2PError(f"x is {x2.dtype}, the experts {self.w13.dtype}")
+        order, counts = route(ids, self.w13.experts)
+        P = order.numel()
+        y = torch.zeros(T, self.w2.rows, dtype=torch.float32, device=x.device)
+        if P:
+            xs = x2.index_select(0, order // K).contiguous()
+            items13, most = items_of(counts, self.w13.item_row_tiles, x.device)
+            gu = self.w13(xs, items13, most, torch.empty(P, self.w13.rows, dtype=x2.dtype, device=x.device))
+            R = self.w13.rows // 2
+            h = (torch.nn.functional.silu(gu[:, :R].float()) * gu[:, R:].float()).to(x2.dtype).contiguous()
+            items2, _ = items_of(counts, self.w2.item_row_tiles, x.device)
+            down = self.w2(h, items2, most, torch.empty(P, self.w2.rows, dtype=x2.dtype, device=x.device))
+            # back to (token, slot) order, weighted, added slot by slot
+            per_slot = torch.zeros(T * K, self.w2.rows, dtype=torch.float32, device=x.device)
+            per_slot[order] = down.float()
+            per_slot *= weights.reshape(-1, 1).float()
+            per_slot = per_slot.view(T, K, -1)
+            for j in range(K):
+                y += per_slot[:, j]
+        return y.to(x2.dtype).reshape(*x.shape[:-1], self.w2.rows)
+
+    def process_weights_after_loading(self, layer) -> None:
+        pass
+
+    def nbytes(self) -> int:
+        return self.w13.nbytes() + self.w2.nbytes()

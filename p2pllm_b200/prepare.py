@@ -12,7 +12,8 @@ File format (p2p/prepare.py:42-84), one safetensors file a layer, dir/layer<i>.s
 
 Routed experts carry a leading expert dimension on every tensor. The format is the reference's, so files written by
 either side install on the other; write() makes its selection on the GPU (Wanda top-k, ties to the lower column) and
-install_replica() hands the blocks to compact.Compact / compact.CompactMoE.
+install_replica() hands the blocks to compact.Compact / compact.CompactMoE (or, with form "grouped", routed experts to
+moe.GroupedMoE, which multiplies them compact instead of expanding them every pass).
 """
 from __future__ import annotations
 
@@ -97,7 +98,8 @@ def blocks_of(tensors: dict, key: str, info: dict, device=None, dtype=None) -> l
 def install_replica(model, file: str, form: str = "compact") -> dict:
     """Replace a copied layer's projections with the replica in `file` and return its metadata: compact as their
     modules' quant_method (the module's weight becomes an empty [rows, 0] tensor), or expanded back into the weight
-    (form "dense", a check) (p2p/prepare.py:86-119)."""
+    (form "dense", a check) (p2p/prepare.py:86-119). Form "grouped" is "compact" with routed experts run by
+    moe.GroupedMoE (gated SiLU) instead of compact.CompactMoE."""
     import torch.nn as nn
     tensors, meta = load(file)
     layer = family.layers(model)[meta["layer"]]
@@ -124,7 +126,11 @@ def install_replica(model, file: str, form: str = "compact") -> dict:
             experts.setdefault(path, {})[param] = parts
     for path, weights in experts.items():
         module = modules[path]
-        module.quant_method = compact.CompactMoE(module.quant_method, weights)
+        if form == "grouped":
+            from . import moe
+            module.quant_method = moe.GroupedMoE(module.quant_method, weights)
+        else:
+            module.quant_method = compact.CompactMoE(module.quant_method, weights)
         for param in weights:
             setattr(module, param, nn.Parameter(getattr(module, param).new_empty(0), requires_grad=False))
     if torch.cuda.is_available():

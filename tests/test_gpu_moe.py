@@ -1,0 +1,100 @@
+"""The grouped MoE path (moe.GroupedMoE: the routed experts multiplied compact, no per-pass expansion) against a
+plain fp32 MoE on the dense pruned weights: the reference's own MoE test case (tests/test_compact.py:80-126, f16) and
+a config-4-shaped layer (128 experts, top-8, hidden 2048, intermediate 768, keep 30, bf16, 272 tokens) with tokens
+routed nowhere, an expert past one grouped item (>256 tokens) and experts no token reaches. rel-L2 <= 1e-2."""
+from typing import NamedTuple
+
+import pytest
+import torch
+import torch.nn.functional as F
+
+from p2pllm_b200 import compact, moe, wanda
+
+pytestmark = pytest.mark.gpu
+
+
+class TopK(NamedTuple):
+    topk_weights: torch.Tensor
+    topk_ids: torch.Tensor
+
+
+class Dispatch(NamedTuple):
+    hidden_states: torch.Tensor
+    topk_output: TopK
+
+
+def _reference_moe(x, ids, weights, w13, w2):
+    """fp32 gated-SiLU MoE on dense weights, expert by expert; ids < 0 route nowhere."""
+    xf, out = x.float(), torch.zeros(x.shape[0], w2.shape[1], device=x.device)
+    R = w13.shape[1] // 2
+    for e in ids[ids >= 0].unique().tolist():
+        t, j = (ids == e).nonzero(as_tuple=True)
+        gu = xf[t] @ w13[e].float().T
+        h = F.silu(gu[:, :R]) * gu[:, R:]
+        out.index_add_(0, t, weights[t, j].float().unsqueeze(1) * (h @ w2[e].float().T))
+    return out
+
+
+def _prune_experts(w, keep, g, form):
+    """Per-expert Wanda selection of w [E, r, C]: the block and the dense pruned weights."""
+    E, r, C = w.shape
+    norms = torch.rand(E, C, generator=g, device="cuda") + 0.1
+    vals, idxs = zip(*(wanda.select(w[e], keep, norms[e]) for e in range(E)))
+    values, idx = torch.stack(vals), torch.stack(idxs)
+    dense = torch.zeros_like(w)
+    dense.scatter_(2, idx.long(), values)
+    if form == "sparse":
+        _, words = compact.pack(dense.reshape(-1, C), dense.reshape(-1, C) != 0)
+        return ("sparse", values, words.view(E, r, -1), C), dense
+    return ("compact", values, idx, C), dense
+
+
+def _layer(E, R, H, keep, dtype, seed, form="compact"):
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    w13 = (torch.randn(E, 2 * R, H, generator=g, device="cuda") * 0.05).to(dtype)
+    w2 = (torch.randn(E, H, R, generator=g, device="cuda") * 0.05).to(dtype)
+    gate, dg = _prune_experts(w13[:, :R].contiguous(), keep, g, form)
+    up, du = _prune_experts(w13[:, R:].contiguous(), keep, g, form)
+    down, dd = _prune_experts(w2, keep, g, form)
+    return {"w13_weight": [gate, up], "w2_weight": [down]}, torch.cat([dg, du], 1), dd, g
+
+
+def _check(got, want):
+    rel = float((got.float() - want).norm() / want.norm())
+    assert rel <= 1e-2, rel
+
+
+def test_the_reference_moe_case():
+    """E 16, R 32, H 64, 5 tokens, 2 experts a token (5 of 16 used), keep 40, f16, the reference's packed blocks."""
+    blocks, w13, w2, g = _layer(16, 32, 64, 40, torch.float16, 0, form="sparse")
+    ids = torch.tensor([[3, 11], [11, 0], [7, 3], [15, 7], [0, 11]], device="cuda")
+    x = torch.randn(5, 64, generator=g, device="cuda").half()
+    w = torch.rand(5, 2, generator=g, device="cuda")
+    got = moe.GroupedMoE(None, blocks).apply(None, Dispatch(x, TopK(w, ids)))
+    assert got.dtype == torch.float16 and got.shape == (5, 64)
+    _check(got, _reference_moe(x, ids, w, w13, w2))
+
+
+def test_a_config4_layer_with_skewed_routing():
+    E, R, H, T, K = 128, 768, 2048, 272, 8
+    blocks, w13, w2, g = _layer(E, R, H, 30, torch.bfloat16, 1)
+    logits = torch.randn(T, E, generator=g, device="cuda")
+    logits[:, 120:] = -1e9                                   # experts 120.. never reached
+    logits[:, 0] += 10                                       # every token to expert 0: 272 > 256 tokens, two items
+    w, ids = logits.softmax(-1).topk(K, dim=-1)
+    ids = ids.clone()
+    ids[::17, -1] = -1                                       # some slots routed nowhere
+    x = torch.randn(T, H, generator=g, device="cuda").bfloat16()
+    layer = moe.GroupedMoE(None, blocks)
+    got = layer.apply(None, Dispatch(x, TopK(w, ids)))
+    _check(got, _reference_moe(x, ids, w, w13, w2))
+    again = layer.apply(None, Dispatch(x, TopK(w, ids)))
+    assert torch.equal(got, again)                           # fixed order: the same bits every pass
+
+
+def test_no_routed_tokens_give_zeros():
+    blocks, _, _, g = _layer(4, 64, 64, 50, torch.bfloat16, 2)
+    x = torch.randn(3, 64, generator=g, device="cuda").bfloat16()
+    ids = torch.full((3, 2), -1, device="cuda")
+    got = moe.GroupedMoE(None, blocks).apply(None, Dispatch(x, TopK(torch.ones(3, 2, device="cuda"), ids)))
+    assert torch.equal(got, torch.zeros_like(got))
