@@ -485,14 +485,54 @@ __global__ void __launch_bounds__(kTcThreads, 1) spmm_tc_kernel(const __grid_con
     __syncthreads();
     if (!s_last) return;
     __threadfence();
-    const int64_t n = (int64_t)p.tokens * tc::kTileRows;
-    for (int64_t i = threadIdx.x; i < n; i += kTcThreads) {
-        const int t = (int)(i / tc::kTileRows);
-        const int64_t row = (int64_t)rt * tc::kTileRows + (i % tc::kTileRows);
-        if (row >= p.rows) continue;
-        float s = 0.f;
-        for (int sp = 0; sp < p.n_split; ++sp) s += __ldcg(p.partial + ((int64_t)sp * p.tokens + t) * p.rows_pad + row);
-        reinterpret_cast<T*>(p.y)[(int64_t)t * p.ldy + row] = from_f32<T>(s);
+    // Four rows a unit (16-byte loads), kUnits units a thread at a time, every split's loads of a pair of splits in
+    // flight together; the sums still run split by split, so the result does not depend on who added them.
+    constexpr int kUnits = 8;
+    const int64_t n4 = (int64_t)p.tokens * (tc::kTileRows / 4);
+    const int64_t col = (int64_t)rt * tc::kTileRows;
+    for (int64_t u0 = threadIdx.x; u0 < n4; u0 += (int64_t)kTcThreads * kUnits) {
+        float4 acc[kUnits];
+        int64_t off[kUnits];                                        // unit q's place in one split's partials
+#pragma unroll
+        for (int q = 0; q < kUnits; ++q) {
+            const int64_t u = u0 + (int64_t)q * kTcThreads;
+            const int64_t uc = u < n4 ? u : 0;
+            off[q] = (uc / 32) * p.rows_pad + col + (uc % 32) * 4;
+            acc[q] = make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+        const int64_t split_stride = (int64_t)p.tokens * p.rows_pad;
+        int sp = 0;
+        for (; sp + 1 < p.n_split; sp += 2) {
+            float4 a[kUnits], b[kUnits];
+#pragma unroll
+            for (int q = 0; q < kUnits; ++q) {
+                a[q] = __ldcg(reinterpret_cast<const float4*>(p.partial + sp * split_stride + off[q]));
+                b[q] = __ldcg(reinterpret_cast<const float4*>(p.partial + (sp + 1) * split_stride + off[q]));
+            }
+#pragma unroll
+            for (int q = 0; q < kUnits; ++q) {
+                acc[q].x += a[q].x; acc[q].y += a[q].y; acc[q].z += a[q].z; acc[q].w += a[q].w;
+                acc[q].x += b[q].x; acc[q].y += b[q].y; acc[q].z += b[q].z; acc[q].w += b[q].w;
+            }
+        }
+        if (sp < p.n_split) {
+#pragma unroll
+            for (int q = 0; q < kUnits; ++q) {
+                const float4 a = __ldcg(reinterpret_cast<const float4*>(p.partial + sp * split_stride + off[q]));
+                acc[q].x += a.x; acc[q].y += a.y; acc[q].z += a.z; acc[q].w += a.w;
+            }
+        }
+#pragma unroll
+        for (int q = 0; q < kUnits; ++q) {
+            const int64_t u = u0 + (int64_t)q * kTcThreads;
+            if (u >= n4) break;
+            const int64_t t = u / 32, row = col + (u % 32) * 4;
+            T* yt = reinterpret_cast<T*>(p.y) + t * p.ldy;
+            const float v[4] = {acc[q].x, acc[q].y, acc[q].z, acc[q].w};
+#pragma unroll
+            for (int c = 0; c < 4; ++c)
+                if (row + c < p.rows) yt[row + c] = from_f32<T>(v[c]);
+        }
     }
     if (threadIdx.x == 0) p.tickets[rt] = 0u;            // the workspace is zeroed again for the next call
 }

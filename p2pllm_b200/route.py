@@ -3,6 +3,7 @@ step's ranks over NCCL (NVLink), and the receiver adds them in fp32 in member or
 
     member_part   p2p/route.py:1254-1274   l(h) for member 0, dtype(l(h) - h) for the others
     send_piece    p2p/route.py:800-810     one NCCL isend per destination rank
+    exchange      a rank's sends and receives of one step as one NCCL batch
     summed        p2p/route.py:825-831     dtype(sum of the parts in fp32, member order)
 
 The SGLang pipeline plumbing around them (stage layout, request framing, KV updates) is not part of this package.
@@ -34,9 +35,24 @@ def send_piece(t: torch.Tensor, dsts: list, group=None) -> list:
 
 
 def recv_parts(srcs: list, like: torch.Tensor, group=None) -> list:
-    """One part from each rank in srcs (member order), received into new tensors shaped like `like`."""
+    """One part from each rank in srcs (member order), received into new tensors shaped like `like`. For a rank that
+    only receives; a rank that also sends in the same step uses exchange()."""
     bufs = [torch.empty_like(like) for _ in srcs]
     works = [dist.irecv(b, src, group=group) for b, src in zip(bufs, srcs)]
     for w in works:
         w.wait()
+    return bufs
+
+
+def exchange(piece: torch.Tensor, dsts: list, srcs: list, group=None) -> list:
+    """Send piece to every rank in dsts and receive one part from every rank in srcs (member order), as one batch:
+    NCCL runs a rank's sends and receives of a step together, so two ranks sending to each other cannot each wait for
+    the other's receive. Returns the received parts."""
+    piece = piece.contiguous()
+    bufs = [torch.empty_like(piece) for _ in srcs]
+    ops = [dist.P2POp(dist.isend, piece, d, group=group) for d in dsts]
+    ops += [dist.P2POp(dist.irecv, b, s, group=group) for b, s in zip(bufs, srcs)]
+    if ops:
+        for w in dist.batch_isend_irecv(ops):
+            w.wait()
     return bufs

@@ -53,6 +53,18 @@ def _hop(rank, world):
     return [g.tolist() for g in got]
 
 
+def _exchange(rank, world):
+    piece = torch.full((2, 3), float(rank + 1))
+    peers = [r for r in range(world) if r != rank]
+    got = route.exchange(piece, peers, peers)
+    return [g.tolist() for g in got]
+
+
+def test_exchange_batches_both_directions():
+    out = _spawn(_exchange)
+    assert out[0] == [[[2.0] * 3] * 2] and out[1] == [[[1.0] * 3] * 2]
+
+
 def test_hop_delivers_every_members_part_in_order():
     out = _spawn(_hop)
     want = [(torch.full((3, 5), float(r + 1)) * torch.arange(5.0)).tolist() for r in range(2)]

@@ -50,10 +50,8 @@ def _hop(rank, world):
     import oracle
     g = torch.Generator(device="cuda").manual_seed(rank)
     piece = torch.randn(17, 4096, generator=g, device="cuda").bfloat16()
-    works = route.send_piece(piece, [r for r in range(world) if r != rank])
-    others = route.recv_parts([r for r in range(world) if r != rank], piece)
-    for w in works:
-        w.wait()
+    peers = [r for r in range(world) if r != rank]
+    others = route.exchange(piece, peers, peers)
     parts = [piece if r == rank else others.pop(0) for r in range(world)]
     got = route.summed(parts)
     bits = lambda t: t.cpu().view(torch.int16).numpy().view(np.uint16)
