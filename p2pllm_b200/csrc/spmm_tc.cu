@@ -21,7 +21,10 @@
 // runs on, so a broken pipeline ends the kernel with an error status instead of hanging the GPU.
 #include <cuda.h>
 
+#include <map>
+#include <mutex>
 #include <type_traits>
+#include <utility>
 
 #include "common.cuh"
 #include "tc_layout.cuh"
@@ -69,7 +72,31 @@ struct TcParams {
     // expert's rows. Null for a plain launch.
     const int4* items;
     int64_t item_bound_tiles, item_bound_rows;   // grouped: the layout's row tiles and x's rows (items past them skip)
+    // Split columns reduced inside a thread-block cluster (the splits of a row tile, cluster dims 1 x n_split): each
+    // CTA leaves its fp32 partial tile [tokens][128] in its own shared memory (the rings, free by then) and adds its
+    // share of the tile's rows over DSMEM, split by split. 0: partials through the global workspace and a ticket.
+    int cluster;
 };
+
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// The shared::cluster address of `saddr` (this CTA's shared memory) in cluster CTA `rank`.
+__device__ __forceinline__ uint32_t cluster_addr(uint32_t saddr, int rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
+    return r;
+}
+
+__device__ __forceinline__ float4 ld_cluster_f4(uint32_t addr) {
+    float4 v;
+    asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "r"(addr)
+                 : "memory");
+    return v;
+}
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -460,11 +487,14 @@ __global__ void __launch_bounds__(kTcThreads, 1) spmm_tc_kernel(const __grid_con
 #pragma unroll
             for (int j = 0; j < 16; ++j) {
                 const int t = c * 16 + j;
-                if (t < tokens && row_ok) {
-                    if (p.n_split == 1)
-                        reinterpret_cast<T*>(p.y)[(xrow0 + t) * p.ldy + row] = from_f32<T>(v[j]);
-                    else
+                if (t < tokens) {
+                    if (p.n_split == 1) {
+                        if (row_ok) reinterpret_cast<T*>(p.y)[(xrow0 + t) * p.ldy + row] = from_f32<T>(v[j]);
+                    } else if (p.cluster) {
+                        reinterpret_cast<float*>(gbase)[t * tc::kTileRows + row_local] = v[j];   // rings are free
+                    } else if (row_ok) {
                         p.partial[((int64_t)split * p.tokens + t) * p.rows_pad + row] = v[j];
+                    }
                 }
             }
         }
@@ -477,6 +507,39 @@ __global__ void __launch_bounds__(kTcThreads, 1) spmm_tc_kernel(const __grid_con
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(p.tmem_cols) : "memory");
     }
     if (p.n_split == 1) return;
+
+    if (p.cluster) {
+        // Every split's partial tile is in its CTA's shared memory; CTA `split` of the cluster adds up its share of the
+        // tile's (token, 4-row) units, split by split, and writes y. The second barrier keeps each CTA's shared memory
+        // alive until every CTA of the cluster has read it.
+        cluster_sync_all();
+        const int ns = p.n_split;
+        const int64_t n4 = (int64_t)tokens * (tc::kTileRows / 4);
+        const int64_t u_begin = n4 * split / ns, u_end = n4 * (split + 1) / ns;
+        const uint32_t part = smem_u32(gbase);
+        for (int64_t u = u_begin + threadIdx.x; u < u_end; u += kTcThreads) {
+            const int t = (int)(u / 32), r4 = (int)(u % 32) * 4;
+            const uint32_t off = part + (uint32_t)(t * tc::kTileRows + r4) * 4u;
+            float4 parts[8];
+            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+            for (int sp = 0; sp < 8; ++sp)
+                if (sp < ns) parts[sp] = ld_cluster_f4(cluster_addr(off, sp));
+#pragma unroll
+            for (int sp = 0; sp < 8; ++sp)
+                if (sp < ns) {
+                    acc.x += parts[sp].x; acc.y += parts[sp].y; acc.z += parts[sp].z; acc.w += parts[sp].w;
+                }
+            const int64_t row = col0 + r4;
+            T* yt = reinterpret_cast<T*>(p.y) + (xrow0 + t) * p.ldy;
+            const float v[4] = {acc.x, acc.y, acc.z, acc.w};
+#pragma unroll
+            for (int c = 0; c < 4; ++c)
+                if (row + c < p.rows) yt[row + c] = from_f32<T>(v[c]);
+        }
+        cluster_sync_all();
+        return;
+    }
 
     // Split columns: the last CTA of this row tile adds the partials in split order.
     __threadfence();
@@ -609,8 +672,74 @@ int encode_x_map(CUtensorMap* map, const void* x, int dtype, int64_t rows, int64
 template <typename T>
 int launch_tc(const CUtensorMap& map, const TcParams& prm, dim3 grid, int smem, cudaStream_t st) {
     if (int e = allow_smem((const void*)spmm_tc_kernel<T>, smem, "p2p_spmm_tc")) return e;
-    spmm_tc_kernel<T><<<grid, kTcThreads, smem, st>>>(map, prm);
+    if (!prm.cluster) {
+        spmm_tc_kernel<T><<<grid, kTcThreads, smem, st>>>(map, prm);
+        return launch_status("p2p_spmm_tc");
+    }
+    // the n_split CTAs of a row tile as one cluster (grid.y == n_split)
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 1;
+    attr[0].val.clusterDim.y = grid.y;
+    attr[0].val.clusterDim.z = 1;
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(kTcThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (cudaLaunchKernelEx(&cfg, spmm_tc_kernel<T>, map, prm) != cudaSuccess) return launch_status("p2p_spmm_tc");
     return launch_status("p2p_spmm_tc");
+}
+
+// Whether a launch's column splits are added inside clusters: 2 to 8 splits, the fp32 partial tile
+// [tokens (rounded to 16)][128] fits the rings it replaces, and the device holds the launch's clusters in as few waves
+// as the plain grid takes (a cluster of whole-SM CTAs must fit one GPC, so fewer clusters than SMs / n_split may be
+// resident at once).
+int max_clusters(const TcPlan& pl, int n_split);
+
+bool cluster_reduce(const TcPlan& pl, int n_split, int64_t row_tiles) {
+    if (n_split < 2 || n_split > 8) return false;
+    if ((int64_t)pl.n_total * tc::kTileRows * 4 > (int64_t)pl.a_slots * kASlotBytes + (int64_t)pl.x_slots * pl.b_bytes)
+        return false;
+    const int resident = max_clusters(pl, n_split);
+    if (resident <= 0) return false;
+    const int64_t sms = sm_count();
+    const int64_t plain_waves = (row_tiles * n_split + sms - 1) / sms;
+    const int64_t cluster_waves = (row_tiles + resident - 1) / resident;
+    return cluster_waves <= plain_waves;
+}
+
+// Clusters of n_split CTAs (this plan's shared memory) the device can run at once (cached per device and shape).
+int max_clusters(const TcPlan& pl, int n_split) {
+    static std::mutex mu;
+    static std::map<std::pair<int, int>, int> known;         // (n_split, device) x smem -> clusters at once
+    std::lock_guard<std::mutex> lock(mu);
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const auto key = std::make_pair(n_split * 64 + dev, pl.smem);
+    auto it = known.find(key);
+    if (it != known.end()) return it->second;
+    int clusters = 0;
+    if (allow_smem((const void*)spmm_tc_kernel<__nv_bfloat16>, pl.smem, "p2p_spmm_tc") == P2P_OK &&
+        allow_smem((const void*)spmm_tc_kernel<__half>, pl.smem, "p2p_spmm_tc") == P2P_OK) {
+        cudaLaunchConfig_t cfg = {};
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = 1;
+        attr[0].val.clusterDim.y = n_split;
+        attr[0].val.clusterDim.z = 1;
+        cfg.gridDim = dim3(1, n_split);
+        cfg.blockDim = dim3(kTcThreads);
+        cfg.dynamicSmemBytes = pl.smem;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        if (cudaOccupancyMaxActiveClusters(&clusters, spmm_tc_kernel<__nv_bfloat16>, &cfg) != cudaSuccess) clusters = 0;
+        cudaGetLastError();                                  // a refusal here only means: use the workspace path
+    }
+    known[key] = clusters;
+    return clusters;
 }
 
 // Columns split so that the row tiles fill the SMs: the fewest waves of CTAs a column tile's work, plus the cost of
@@ -659,6 +788,8 @@ extern "C" size_t p2p_spmm_tc_workspace(int64_t rows, int64_t cols, int64_t toke
         int n = 1, per = col_tiles;
         plan_split(row_tiles, col_tiles, t, sm_count(), &n, &per);
         if (n == 1) continue;
+        TcPlan pl;
+        if (plan_tokens(t, pl) == P2P_OK && cluster_reduce(pl, n, row_tiles)) continue;   // partials stay in smem
         const size_t w = kTicketRegion + (size_t)n * t * row_tiles * tc::kTileRows * sizeof(float);
         need = need > w ? need : w;
     }
@@ -714,7 +845,8 @@ extern "C" int p2p_spmm_tc(const void* x, int dtype, int64_t tokens, int64_t col
         prm.rows_pad = row_tiles * tc::kTileRows;
         prm.partial = nullptr;
         prm.tickets = nullptr;
-        if (pl.n_split > 1) {
+        prm.cluster = cluster_reduce(pl, pl.n_split, row_tiles) ? 1 : 0;
+        if (pl.n_split > 1 && !prm.cluster) {
             const size_t need = kTicketRegion + (size_t)pl.n_split * tn * prm.rows_pad * sizeof(float);
             P2P_REQUIRE(workspace && workspace_bytes >= need, "p2p_spmm_tc: workspace of %zu bytes, %zu needed",
                         workspace_bytes, need);
@@ -784,6 +916,7 @@ extern "C" int p2p_spmm_tc_grouped(const void* x, int dtype, int64_t x_rows, int
     prm.items = reinterpret_cast<const int4*>(items);
     prm.item_bound_tiles = layout_row_tiles;
     prm.item_bound_rows = x_rows;
+    prm.cluster = 0;
     CUtensorMap map;
     if (int e = encode_x_map(&map, x, dtype, x_rows, cols, ldx, pl.box_rows)) return e;
     const dim3 grid((unsigned)item_row_tiles, (unsigned)n_items);
