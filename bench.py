@@ -57,6 +57,10 @@ def parse():
     p.add_argument("--tokens", type=int, default=272)
     p.add_argument("--calib-tokens", type=int, default=128 * 2048)
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--workload", default="cfg2", choices=["cfg2", "cfg1", "cfg3", "cfg5"],
+                   help="cfg2 (default): the headline line. cfg1, cfg3, cfg5: one extra line each on one GPU (config "
+                        "1's fp32 projection; config 3's replica block + group combine at T = 1, 8, 32, 64; a "
+                        "Qwen2.5-32B replica layer at keep 40)")
     return p.parse_args()
 
 
@@ -135,10 +139,10 @@ class ReplicaLayer:
     """A Llama-3-8B replica layer's four linear modules, each a Compact over its projections' blocks, calibrated and
     selected on the GPU."""
 
-    def __init__(self, seed: int, tokens: int, calib_tokens: int, device: torch.device):
+    def __init__(self, seed: int, tokens: int, calib_tokens: int, device: torch.device, projections=None):
         from p2pllm_b200 import compact, kernels, wanda
         self.device, self.tokens = device, tokens
-        self.proj = {p.name: p for p in workloads.LLAMA3_8B}
+        self.proj = {p.name: p for p in (projections or workloads.LLAMA3_8B)}
         self.inputs, self.methods, self.k = {}, {}, {}
         calib_ms, select_ms, calib_bytes = 0.0, 0.0, 0
         ev = lambda: torch.cuda.Event(enable_timing=True)
@@ -440,9 +444,98 @@ def run_b200(args, rank, world, local):
         print(json.dumps(out), flush=True)
 
 
+def _timed_us(fn, reps: int) -> float:
+    """Median CUDA-event time of fn over reps calls, each queued behind a spin (device time, not launch cost)."""
+    for _ in range(3):
+        fn()
+    torch.cuda.synchronize()
+    out = []
+    for _ in range(reps):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda._sleep(HEAD_START_CYCLES // 10)
+        a.record()
+        fn()
+        b.record()
+        torch.cuda.synchronize()
+        out.append(a.elapsed_time(b) * 1e3)
+    return statistics.median(out)
+
+
+def run_extra(args):
+    """The extra workloads, one JSON line each (one GPU; not the headline)."""
+    from p2pllm_b200 import compact, kernels, replica, wanda
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    peak = measured_peaks()
+    reps = max(10, min(args.steps, 50))
+    line = {"workload": args.workload, "n_gpus": 1, "higher_is_better": True, "data": "synthetic (seeded)",
+            "peak_hbm_gbs": peak["hbm_gbs"], "peak_source": peak["source"]}
+    if args.workload == "cfg1":
+        # fp32 W [2048, 2048] keep 40, calibration 128 x 512 tokens, a 17-token forward (CUDA-core row kernel)
+        cfg = workloads.config1(seed=0)
+        sums = torch.zeros(cfg.w.shape[1], dtype=torch.float64, device=device)
+        for chunk in cfg.calib_chunks(device):
+            kernels.sumsq_cols(chunk, sums)
+        w = cfg.w.to(device)
+        values, idx = wanda.select(w, cfg.keep, wanda.channel_norms(sums, w))
+        method = compact.Compact([("compact", values, idx, w.shape[1])])
+        x = cfg.x.to(device)
+        us = _timed_us(lambda: method.apply(None, x), reps)
+        alg = values.numel() * (4 + 2) + 2 * x.numel() * 4
+        line.update(metric="config-1 projection tokens/s (fp32, 2048 x 2048, keep 40, T=17)", value=17 / us * 1e6,
+                    unit="tokens/s", us_per_pass=us, algorithmic_bytes=alg, hbm_gbs=alg / us / 1e3,
+                    frac=alg / us / 1e3 / peak["hbm_gbs"], dtype="f32", kernel="spmm_rows (layout rows)")
+    elif args.workload == "cfg3":
+        # A Llama-shaped residual MLP block (hidden 4096, intermediate 14336): l(x) = x + down(silu(gate x) * up x).
+        # The group: the dense block l0 (torch GEMMs, not timed) and the keep-40 replica of the next block; timed:
+        # the replica's compact GEMMs, its SiLU * up, and the group combine h' = l0(h) + dtype(l1'(h) - h).
+        H, I = 4096, 14336
+        g = torch.Generator(device=device).manual_seed(3)
+        mods = {}
+        for name, rows, cols in (("gate_up", 2 * I, H), ("down", H, I)):
+            w = (torch.randn(rows, cols, generator=g, device=device) * 0.02).bfloat16()
+            norms = torch.rand(cols, generator=g, device=device) + 0.1
+            values, idx = wanda.select(w, 40, norms)
+            mods[name] = (compact.Compact([("compact", values, idx, cols)]), values.numel() * 4)
+            del w
+        per_t = {}
+        for T in (1, 8, 32, 64):
+            h = torch.randn(T, H, generator=g, device=device)
+            h = (h / h.pow(2).mean(-1, keepdim=True).sqrt()).bfloat16()          # RMS-normalised rows
+            l0 = torch.randn(T, H, generator=g, device=device).bfloat16()        # the dense member's output
+
+            def step():
+                gu = mods["gate_up"][0].apply(None, h)
+                a = (torch.nn.functional.silu(gu[:, :I].float()) * gu[:, I:].float()).bfloat16()
+                l1 = h + mods["down"][0].apply(None, a)
+                return replica.combine([l0, l1], h, h)
+
+            us = _timed_us(step, reps)
+            alg = mods["gate_up"][1] + mods["down"][1] + T * (H * 2 + 2 * I * 2 + I * 2 + H * 2) + 4 * T * H * 2
+            per_t[T] = {"us": us, "tokens_per_s": T / us * 1e6, "hbm_gbs": alg / us / 1e3,
+                        "frac": alg / us / 1e3 / peak["hbm_gbs"]}
+        line.update(metric="config-3 replica member + combine tokens/s (keep 40 MLP block, hidden 4096)",
+                    value=per_t[64]["tokens_per_s"], unit="tokens/s", per_tokens=per_t, dtype="bf16",
+                    note="synthetic residual-MLP block stands in for a decoder layer (no KV cache here)")
+    else:
+        # a Qwen2.5-32B replica layer (keep 40 everywhere), T = 17
+        layer = ReplicaLayer(seed=0, tokens=17, calib_tokens=args.calib_tokens, device=device,
+                             projections=workloads.QWEN25_32B)
+        us = _timed_us(layer.step, reps)
+        alg = sum(layer.algorithmic_bytes(n, 17) for n in MODULES)
+        line.update(metric="config-5 replica layer tokens/s (Qwen2.5-32B shapes, keep 40, T=17)", value=17 / us * 1e6,
+                    unit="tokens/s", us_per_pass=us, algorithmic_bytes=alg, hbm_gbs=alg / us / 1e3,
+                    frac=alg / us / 1e3 / peak["hbm_gbs"], dtype="bf16")
+    print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse()
     rank, world, local = dist_env()
+    if args.workload != "cfg2":
+        if rank == 0:
+            run_extra(args)
+        return
     if args.impl == "reference":
         run_reference(args, rank, world)
         return
