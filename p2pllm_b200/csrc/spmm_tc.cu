@@ -324,10 +324,17 @@ __global__ void __launch_bounds__(kTcThreads, 1) spmm_tc_kernel(const __grid_con
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = s_tmem;
+    // Every CTA of this grid is resident: the next kernel in the stream may start launching on SMs as they free up.
+    if (threadIdx.x == 0) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
     if (warp == kProducerWarp) {
         // The x tiles (the B operand), one producer lane per slot so the slots' waits and TMA issues run side by side.
         if (lane == 0) asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmap_x)) : "memory");
+        // Launched as a programmatic dependent of the stream's previous kernel, this CTA may start while that kernel
+        // still runs: everything before the first x load (barriers, TMEM, segment offsets, the weights streaming in,
+        // expansion of the first tiles) overlaps its tail. x may be that kernel's output, so its loads wait here for
+        // it to complete; every global write of this kernel comes after an MMA, hence after this wait.
+        asm volatile("griddepcontrol.wait;" ::: "memory");
         if (lane < SX) {
             const int s = lane;
             uint32_t ph = 0;
@@ -672,23 +679,22 @@ int encode_x_map(CUtensorMap* map, const void* x, int dtype, int64_t rows, int64
 template <typename T>
 int launch_tc(const CUtensorMap& map, const TcParams& prm, dim3 grid, int smem, cudaStream_t st) {
     if (int e = allow_smem((const void*)spmm_tc_kernel<T>, smem, "p2p_spmm_tc")) return e;
-    if (!prm.cluster) {
-        spmm_tc_kernel<T><<<grid, kTcThreads, smem, st>>>(map, prm);
-        return launch_status("p2p_spmm_tc");
-    }
-    // the n_split CTAs of a row tile as one cluster (grid.y == n_split)
+    // A programmatic dependent of the stream's previous kernel (the kernel waits for it before loading x), and with
+    // split columns reduced in clusters, the n_split CTAs of a row tile as one cluster (grid.y == n_split).
     cudaLaunchConfig_t cfg = {};
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = 1;
-    attr[0].val.clusterDim.y = grid.y;
-    attr[0].val.clusterDim.z = 1;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = 1;
+    attr[1].val.clusterDim.y = grid.y;
+    attr[1].val.clusterDim.z = 1;
     cfg.gridDim = grid;
     cfg.blockDim = dim3(kTcThreads);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = prm.cluster ? 2 : 1;
     if (cudaLaunchKernelEx(&cfg, spmm_tc_kernel<T>, map, prm) != cudaSuccess) return launch_status("p2p_spmm_tc");
     return launch_status("p2p_spmm_tc");
 }
