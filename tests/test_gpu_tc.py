@@ -171,3 +171,38 @@ def test_split_launches_of_different_shapes_share_a_workspace():
         sample = torch.arange(0, rows, 61, device="cuda")
         want = oracle.forward(_bits(x), _bits(values[sample]), idx[sample].cpu().numpy(), cols, "bf16")
         _check(y[:, sample], want, torch.bfloat16)
+
+
+def test_dependent_launches_see_the_previous_kernels_output():
+    """Each launch is a programmatic dependent of the stream's previous kernel and may start before it ends; its x
+    loads wait for it. Chained modules (B on A's output) and x rewritten in place just before a launch must give the
+    same bits as runs separated by a synchronize."""
+    g = torch.Generator(device="cuda").manual_seed(9)
+    mods = []
+    for seed in (1, 2, 3):
+        values, idx = _module(4096, 4096, 33, seed=seed)
+        mods.append(compact.Compact([("compact", values, idx, 4096)]))
+    x = torch.randn(17, 4096, generator=g, device="cuda").bfloat16()
+    want = x
+    steps = []
+    for m in mods:                                          # the reference: one module at a time, synchronised
+        want = m.apply(None, want)
+        torch.cuda.synchronize()
+        steps.append(want.clone())
+    for _ in range(3):
+        torch.cuda._sleep(2_000_000)                        # the host queues the chain while the GPU is busy
+        y = x
+        for m in mods:
+            y = m.apply(None, y)
+        torch.cuda.synchronize()
+        assert torch.equal(y, steps[-1])
+    # an in-place torch kernel on x right before a launch
+    m = mods[0]
+    for scale in (2.0, -0.5, 3.0):
+        x2 = x.clone()
+        torch.cuda.synchronize()
+        torch.cuda._sleep(1_000_000)
+        x2.mul_(scale)
+        got = m.apply(None, x2)
+        torch.cuda.synchronize()
+        assert torch.equal(got, m.apply(None, (x * scale)))
