@@ -169,17 +169,32 @@ int p2p_spmm_tc(const void* x, int dtype, int64_t tokens, int64_t cols, int64_t 
                 size_t workspace_bytes, void* stream);
 
 /* Routed experts in one launch: y [x_rows, ldy] row x_row0 + t = x row x_row0 + t times its expert's matrix, for every
- * item {first row tile of the expert in the stacked tensor-core layout, x_row0, tokens (1..256), 0} of items
- * [n_items][4] (device memory, int32, 16-byte aligned). The layout stacks the experts' matrices, each starting on a
- * 128-row tile (layout_row_tiles row tiles in all, item_row_tiles = ceil(rows / 128) an expert); x holds each
- * expert's tokens contiguously (sorted by expert); max_tokens bounds every item's tokens. Items that point past the
- * layout or x are skipped. No workspace: an item takes whole rows.
+ * item {expert, x_row0, tokens (1..256), 0} of items [n_items][4] (device memory, int32, 16-byte aligned;
+ * p2p_moe_route writes them). The layout stacks the experts' matrices, expert e starting at row tile
+ * e * item_row_tiles (layout_row_tiles row tiles in all, item_row_tiles = ceil(rows / 128)); x holds each expert's
+ * tokens contiguously (sorted by expert); max_tokens bounds every item's tokens. Items that point past the layout or x
+ * are skipped. No workspace: an item takes whole rows.
  * Replaces p2p/compact.py:241-256 (CompactMoE.apply, which expands every used expert to dense each pass) for the
  * routed experts' GEMMs. */
 int p2p_spmm_tc_grouped(const void* x, int dtype, int64_t x_rows, int64_t cols, int64_t ldx, const uint32_t* words,
                         const int64_t* seg, int64_t layout_row_tiles, int64_t rows, int64_t item_row_tiles,
                         int64_t seg_cap_words, const int32_t* items, int64_t n_items, int64_t max_tokens, void* y,
                         int64_t ldy, void* stream);
+
+/* The routing of a routed-experts pass, on the GPU: ids [n_pairs] int64 (a token's slots consecutive; < 0: no expert).
+ * order [n_pairs]: the routed pairs sorted by expert, and within an expert by pair index (stable); where [n_pairs]:
+ * each pair's place in order, or -1; counts [experts] int32; items [max_items][4] int32: {expert, first place,
+ * places (1..256), 0} for the grouped GEMM (max_items >= ceil(n_pairs / 256) + experts); meta [3] int64: {routed
+ * pairs, items, most places in an item}. One block; experts <= 8192.
+ * Replaces the routing CompactMoE leaves to torch and SGLang (p2p/compact.py:241-256: unique, renumbering). */
+int p2p_moe_route(const int64_t* ids, int64_t n_pairs, int experts, int64_t* order, int64_t* where, int32_t* counts,
+                  int32_t* items, int64_t max_items, int64_t* meta, void* stream);
+
+/* out [tokens, ldo] row t = dtype(sum over slots j = 0.. k-1, in order, of weights[t k + j] * y[where[t k + j]]),
+ * the fp32 weights and y [*, ldy] (bf16 or f16) in the pair order of p2p_moe_route; pairs with where < 0 add nothing.
+ * The weighted sum a fused MoE ends with (SGLang's, which CompactMoE hands the experts to). */
+int p2p_moe_combine(const void* y, int dtype, int64_t ldy, const int64_t* where, const float* weights, int64_t tokens,
+                    int k, int64_t hidden, void* out, int64_t ldo, void* stream);
 
 /* P2P_OK unless a p2p_spmm_tc launch since the last reset gave up waiting on its pipeline (then P2P_ECUDA, naming
  * the site); reset != 0 clears the flag. Syncs the stream. */

@@ -67,10 +67,11 @@ struct TcParams {
     float* partial;                   // [n_split, tokens, rows_pad] when n_split > 1
     unsigned* tickets;                // [row_tiles]
     int64_t rows_pad;
-    // Grouped launches (routed experts): CTA (x, y) takes row tile x of item y, an item being {first row tile of its
-    // expert in the stacked layout, first row of its tokens in x and y, tokens (at most 256), 0}; rows = an
-    // expert's rows. Null for a plain launch.
+    // Grouped launches (routed experts): CTA (x, y) takes row tile x of item y, an item being {expert, first row of
+    // its tokens in x and y, tokens (at most 256), 0}; expert e's rows start at row tile e * item_row_tiles of the
+    // stacked layout; rows = an expert's rows. Null for a plain launch.
     const int4* items;
+    int item_row_tiles;
     int64_t item_bound_tiles, item_bound_rows;   // grouped: the layout's row tiles and x's rows (items past them skip)
     // Split columns reduced inside a thread-block cluster (the splits of a row tile, cluster dims 1 x n_split): each
     // CTA leaves its fp32 partial tile [tokens][128] in its own shared memory (the rings, free by then) and adds its
@@ -276,7 +277,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) spmm_tc_kernel(const __grid_con
     int64_t xrow0 = 0, col0;
     if (p.items) {
         const int4 it = p.items[blockIdx.y];
-        rt = it.x + (int)blockIdx.x;
+        rt = it.x * p.item_row_tiles + (int)blockIdx.x;
         split = 0;
         xrow0 = it.y;
         tokens = it.z;
@@ -863,6 +864,7 @@ extern "C" int p2p_spmm_tc(const void* x, int dtype, int64_t tokens, int64_t col
 
         prm.items = nullptr;
         prm.item_bound_tiles = prm.item_bound_rows = 0;
+        prm.item_row_tiles = 0;
         CUtensorMap map;
         const void* xt = reinterpret_cast<const char*>(x) + t0 * ldx * elem;
         if (int e = encode_x_map(&map, xt, dtype, tn, cols, ldx, pl.box_rows)) return e;
@@ -922,6 +924,7 @@ extern "C" int p2p_spmm_tc_grouped(const void* x, int dtype, int64_t x_rows, int
     prm.items = reinterpret_cast<const int4*>(items);
     prm.item_bound_tiles = layout_row_tiles;
     prm.item_bound_rows = x_rows;
+    prm.item_row_tiles = (int)item_row_tiles;
     prm.cluster = 0;
     CUtensorMap map;
     if (int e = encode_x_map(&map, x, dtype, x_rows, cols, ldx, pl.box_rows)) return e;

@@ -5,18 +5,19 @@ instead of expanding every used expert to dense on every pass (p2p/compact.py:22
                   each expert starting on a 128-row tile
     GroupedMoE    quant_method.apply(layer, dispatch_output): gated-SiLU experts (w13 = gate then up, w2 = down)
 
-A pass: the routed (token, slot) pairs are sorted by expert on the GPU and x's rows gathered in that order; one
-grouped launch of the compact GEMM (p2p_spmm_tc_grouped: a CTA takes one row tile of one expert's run of up to 256
-tokens) gives gate and up for every pair; SiLU(gate) * up in fp32, rounded to x's dtype; a second grouped launch gives
-down; each token's outputs are weighted by its routing weights and added in slot order in fp32 (deterministic). The
-per-expert token counts are read back once a pass (the reference's CompactMoE also syncs, on torch.unique).
+A pass: one kernel (p2p_moe_route) sorts the routed (token, slot) pairs by expert (stable) and writes the grouped
+GEMM's items; x's rows are gathered in that order; one grouped launch of the compact GEMM (p2p_spmm_tc_grouped: a CTA
+takes one row tile of one expert's run of up to 256 tokens) gives gate and up for every pair; SiLU(gate) * up in fp32,
+rounded to x's dtype; a second grouped launch gives down; p2p_moe_combine weights each token's outputs by its routing
+weights and adds them in slot order in fp32 (deterministic). Three numbers (pairs, items, the largest item) are read
+back once a pass to size the launches (the reference's CompactMoE also syncs, on torch.unique).
 """
 from __future__ import annotations
 
 import torch
 
 from . import kernels
-from ._lib import P2PError, call, dtype_code, ptr, stream_of
+from ._lib import P2PError, call, dtype_code, ptr, require_cuda, stream_of
 from .compact import _cols, to_compact
 
 ITEM_TOKENS = 256                       # tokens one grouped CTA takes (an accumulator of at most 256 columns)
@@ -65,25 +66,24 @@ class ExpertTiles:
         return self.words.numel() * 4 + self.seg.numel() * 8
 
 
-def route(ids: torch.Tensor, experts: int) -> tuple:
-    """The pairs (token, slot) with an expert, sorted by expert (stable): (order [P] into ids.flatten(), per-expert
-    counts on the host)."""
-    flat = ids.reshape(-1)
-    key = torch.where(flat >= 0, flat, torch.full_like(flat, experts)).to(torch.int64)
-    order = torch.argsort(key, stable=True)
-    counts = torch.bincount(key, minlength=experts + 1)[:experts].tolist()
-    return order[: sum(counts)], counts
-
-
-def items_of(counts: list, item_row_tiles: int, device) -> tuple:
-    """Items {first row tile of the expert, first row of its tokens, tokens, 0} of at most ITEM_TOKENS tokens."""
-    out, start = [], 0
-    for e, n in enumerate(counts):
-        for s in range(0, n, ITEM_TOKENS):
-            out.append((e * item_row_tiles, start + s, min(ITEM_TOKENS, n - s), 0))
-        start += n
-    t = torch.tensor(out if out else [(0, 0, 0, 0)], dtype=torch.int32).to(device)
-    return t[: len(out)], max((o[2] for o in out), default=0)
+def route(ids: torch.Tensor, experts: int) -> dict:
+    """The pass's routing on the GPU (p2p_moe_route): order [P] (pairs sorted by expert, stable), where [T K] (each
+    pair's place, -1 if routed nowhere), counts [E], items [n, 4] ({expert, first place, places, 0}), and on the host
+    P, the item count and the largest item."""
+    require_cuda(ids)
+    flat = ids.reshape(-1).to(torch.int64).contiguous()
+    n = flat.numel()
+    dev = flat.device
+    max_items = -(-n // ITEM_TOKENS) + experts
+    order = torch.empty(max(n, 1), dtype=torch.int64, device=dev)
+    where = torch.empty(max(n, 1), dtype=torch.int64, device=dev)
+    counts = torch.empty(experts, dtype=torch.int32, device=dev)
+    items = torch.empty(max_items, 4, dtype=torch.int32, device=dev)
+    meta = torch.empty(3, dtype=torch.int64, device=dev)
+    call("p2p_moe_route", ptr(flat), n, experts, ptr(order), ptr(where), ptr(counts), ptr(items), max_items, ptr(meta),
+         stream_of(flat))
+    pairs, n_items, most = meta.tolist()
+    return {"order": order[:pairs], "where": where[:n], "counts": counts, "items": items[:n_items], "most": most}
 
 
 class GroupedMoE(torch.nn.Module):
@@ -113,25 +113,20 @@ class GroupedMoE(torch.nn.Module):
         x2 = x.reshape(-1, x.shape[-1])
         if x2.dtype != self.w13.dtype:
             raise P2PError(f"x is {x2.dtype}, the experts {self.w13.dtype}")
-        order, counts = route(ids, self.w13.experts)
-        P = order.numel()
-        y = torch.zeros(T, self.w2.rows, dtype=torch.float32, device=x.device)
-        if P:
-            xs = x2.index_select(0, order // K).contiguous()
-            items13, most = items_of(counts, self.w13.item_row_tiles, x.device)
-            gu = self.w13(xs, items13, most, torch.empty(P, self.w13.rows, dtype=x2.dtype, device=x.device))
-            R = self.w13.rows // 2
-            h = (torch.nn.functional.silu(gu[:, :R].float()) * gu[:, R:].float()).to(x2.dtype).contiguous()
-            items2, _ = items_of(counts, self.w2.item_row_tiles, x.device)
-            down = self.w2(h, items2, most, torch.empty(P, self.w2.rows, dtype=x2.dtype, device=x.device))
-            # back to (token, slot) order, weighted, added slot by slot
-            per_slot = torch.zeros(T * K, self.w2.rows, dtype=torch.float32, device=x.device)
-            per_slot[order] = down.float()
-            per_slot *= weights.reshape(-1, 1).float()
-            per_slot = per_slot.view(T, K, -1)
-            for j in range(K):
-                y += per_slot[:, j]
-        return y.to(x2.dtype).reshape(*x.shape[:-1], self.w2.rows)
+        r = route(ids, self.w13.experts)
+        P = r["order"].numel()
+        out = torch.empty(T, self.w2.rows, dtype=x2.dtype, device=x.device)
+        if P == 0:
+            return out.zero_().reshape(*x.shape[:-1], self.w2.rows)
+        xs = x2.index_select(0, r["order"] // K).contiguous()
+        gu = self.w13(xs, r["items"], r["most"], torch.empty(P, self.w13.rows, dtype=x2.dtype, device=x.device))
+        R = self.w13.rows // 2
+        h = (torch.nn.functional.silu(gu[:, :R].float()) * gu[:, R:].float()).to(x2.dtype).contiguous()
+        down = self.w2(h, r["items"], r["most"], torch.empty(P, self.w2.rows, dtype=x2.dtype, device=x.device))
+        w = weights.reshape(-1).float().contiguous()
+        call("p2p_moe_combine", ptr(down), dtype_code(down), down.stride(0), ptr(r["where"]), ptr(w), T, K,
+             self.w2.rows, ptr(out), out.stride(0), stream_of(down))
+        return out.reshape(*x.shape[:-1], self.w2.rows)
 
     def process_weights_after_loading(self, layer) -> None:
         pass

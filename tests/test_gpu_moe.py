@@ -98,3 +98,29 @@ def test_no_routed_tokens_give_zeros():
     ids = torch.full((3, 2), -1, device="cuda")
     got = moe.GroupedMoE(None, blocks).apply(None, Dispatch(x, TopK(torch.ones(3, 2, device="cuda"), ids)))
     assert torch.equal(got, torch.zeros_like(got))
+
+
+@pytest.mark.parametrize("T,K,E", [(272, 8, 128), (5, 2, 16), (3000, 4, 64), (1, 1, 1)])
+def test_route_is_a_stable_sort_by_expert(T, K, E):
+    """p2p_moe_route against torch: pairs sorted by expert (ties by pair index), places, counts, items of <= 256."""
+    g = torch.Generator(device="cuda").manual_seed(T)
+    ids = torch.randint(-1, E, (T, K), generator=g, device="cuda")
+    ids[0, 0] = 0
+    r = moe.route(ids, E)
+    flat = ids.reshape(-1)
+    key = torch.where(flat >= 0, flat, torch.full_like(flat, E))
+    want = torch.argsort(key, stable=True)[: int((flat >= 0).sum())]
+    assert torch.equal(r["order"], want)
+    where = torch.full_like(flat, -1)
+    where[want] = torch.arange(want.numel(), device="cuda")
+    assert torch.equal(r["where"], where)
+    counts = torch.bincount(flat[flat >= 0], minlength=E)
+    assert torch.equal(r["counts"].long(), counts)
+    items = r["items"].cpu().tolist()
+    start, k = 0, 0
+    for e, c in enumerate(counts.tolist()):
+        for s in range(0, c, 256):
+            assert items[k] == [e, start + s, min(256, c - s), 0]
+            k += 1
+        start += c
+    assert k == len(items) and r["most"] == max((it[2] for it in items), default=0)
