@@ -163,6 +163,10 @@ size_t p2p_spmm_tc_workspace(int64_t rows, int64_t cols, int64_t tokens);
  * layout, on tcgen05 tensor cores (fp32 accumulation in TMEM, x staged by TMA). bf16 or f16; cols a multiple of 8;
  * seg_cap_words: the largest segment's word count. Any token count (512 a launch). workspace: zeroed once before its
  * first use (left zeroed again); calls sharing it must not overlap on the GPU.
+ * Each launch is a programmatic dependent of the stream's previous kernel: it may start while that kernel finishes,
+ * reading words and seg (and setting up) at once, but it reads x and writes y / the workspace only after that kernel
+ * has completed. So x may be the previous kernel's output; words and seg must not be (build them, then synchronize,
+ * as p2p_tiles_fill does). Column splits of a row tile may run as a thread-block cluster reducing over DSMEM.
  * Replaces p2p/compact.cu:82-278 (spmm_kernel, sum_parts, spmm) and p2p/compact.py:192-199 (Tiles.__call__). */
 int p2p_spmm_tc(const void* x, int dtype, int64_t tokens, int64_t cols, int64_t ldx, const uint32_t* words,
                 const int64_t* seg, int64_t rows, int64_t seg_cap_words, void* y, int64_t ldy, void* workspace,
