@@ -213,33 +213,47 @@ class ReplicaLayer:
         return outs
 
 
-def cpu_layer_time(layer: ReplicaLayer, budget_s: float) -> tuple:
-    """The reference's CPU forward of every projection (F.linear of the unpacked rows, in bf16) on the host cores, on
-    a sample of each projection's rows scaled to all of them. Returns (seconds per layer pass, sample description)."""
-    from oracle import cpu_ref
-    torch.set_num_threads(os.cpu_count() or 1)
-    g = torch.Generator().manual_seed(0)
-    total = 0.0
-    frac = 1.0 / 16
-    for module, (group, names) in MODULES.items():
-        x = layer.inputs[group].cpu()
-        for n in names:
-            p = layer.proj[n]
-            rows = max(64, int(p.rows * frac))
-            k = layer.k[n]
+class ReferenceCPU:
+    """The reference's CPU forward of a Llama-3-8B replica layer (the oracle port of compact.unpack's CPU branch +
+    F.linear, p2p/compact.py:57-61, in bf16) on all host cores, on a sample of each projection's rows (1/16, >= 64)
+    with a random k-subset kept in each row (the CPU cost does not depend on which), scaled to all rows. Used by both
+    the headline's cpu_baseline and the --impl reference arm, so the two report the same measurement."""
+
+    def __init__(self, tokens: int):
+        from oracle import cpu_ref
+        self.cpu_ref = cpu_ref
+        torch.set_num_threads(os.cpu_count() or 1)
+        self.cores = torch.get_num_threads()
+        self.tokens = tokens
+        g = torch.Generator().manual_seed(0)
+        self.projs = list(workloads.LLAMA3_8B)
+        self.mats, self.xs = {}, {}
+        for p in self.projs:
+            rows = max(64, int(p.rows / 16))
+            k = max(1, round(p.keep / 100 * p.cols))
             w = (torch.randn(rows, p.cols, generator=g) * 0.02).bfloat16()
             idx = torch.rand(rows, p.cols, generator=g).topk(k, dim=1).indices.sort(dim=1).values
-            dense = cpu_ref.unpack_rows(torch.gather(w, 1, idx), idx, p.cols)
-            cpu_ref.forward(x, dense)                                  # warm-up
-            times, t_start = [], time.perf_counter()
-            while len(times) < 3 or (time.perf_counter() - t_start < budget_s / 7 and len(times) < 20):
-                t0 = time.perf_counter()
-                cpu_ref.forward(x, dense)
-                times.append(time.perf_counter() - t0)
-            total += statistics.median(times) * p.rows / rows
-    sample = (f"rows 1/16 of each projection (>= 64), {layer.tokens} tokens, bf16 F.linear of the unpacked rows, "
-              f"median of >= 3 runs per projection, scaled to all rows")
-    return total, sample
+            self.mats[p.name] = (cpu_ref.unpack_rows(torch.gather(w, 1, idx), idx, p.cols), p.rows / rows)
+            if INPUT_OF[p.name] not in self.xs:
+                self.xs[INPUT_OF[p.name]] = (torch.randn(tokens, p.cols, generator=g)
+                                             * workloads.channel_scale(p.cols, g)).bfloat16()
+        self.sample = (f"rows 1/16 of each projection (>= 64), {tokens} tokens, bf16 F.linear of the unpacked rows, "
+                       "scaled to all rows; median over steps")
+
+    def step(self) -> float:
+        """Seconds of one layer pass (scaled from the sample)."""
+        total = 0.0
+        for p in self.projs:
+            dense, scale = self.mats[p.name]
+            t0 = time.perf_counter()
+            self.cpu_ref.forward(self.xs[INPUT_OF[p.name]], dense)
+            total += (time.perf_counter() - t0) * scale
+        return total
+
+    def layer_seconds(self, steps: int, warmup: int) -> float:
+        for _ in range(warmup):
+            self.step()
+        return statistics.median(self.step() for _ in range(steps))
 
 
 # ---------------------------------------------------------------------------------------------------------- driver --
@@ -270,47 +284,17 @@ def run_reference(args, rank, world):
     """The reference's CPU forward on the host cores, rank 0 only."""
     if rank != 0:
         return
-    from oracle import cpu_ref
-    torch.set_num_threads(os.cpu_count() or 1)
-    cores = torch.get_num_threads()
-    tokens = args.tokens
-    g = torch.Generator().manual_seed(0)
-    projs = list(workloads.LLAMA3_8B)
-    frac = 1.0 / 16
-    mats, xs = {}, {}
-    for p in projs:
-        rows = max(64, int(p.rows * frac))
-        k = max(1, round(p.keep / 100 * p.cols))
-        w = (torch.randn(rows, p.cols, generator=g) * 0.02).bfloat16()
-        # a random k-subset of each row, as a Wanda selection would give: the CPU cost does not depend on which
-        idx = torch.rand(rows, p.cols, generator=g).topk(k, dim=1).indices.sort(dim=1).values
-        mats[p.name] = (cpu_ref.unpack_rows(torch.gather(w, 1, idx), idx, p.cols), p.rows / rows)
-        if INPUT_OF[p.name] not in xs:
-            xs[INPUT_OF[p.name]] = (torch.randn(tokens, p.cols, generator=g) * workloads.channel_scale(p.cols, g)).bfloat16()
-
-    def step():
-        total = 0.0
-        for p in projs:
-            dense, scale = mats[p.name]
-            t0 = time.perf_counter()
-            cpu_ref.forward(xs[INPUT_OF[p.name]], dense)
-            total += (time.perf_counter() - t0) * scale
-        return total
-
-    for _ in range(args.warmup):
-        step()
-    times = [step() for _ in range(args.steps)]
-    layer_s = statistics.median(times)
-    value = tokens / layer_s
-    sample = (f"rows 1/16 of each projection (>= 64), {tokens} tokens, bf16 F.linear of the unpacked rows, "
-              "scaled to all rows; median over steps")
+    ref = ReferenceCPU(args.tokens)
+    layer_s = ref.layer_seconds(args.steps, args.warmup)
+    value = args.tokens / layer_s
     print(json.dumps({
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": layer_s * 1e3, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": "cfg2 Llama-3-8B replica layer (q,k,v,o keep 33; gate,up,down keep 36), T=%d" % tokens,
-                   "tokens": tokens, "path": "reference CPU forward (oracle port of compact.unpack + F.linear)"},
-        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample},
+        "config": {"workload": "cfg2 Llama-3-8B replica layer (q,k,v,o keep 33; gate,up,down keep 36), T=%d"
+                               % args.tokens,
+                   "tokens": args.tokens, "path": "reference CPU forward (oracle port of compact.unpack + F.linear)"},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": ref.cores, "kind": "port", "sample": ref.sample},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }), flush=True)
 
@@ -442,9 +426,9 @@ def run_b200(args, rank, world, local):
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        layer_s, sample = cpu_layer_time(layer, budget_s=15.0)
-        cpu = {"value": args.tokens / layer_s, "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port",
-               "sample": sample}
+        ref = ReferenceCPU(args.tokens)
+        layer_s = ref.layer_seconds(steps=5, warmup=2)
+        cpu = {"value": args.tokens / layer_s, "unit": UNIT, "cores": ref.cores, "kind": "port", "sample": ref.sample}
 
     if rank == 0:
         weights = sum(layer.proj[n].rows * layer.k[n] * 4 for n in layer.proj)
