@@ -77,6 +77,9 @@ struct TcParams {
     // CTA leaves its fp32 partial tile [tokens][128] in its own shared memory (the rings, free by then) and adds its
     // share of the tile's rows over DSMEM, split by split. 0: partials through the global workspace and a ticket.
     int cluster;
+    // Unsplit plain launches: y leaves through shared memory and TMA stores (tmap_y: y [tokens, rows], boxes of 128
+    // rows x box_rows tokens), instead of one 2-byte store per value.
+    int y_tma;
 };
 
 __device__ __forceinline__ void cluster_sync_all() {
@@ -246,8 +249,16 @@ __device__ __forceinline__ void load_piece(const uint32_t* words, int lo, int hi
     }
 }
 
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, uint32_t src, int c0, int c1) {
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
+                     reinterpret_cast<uint64_t>(map)),
+                 "r"(c0), "r"(c1), "r"(src)
+                 : "memory");
+}
+
 template <typename T>
-__global__ void __launch_bounds__(kTcThreads, 1) spmm_tc_kernel(const __grid_constant__ CUtensorMap tmap_x, TcParams p) {
+__global__ void __launch_bounds__(kTcThreads, 1)
+    spmm_tc_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_y, TcParams p) {
     extern __shared__ uint8_t smem_raw[];
     __shared__ uint32_t s_tmem;
     __shared__ int s_last;
@@ -496,7 +507,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) spmm_tc_kernel(const __grid_con
             for (int j = 0; j < 16; ++j) {
                 const int t = c * 16 + j;
                 if (t < tokens) {
-                    if (p.n_split == 1) {
+                    if (p.y_tma) {
+                        reinterpret_cast<T*>(gbase)[t * tc::kTileRows + row_local] = from_f32<T>(v[j]);  // rings free
+                    } else if (p.n_split == 1) {
                         if (row_ok) reinterpret_cast<T*>(p.y)[(xrow0 + t) * p.ldy + row] = from_f32<T>(v[j]);
                     } else if (p.cluster) {
                         reinterpret_cast<float*>(gbase)[t * tc::kTileRows + row_local] = v[j];   // rings are free
@@ -506,6 +519,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) spmm_tc_kernel(const __grid_con
                 }
             }
         }
+        if (p.y_tma) asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // the staged tile, for the TMA
     }
 
     tc_fence_before();
@@ -513,6 +527,18 @@ __global__ void __launch_bounds__(kTcThreads, 1) spmm_tc_kernel(const __grid_con
     if (warp == kProducerWarp) {
         tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(p.tmem_cols) : "memory");
+    }
+    if (p.y_tma) {
+        // The tile of y staged as [token][128 rows] in shared memory goes out in one TMA store a box (rows past the
+        // module and tokens past the pass lie outside the map and are not written).
+        if (threadIdx.x == 0) {
+            for (int b = 0; b < p.n_boxes; ++b)
+                tma_store_2d(&tmap_y, smem_u32(gbase) + (uint32_t)(b * p.box_rows * tc::kTileRows * 2), (int)col0,
+                             b * p.box_rows);
+            asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+            asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+        }
+        return;
     }
     if (p.n_split == 1) return;
 
@@ -677,8 +703,25 @@ int encode_x_map(CUtensorMap* map, const void* x, int dtype, int64_t rows, int64
     return P2P_OK;
 }
 
+// The TMA map of y [tokens, rows] (row stride ldy elements) for the epilogue's stores: boxes of 128 rows x box_rows
+// tokens, no swizzle.
+int encode_y_map(CUtensorMap* map, void* y, int dtype, int64_t tokens, int64_t rows, int64_t ldy, int box_rows) {
+    EncodeTiledFn encode = encode_fn();
+    if (!encode) return fail(P2P_ECUDA, "p2p_spmm_tc: cuTensorMapEncodeTiled unavailable");
+    const cuuint64_t gdim[2] = {(cuuint64_t)rows, (cuuint64_t)tokens};
+    const cuuint64_t gstride[1] = {(cuuint64_t)(ldy * 2)};
+    const cuuint32_t box[2] = {(cuuint32_t)tc::kTileRows, (cuuint32_t)box_rows};
+    const cuuint32_t estride[2] = {1, 1};
+    CUresult r = encode(map, dtype == P2P_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, y,
+                        gdim, gstride, box, estride, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                        CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(P2P_ECUDA, "p2p_spmm_tc: y tensor map encode failed (%d)", (int)r);
+    return P2P_OK;
+}
+
 template <typename T>
-int launch_tc(const CUtensorMap& map, const TcParams& prm, dim3 grid, int smem, cudaStream_t st) {
+int launch_tc(const CUtensorMap& map, const CUtensorMap& ymap, const TcParams& prm, dim3 grid, int smem,
+              cudaStream_t st) {
     if (int e = allow_smem((const void*)spmm_tc_kernel<T>, smem, "p2p_spmm_tc")) return e;
     // A programmatic dependent of the stream's previous kernel (the kernel waits for it before loading x), and with
     // split columns reduced in clusters, the n_split CTAs of a row tile as one cluster (grid.y == n_split).
@@ -696,7 +739,7 @@ int launch_tc(const CUtensorMap& map, const TcParams& prm, dim3 grid, int smem, 
     cfg.stream = st;
     cfg.attrs = attr;
     cfg.numAttrs = prm.cluster ? 2 : 1;
-    if (cudaLaunchKernelEx(&cfg, spmm_tc_kernel<T>, map, prm) != cudaSuccess) return launch_status("p2p_spmm_tc");
+    if (cudaLaunchKernelEx(&cfg, spmm_tc_kernel<T>, map, ymap, prm) != cudaSuccess) return launch_status("p2p_spmm_tc");
     return launch_status("p2p_spmm_tc");
 }
 
@@ -865,12 +908,18 @@ extern "C" int p2p_spmm_tc(const void* x, int dtype, int64_t tokens, int64_t col
         prm.items = nullptr;
         prm.item_bound_tiles = prm.item_bound_rows = 0;
         prm.item_row_tiles = 0;
-        CUtensorMap map;
+        CUtensorMap map, ymap;
         const void* xt = reinterpret_cast<const char*>(x) + t0 * ldx * elem;
         if (int e = encode_x_map(&map, xt, dtype, tn, cols, ldx, pl.box_rows)) return e;
+        // y through TMA stores when unsplit and aligned (rows of y start on 16 bytes); the staged tile is
+        // n_total x 128 x 2 bytes of the rings
+        prm.y_tma = pl.n_split == 1 && ldy % 8 == 0 && aligned16(prm.y) &&
+                    (int64_t)pl.n_total * tc::kTileRows * 2 <= (int64_t)pl.a_slots * kASlotBytes;
+        ymap = map;
+        if (prm.y_tma && encode_y_map(&ymap, prm.y, dtype, tn, rows, ldy, pl.box_rows) != P2P_OK) prm.y_tma = 0;
         const dim3 grid((unsigned)row_tiles, (unsigned)pl.n_split);
-        if (int e = dtype == P2P_BF16 ? launch_tc<__nv_bfloat16>(map, prm, grid, pl.smem, st)
-                                      : launch_tc<__half>(map, prm, grid, pl.smem, st))
+        if (int e = dtype == P2P_BF16 ? launch_tc<__nv_bfloat16>(map, ymap, prm, grid, pl.smem, st)
+                                      : launch_tc<__half>(map, ymap, prm, grid, pl.smem, st))
             return e;
     }
     return P2P_OK;
@@ -925,12 +974,13 @@ extern "C" int p2p_spmm_tc_grouped(const void* x, int dtype, int64_t x_rows, int
     prm.item_bound_tiles = layout_row_tiles;
     prm.item_bound_rows = x_rows;
     prm.item_row_tiles = (int)item_row_tiles;
+    prm.y_tma = 0;
     prm.cluster = 0;
     CUtensorMap map;
     if (int e = encode_x_map(&map, x, dtype, x_rows, cols, ldx, pl.box_rows)) return e;
     const dim3 grid((unsigned)item_row_tiles, (unsigned)n_items);
-    return dtype == P2P_BF16 ? launch_tc<__nv_bfloat16>(map, prm, grid, pl.smem, st)
-                             : launch_tc<__half>(map, prm, grid, pl.smem, st);
+    return dtype == P2P_BF16 ? launch_tc<__nv_bfloat16>(map, map, prm, grid, pl.smem, st)
+                             : launch_tc<__half>(map, map, prm, grid, pl.smem, st);
 }
 
 extern "C" int p2p_spmm_tc_status(int reset, void* stream) {
