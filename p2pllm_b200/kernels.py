@@ -13,8 +13,10 @@ _workspaces: dict = {}
 
 
 def _workspace(device: torch.device, nbytes: int, purpose: str = "sumsq") -> torch.Tensor:
-    """A zeroed scratch buffer of at least nbytes per device and purpose (the kernels leave it zeroed again)."""
-    key = (device.type, device.index, purpose)
+    """A zeroed scratch buffer of at least nbytes per device, purpose and stream (the kernels leave it zeroed again;
+    launches on one stream run in order, so they can share it, while launches on two streams may overlap and must
+    not)."""
+    key = (device.type, device.index, purpose, torch.cuda.current_stream(device).cuda_stream)
     ws = _workspaces.get(key)
     if ws is None or ws.numel() < nbytes:
         ws = torch.zeros(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
