@@ -168,6 +168,19 @@ def check_idx(idx: torch.Tensor, cols: int) -> None:
          stream_of(idx))
 
 
+def _out(out: torch.Tensor | None, shape: tuple, like: torch.Tensor, whole: bool = False) -> torch.Tensor:
+    """A caller's output tensor, checked (shape, dtype, device, unit column stride; `whole`: contiguous), or a new one."""
+    if out is None:
+        return torch.empty(shape, dtype=like.dtype, device=like.device)
+    require_cuda(out)
+    if tuple(out.shape) != tuple(shape) or out.dtype != like.dtype or out.device != like.device:
+        raise P2PError(f"out of {tuple(out.shape)} {out.dtype} on {out.device}, wanted {tuple(shape)} {like.dtype} "
+                       f"on {like.device}")
+    if (whole and not out.is_contiguous()) or (out.dim() and out.stride(-1) != 1 and out.numel()):
+        raise P2PError(f"out of strides {out.stride()} is not laid out as the kernel writes it")
+    return out
+
+
 def spmm_rows(x: torch.Tensor, blocks: list, cols: int, out_rows: int, out: torch.Tensor | None = None) -> torch.Tensor:
     """y [tokens, out_rows] = x [tokens, cols] times row blocks (CUDA cores). blocks: (row0, values, idx | None) with
     values [rows, k] (k == cols when idx is None: a dense block). Replaces p2p/compact.cu:265-278 for row layouts."""
@@ -176,8 +189,7 @@ def spmm_rows(x: torch.Tensor, blocks: list, cols: int, out_rows: int, out: torc
         raise P2PError(f"x of {tuple(x.shape)} does not have {cols} columns")
     if x.stride(1) != 1:
         x = x.contiguous()
-    if out is None:
-        out = torch.empty(x.shape[0], out_rows, dtype=x.dtype, device=x.device)
+    out = _out(out, (x.shape[0], out_rows), x)
     table = (_lib.RowBlock * len(blocks))()
     idx_bytes = 2
     for i, (row0, v, ix) in enumerate(blocks):
@@ -238,8 +250,7 @@ def spmm_tc(x: torch.Tensor, words: torch.Tensor, seg: torch.Tensor, rows: int, 
         x = x.contiguous()
         if x.data_ptr() % 16:
             x = x.clone()
-    if out is None:
-        out = torch.empty(x.shape[0], rows, dtype=x.dtype, device=x.device)
+    out = _out(out, (x.shape[0], rows), x)
     lib = _lib.load()
     need = lib.p2p_spmm_tc_workspace(rows, cols, x.shape[0])
     ws = _workspace(x.device, need, "spmm_tc") if need else None
@@ -275,7 +286,7 @@ def combine(parts: list, h: torch.Tensor, h_copy: torch.Tensor, out: torch.Tenso
     """h' = l_0(h) + sum_mid dtype(l_k(h) - h) + dtype(l_last(h~) - h~), fp32 sums (p2p/replica.py:81-85)."""
     parts = _same(parts, h)
     h, h_copy = _same([h, h_copy], h)
-    out = torch.empty_like(h) if out is None else out
+    out = _out(out, tuple(h.shape), h, whole=True)
     call("p2p_combine", _ptr_array(parts), len(parts), ptr(h), ptr(h_copy), ptr(out), dtype_code(h), h.numel(),
          stream_of(h))
     return out
@@ -284,7 +295,7 @@ def combine(parts: list, h: torch.Tensor, h_copy: torch.Tensor, out: torch.Tenso
 def sum_parts(parts: list, out: torch.Tensor | None = None) -> torch.Tensor:
     """dtype(sum of the parts in fp32, member order) (p2p/route.py:825-831)."""
     parts = _same(parts, parts[0])
-    out = torch.empty_like(parts[0]) if out is None else out
+    out = _out(out, tuple(parts[0].shape), parts[0], whole=True)
     call("p2p_sum_parts", _ptr_array(parts), len(parts), ptr(out), dtype_code(out), out.numel(), stream_of(out))
     return out
 
@@ -292,6 +303,6 @@ def sum_parts(parts: list, out: torch.Tensor | None = None) -> torch.Tensor:
 def member_part(y: torch.Tensor, x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
     """dtype(float(y) - float(x)) (p2p/route.py:1268-1274)."""
     y, x = _same([y, x], y)
-    out = torch.empty_like(y) if out is None else out
+    out = _out(out, tuple(y.shape), y, whole=True)
     call("p2p_member_part", ptr(y), ptr(x), ptr(out), dtype_code(y), y.numel(), stream_of(y))
     return out

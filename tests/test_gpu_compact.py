@@ -176,3 +176,22 @@ def test_expand_experts_and_compact_moe_match_a_reference_moe():
     got = compact.CompactMoE(Method(), blocks).apply(empty, d)
     assert torch.equal(got, Method().apply(dense, d))
     assert all(empty._parameters[name].numel() == 0 for name in pruned)
+
+
+def test_out_is_checked_and_may_be_a_column_slice():
+    """A caller's out: the wrong shape or dtype is refused; a column slice of a wider buffer is written in place."""
+    (w, mask), _, _ = _pruned(256, 512, 30, torch.bfloat16, seed=4)
+    for layout in ("tc", "rows"):
+        tiles = compact.Tiles([("sparse", *compact.pack(w, mask), 512)], layout=layout)
+        x = torch.randn(17, 512, device="cuda").bfloat16()
+        wide = torch.full((17, 400), 7.0, device="cuda").bfloat16()
+        got = tiles(x, out=wide[:, 16:272])
+        assert got.data_ptr() == wide[:, 16:272].data_ptr()
+        assert torch.equal(wide[:, 16:272], tiles(x))
+        assert (wide[:, :16] == 7).all() and (wide[:, 272:] == 7).all()
+        with pytest.raises(P2PError, match="wanted"):
+            tiles(x, out=torch.empty(17, 255, device="cuda", dtype=torch.bfloat16))
+        with pytest.raises(P2PError, match="wanted"):
+            tiles(x, out=torch.empty(17, 256, device="cuda", dtype=torch.float16))
+        with pytest.raises(P2PError, match="strides"):
+            tiles(x, out=torch.empty(256, 17, device="cuda", dtype=torch.bfloat16).T)
