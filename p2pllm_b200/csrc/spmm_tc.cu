@@ -43,6 +43,7 @@ constexpr int kASlotBytes = kATileBytes;                           // 1 KiB alig
 constexpr int kMaxASlots = 12;                                     // A tiles in flight (even: the groups alternate)
 constexpr int kMaxXSlots = 4;                                      // x tiles in flight
 constexpr int kChunks = 4;                                         // 16-byte loads a lane holds for one tile
+constexpr int kL2Ahead = 8;                                        // tiles between a segment's L2 prefetch and its loads
 constexpr uint32_t kOffsetMask = 0x3FFEu;                         // an even byte offset inside the 16 KiB tile
 constexpr int kMaxTilesPerCta = 256;                               // segment offsets and headers staged in smem
 // Dynamic shared memory: the 227 KiB a block may hold, less the static offsets and headers and a few scalars.
@@ -249,6 +250,11 @@ __device__ __forceinline__ void load_piece(const uint32_t* words, int lo, int hi
     }
 }
 
+// A hint: bring `bytes` (a multiple of 16, 16-byte aligned) of global memory into L2, with no completion to wait on.
+__device__ __forceinline__ void l2_prefetch(const void* src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
 __device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, uint32_t src, int c0, int c1) {
     asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
                      reinterpret_cast<uint64_t>(map)),
@@ -256,7 +262,8 @@ __device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, uint32_t sr
                  : "memory");
 }
 
-template <typename T>
+// kL2: the launch prefetches segments into L2 ahead of the register loads (few tokens; see the expanders).
+template <typename T, bool kL2>
 __global__ void __launch_bounds__(kTcThreads, 1)
     spmm_tc_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_y, TcParams p) {
     extern __shared__ uint8_t smem_raw[];
@@ -410,10 +417,20 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         const uint32_t* wbase = p.words + s_offs[0];        // 16-byte aligned: segments start on 4-word boundaries
         uint4 b0[kChunks], b1[kChunks], b2[kChunks];
         int l0 = 0, h0 = 0, l1 = 0, h1 = 0, l2 = 0, h2 = 0;
+        // With few tokens (the loads, not the tensor cores or the x tiles, set the pace), each group also pulls its tile
+        // kL2Ahead tiles past the one it loads into L2 (one bulk prefetch a segment), so the register loads, a few
+        // tiles later, wait on L2 rather than HBM. (Measured on gate_up, 2 x 14336 x 4096: 6% faster at 17 tokens,
+        // 2% slower at 272, where the x tiles and the MMAs already share the L2 traffic.)
+        auto prefetch = [&](int j) {
+            if (kL2 && wg == 0 && lane == 0 && j < nk)
+                l2_prefetch(p.words + s_offs[j], (uint32_t)(4 * (s_offs[j + 1] - s_offs[j])));
+        };
+        for (int j = grp; j < kL2Ahead + 2 * kGroups && j < nk; j += kGroups) prefetch(j);
         auto fetch = [&](int i, uint4 (&b)[kChunks], int& lo, int& hi) {
             if (i < nk) {
                 warp_piece(s_offs, hdr, i, wg, lo, hi);
                 load_piece(wbase, lo, hi, lane, b);
+                prefetch(i + kL2Ahead + 2 * kGroups);
             }
         };
         // Zeroing a slot's rows: with three or more slots a group, the group's next slot is zeroed while this tile is
@@ -722,7 +739,10 @@ int encode_y_map(CUtensorMap* map, void* y, int dtype, int64_t tokens, int64_t r
 template <typename T>
 int launch_tc(const CUtensorMap& map, const CUtensorMap& ymap, const TcParams& prm, dim3 grid, int smem,
               cudaStream_t st) {
-    if (int e = allow_smem((const void*)spmm_tc_kernel<T>, smem, "p2p_spmm_tc")) return e;
+    // Few tokens: the variant that prefetches the segments into L2.
+    const bool l2 = prm.n_total <= 64;
+    auto kernel = l2 ? spmm_tc_kernel<T, true> : spmm_tc_kernel<T, false>;
+    if (int e = allow_smem((const void*)kernel, smem, "p2p_spmm_tc")) return e;
     // A programmatic dependent of the stream's previous kernel (the kernel waits for it before loading x), and with
     // split columns reduced in clusters, the n_split CTAs of a row tile as one cluster (grid.y == n_split).
     cudaLaunchConfig_t cfg = {};
@@ -739,7 +759,7 @@ int launch_tc(const CUtensorMap& map, const CUtensorMap& ymap, const TcParams& p
     cfg.stream = st;
     cfg.attrs = attr;
     cfg.numAttrs = prm.cluster ? 2 : 1;
-    if (cudaLaunchKernelEx(&cfg, spmm_tc_kernel<T>, map, ymap, prm) != cudaSuccess) return launch_status("p2p_spmm_tc");
+    if (cudaLaunchKernelEx(&cfg, kernel, map, ymap, prm) != cudaSuccess) return launch_status("p2p_spmm_tc");
     return launch_status("p2p_spmm_tc");
 }
 
@@ -772,8 +792,10 @@ int max_clusters(const TcPlan& pl, int n_split) {
     auto it = known.find(key);
     if (it != known.end()) return it->second;
     int clusters = 0;
-    if (allow_smem((const void*)spmm_tc_kernel<__nv_bfloat16>, pl.smem, "p2p_spmm_tc") == P2P_OK &&
-        allow_smem((const void*)spmm_tc_kernel<__half>, pl.smem, "p2p_spmm_tc") == P2P_OK) {
+    if (allow_smem((const void*)spmm_tc_kernel<__nv_bfloat16, false>, pl.smem, "p2p_spmm_tc") == P2P_OK &&
+        allow_smem((const void*)spmm_tc_kernel<__nv_bfloat16, true>, pl.smem, "p2p_spmm_tc") == P2P_OK &&
+        allow_smem((const void*)spmm_tc_kernel<__half, false>, pl.smem, "p2p_spmm_tc") == P2P_OK &&
+        allow_smem((const void*)spmm_tc_kernel<__half, true>, pl.smem, "p2p_spmm_tc") == P2P_OK) {
         cudaLaunchConfig_t cfg = {};
         cudaLaunchAttribute attr[1];
         attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -785,7 +807,8 @@ int max_clusters(const TcPlan& pl, int n_split) {
         cfg.dynamicSmemBytes = pl.smem;
         cfg.attrs = attr;
         cfg.numAttrs = 1;
-        if (cudaOccupancyMaxActiveClusters(&clusters, spmm_tc_kernel<__nv_bfloat16>, &cfg) != cudaSuccess) clusters = 0;
+        if (cudaOccupancyMaxActiveClusters(&clusters, spmm_tc_kernel<__nv_bfloat16, false>, &cfg) != cudaSuccess)
+            clusters = 0;
         cudaGetLastError();                                  // a refusal here only means: use the workspace path
     }
     known[key] = clusters;
