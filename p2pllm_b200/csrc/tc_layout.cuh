@@ -8,10 +8,9 @@
 //                 0 .. 8j + 7, so 16-row slice s owns entries [header[2s-1], header[2s+1]) (header[-1] = 0) and
 //                 header[15] is the segment's entry count
 //   words 8..     one word per kept weight, slice after slice. Within a slice the order is free (every word
-//                 carries its place); the builder deals the entries, in (rank within their shared-memory bank, bank)
-//                 order, to the GEMM's store rounds (tiles.cu, bank_order_kernel), so the 32 entries one store writes
-//                 mostly differ in bank (about 40% fewer shared-memory wavefronts than row order at keep 36). Each
-//                 word:
+//                 carries its place); the builder fills the GEMM's store rounds (tiles.cu, bank_order_kernel) so
+//                 that the entries one store writes fall in as few passes of shared-memory banks as the slice
+//                 allows, round by round. Each word:
 //                   bits 31..16  the value (bf16 or f16 bits)
 //                   bits 13..0   the byte offset of that weight in the 128 x 64 tile as the tensor cores read it:
 //                                row * 128 + ((2 * column) ^ ((row % 8) << 4)), the 128-byte swizzle (always even)

@@ -181,9 +181,11 @@ __global__ void __launch_bounds__(kBuildBlock) fill_kernel(Blocks bl, int64_t ro
 // A + 4 (l + 32 c) .. + 3, and store round 4 c + j writes word j of every lane's load c (rounds 0..15, the first 512
 // words from A); past those, round 16 + m stores words A + 512 + 32 m + l. A store takes one pass per entry on its
 // busiest shared-memory bank (bits 2..6 of the entry's byte offset), so the entries of one round should differ in
-// bank. Entries are ranked within their bank (in their current order), put in (rank, bank) order -- bank round r holds
-// one entry of every bank with more than r entries -- and dealt in that order to the store rounds' positions, round
-// by round, lane by lane. One warp a slice (16 rows x 64 columns: at most 32 entries a bank, 1024 in all).
+// bank. Round by round, the places are filled greedily: the fewest entries of any one bank the remaining entries allow
+// (every bank gives up to m - 1, the banks with the most left give the m-th ones), which also keeps the banks' counts
+// level for the later rounds. (Dealing entries in (rank within bank, bank) order instead lets the rounds drift off the
+// bank boundaries once banks run out, and costs about half again as many store passes at keep 36.) One warp a slice
+// (16 rows x 64 columns: at most 32 entries a bank, 1024 in all).
 constexpr int kOrderWarps = 4;
 constexpr int kSliceMax = 16 * tc::kTileCols;
 constexpr int kStoreRounds = 16 + (kSliceMax + 3 - 512 + 31) / 32;   // rounds over the slice's words from A
@@ -204,13 +206,12 @@ __device__ __forceinline__ void store_round(int pr, int& round, int& lane) {
 __global__ void __launch_bounds__(kOrderWarps * 32) bank_order_kernel(const int64_t* __restrict__ seg, int64_t n_seg,
                                                                       uint32_t* __restrict__ words) {
     __shared__ uint32_t buf[kOrderWarps][kSliceMax];
-    __shared__ uint32_t byrank[kOrderWarps][kSliceMax];
+    __shared__ uint32_t byrank[kOrderWarps][kSliceMax];        // the entries grouped by bank
     __shared__ uint8_t rk[kOrderWarps][kSliceMax];
     __shared__ int cnt[kOrderWarps][32];
-    __shared__ uint32_t rmask[kOrderWarps][32];
-    __shared__ int rpre[kOrderWarps][32];
-    __shared__ int llo[kOrderWarps][kStoreRounds + 1];
-    __shared__ int rstart[kOrderWarps][kStoreRounds + 1];
+    __shared__ int rpre[kOrderWarps][32];                       // where each bank's entries start in byrank
+    __shared__ int llo[kOrderWarps][kStoreRounds + 1];          // a round's first lane in the slice
+    __shared__ int rstart[kOrderWarps][kStoreRounds + 1];       // and its lanes in the slice
     const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const unsigned below = (1u << lane) - 1u;
     const int64_t n_work = n_seg * (8 / kOrderWarps);
@@ -243,30 +244,22 @@ __global__ void __launch_bounds__(kOrderWarps * 32) bank_order_kernel(const int6
                 if (ok && before == 0) cnt[w][b] += __popc(peers);
                 __syncwarp();
             }
-            // bank round r: the banks with more than r entries, and where it starts in (rank, bank) order
+            // the entries grouped by bank (lane b: bank b), each bank's in their current order
             const int cb = cnt[w][lane];
-            uint32_t mine = 0;
-            for (int r = 0; r < 32; ++r) {
-                const uint32_t m = __ballot_sync(0xffffffffu, cb > r);
-                if (lane == r) mine = m;
-            }
-            const int nr = __popc(mine);
-            int incl = nr;
+            int start = cb;
             for (int d = 1; d < 32; d <<= 1) {
-                const int t = __shfl_up_sync(0xffffffffu, incl, d);
-                if (lane >= d) incl += t;
+                const int t = __shfl_up_sync(0xffffffffu, start, d);
+                if (lane >= d) start += t;
             }
-            rmask[w][lane] = mine;
-            rpre[w][lane] = incl - nr;
+            start -= cb;
+            rpre[w][lane] = start;
             __syncwarp();
             for (int e = lane; e < n; e += 32) {
                 const uint32_t v = buf[w][e];
-                const int b = (int)((v >> 2) & 31u), r = rk[w][e];
-                byrank[w][rpre[w][r] + __popc(rmask[w][r] & ((1u << b) - 1u))] = v;
+                byrank[w][rpre[w][(v >> 2) & 31u] + rk[w][e]] = v;
             }
-            // the store rounds: the lanes [llo, lhi) of round R that fall in the slice, and where R starts
+            // the store rounds: the lanes [llo, lhi) of round R that fall in the slice
             if (lane == 0) {
-                int run = 0;
                 for (int R = 0; R < kStoreRounds; ++R) {
                     int lo_l, hi_l;
                     if (R < 16) {
@@ -279,15 +272,42 @@ __global__ void __launch_bounds__(kOrderWarps * 32) bank_order_kernel(const int6
                         hi_l = min(32, lo_rel + n - b0);
                     }
                     llo[w][R] = lo_l;
-                    rstart[w][R] = run;
-                    run += hi_l > lo_l ? hi_l - lo_l : 0;
+                    rstart[w][R] = hi_l > lo_l ? hi_l - lo_l : 0;   // the round's entries
                 }
             }
             __syncwarp();
-            for (int pr = lo_rel + lane; pr < lo_rel + n; pr += 32) {
-                int R, l;
-                store_round(pr, R, l);
-                base[pr] = byrank[w][rstart[w][R] + l - llo[w][R]];
+            // Round by round, the fewest entries of any one bank: with cap places, the smallest m with
+            // sum_b min(rem_b, m) >= cap; every bank gives min(rem_b, m - 1), and the banks with the most left give
+            // the m-th entries still needed (ties to the lower bank), which keeps the counts level for later rounds.
+            int rem = cb, taken = 0;
+            for (int R = 0; R < kStoreRounds; ++R) {
+                const int cap = rstart[w][R];
+                if (cap == 0) continue;
+                int m = 1;
+                while (__reduce_add_sync(0xffffffffu, min(rem, m)) < cap) ++m;
+                const int base_take = min(rem, m - 1);
+                const int extra = cap - __reduce_add_sync(0xffffffffu, base_take);
+                const bool cand = rem >= m;
+                int rank = 0;
+                for (int o = 0; o < 32; ++o) {
+                    const int ro = __shfl_sync(0xffffffffu, rem, o);
+                    const bool co = __shfl_sync(0xffffffffu, cand ? 1 : 0, o) != 0;
+                    rank += (co && (ro > rem || (ro == rem && o < lane))) ? 1 : 0;
+                }
+                const int take = base_take + ((cand && rank < extra) ? 1 : 0);
+                int off = take;
+                for (int d = 1; d < 32; d <<= 1) {
+                    const int t = __shfl_up_sync(0xffffffffu, off, d);
+                    if (lane >= d) off += t;
+                }
+                off -= take;
+                for (int q = 0; q < take; ++q) {
+                    const int l = llo[w][R] + off + q;                    // the round's lane, hence its word
+                    const int pr = R < 16 ? 128 * (R >> 2) + 4 * l + (R & 3) : 512 + 32 * (R - 16) + l;
+                    base[pr] = byrank[w][start + taken + q];
+                }
+                rem -= take;
+                taken += take;
             }
         }
         __syncwarp();

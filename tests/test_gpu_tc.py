@@ -35,7 +35,9 @@ def _check(got, want, dtype):
 def test_layout_decodes_to_the_selection(rows, cols, keep):
     """Every segment: a header of cumulative 8-row-group counts, then one word per kept weight holding its value and
     its swizzled byte offset in the 128 x 64 tile, 16-row slice after slice, each slice dealt to the GEMM's store rounds
-    in bank order (by rank within its shared-memory bank, then bank); decoded, the layout is the selection, bit for bit."""
+    so that each store round holds as few entries of any one shared-memory bank as the slice's remaining entries allow
+    (the smallest m with sum over banks of min(left, m) >= the round's places); decoded, the layout is the selection,
+    bit for bit."""
     values, idx = _module(rows, cols, keep)
     words, seg, cap = kernels.tiles_build([(0, values, idx)], cols)
     w = words.cpu().numpy().view(np.uint32)
@@ -60,19 +62,19 @@ def test_layout_decodes_to_the_selection(rows, cols, keep):
         bounds = np.concatenate([[0], hdr[1::2]])                   # slice s: [hdr[2s-1], hdr[2s+1])
         assert ((bounds[sl] <= e) & (e < bounds[sl + 1])).all()
         bank = (off >> 2) & 31
-        for q in range(8):                                          # read in store-round order, (rank, bank) ascends
+        for q in range(8):                                          # each slice's store rounds, in order
             first = s[i] + 8 + bounds[q]
             pr = np.arange(bounds[q + 1] - bounds[q]) + (first & 3)  # places above the 4-word boundary
             rnd = np.where(pr < 512, (pr >> 7) * 4 + (pr & 3), 16 + ((pr - 512) >> 5))
-            ln = np.where(pr < 512, (pr & 127) >> 2, (pr - 512) & 31)
-            b = bank[bounds[q]:bounds[q + 1]][np.lexsort((ln, rnd))]
-            seen_b = np.zeros(32, np.int64)
-            rank = np.zeros(len(b), np.int64)
-            for j, x in enumerate(b):
-                rank[j] = seen_b[x]
-                seen_b[x] += 1
-            key = rank * 32 + b
-            assert (np.diff(key) > 0).all()
+            b = bank[bounds[q]:bounds[q + 1]]
+            left = np.bincount(b, minlength=32)
+            for R in np.unique(rnd):
+                here = np.bincount(b[rnd == R], minlength=32)
+                m = 1
+                while np.minimum(left, m).sum() < here.sum():
+                    m += 1
+                assert here.max() == m
+                left -= here
         np.add.at(seen, (rt * 128 + r, ct * 64 + c), 1)
         got[rt * 128 + r, ct * 64 + c] = (ents >> 16).astype(np.uint16)
     assert cap == int(np.diff(s).max())
