@@ -40,12 +40,14 @@ def shrink(layer: nn.Module, keep: dict, sums: dict, i: int, form: str = "dense"
     c.__dict__.pop("forward", None)
     modules = dict(c.named_modules())
     blocks: dict = {}
+    pruned: set = set()                  # module tensors with a projection below keep 100; the rest stay shared
     for name, p in family.projections(layer).items():
         module = modules[p.path]
         w = getattr(module, p.param).data
         if keep[name] >= 100:
             blocks.setdefault((p.path, p.param), []).append((p.rows, ("dense", w[p.rows])))
             continue
+        pruned.add((p.path, p.param))
         norms = wanda.channel_norms(sums[i, p.key], w, family.split_group(module, p))
         if form == "dense":
             blocks.setdefault((p.path, p.param), []).append((p.rows, ("dense", wanda.prune(w[p.rows], keep[name], norms))))
@@ -53,8 +55,10 @@ def shrink(layer: nn.Module, keep: dict, sums: dict, i: int, form: str = "dense"
             values, idx = wanda.select(w[p.rows], keep[name], norms)
             blocks.setdefault((p.path, p.param), []).append((p.rows, ("compact", values, idx, w.shape[-1])))
     for (path, param), parts in blocks.items():
+        if (path, param) not in pruned:
+            continue
         module = modules[path]
-        parts = [b for _, b in sorted(parts, key=lambda rb: rb[0].start or 0)]
+        parts = [b for _, b in sorted(parts, key=lambda rb: _first_row(rb[0]))]
         if form == "dense" or param != "weight":
             setattr(module, param, nn.Parameter(torch.cat([compact.expand(b) for b in parts], dim=-2),
                                                 requires_grad=False))
@@ -64,6 +68,12 @@ def shrink(layer: nn.Module, keep: dict, sums: dict, i: int, form: str = "dense"
             module.quant_method = method
             module.forward = functools.partial(_compact_forward, method, bias)
     return c
+
+
+def _first_row(rows) -> int:
+    """Where a projection starts in its module's tensor (routed experts: the slice after the expert axis)."""
+    rows = rows[-1] if isinstance(rows, tuple) else rows
+    return rows.start or 0
 
 
 def _compact_forward(method, bias, x):

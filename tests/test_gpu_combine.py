@@ -96,3 +96,49 @@ def test_group_install_matches_the_formula():
                 assert (got.float() - want.float()).norm() / want.float().norm() <= 1e-2
         replica.remove(layers)
         assert torch.equal(layers[1](h), _Block.forward(layers[1], h))
+
+
+def test_shrink_prunes_routed_experts_per_projection():
+    """p2p/replica.py:34-49 on a layer with routed experts: gate, up and down of every expert pruned on their own
+    (per-expert channel norms from [E, C] sums), the rest of the layer shared; the compact form expands experts."""
+    import torch.nn as nn
+
+    from p2pllm_b200 import wanda
+
+    E, R, H = 4, 32, 64
+    g = torch.Generator(device="cuda").manual_seed(0)
+
+    class Experts(nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.w13_weight = nn.Parameter(torch.randn(E, 2 * R, H, generator=g, device="cuda").bfloat16(), False)
+            self.w2_weight = nn.Parameter(torch.randn(E, H, R, generator=g, device="cuda").bfloat16(), False)
+
+    class Mlp(nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.experts = Experts()
+            self.down_proj = nn.Linear(R, H, bias=False, device="cuda", dtype=torch.bfloat16)
+            self.gate_proj = nn.Linear(H, R, bias=False, device="cuda", dtype=torch.bfloat16)
+
+    class Layer(nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.mlp = Mlp()
+
+    layer = Layer()
+    sums = {(0, "mlp.experts.w13_weight"): torch.rand(E, H, generator=g, device="cuda").double() + 0.1,
+            (0, "mlp.experts.w2_weight"): torch.rand(E, R, generator=g, device="cuda").double() + 0.1}
+    sums[0, "mlp.experts.w2_weight"][2] = 0                    # an expert no token reached: norms of one
+    keep = {"egate": 30, "eup": 50, "edown": 40, "down": 100, "gate": 100}
+    for form in ("dense", "compact"):
+        c = replica.shrink(layer, keep, sums, 0, form=form)
+        w13, w2 = layer.mlp.experts.w13_weight, layer.mlp.experts.w2_weight
+        n13 = wanda.channel_norms(sums[0, "mlp.experts.w13_weight"], w13)
+        n2 = wanda.channel_norms(sums[0, "mlp.experts.w2_weight"], w2)
+        want13 = torch.cat([wanda.prune(w13[:, :R], 30, n13), wanda.prune(w13[:, R:], 50, n13)], dim=1)
+        assert torch.equal(c.mlp.experts.w13_weight, want13)
+        assert torch.equal(c.mlp.experts.w2_weight, wanda.prune(w2, 40, n2))
+        assert (c.mlp.experts.w13_weight != 0).sum() == E * R * (round(0.3 * H) + round(0.5 * H))
+        assert c.mlp.down_proj.weight is layer.mlp.down_proj.weight   # keep 100: shared, untouched
+        assert layer.mlp.experts.w13_weight is w13 and torch.equal(w13, layer.mlp.experts.w13_weight)
