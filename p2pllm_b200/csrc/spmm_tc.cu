@@ -408,15 +408,15 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         // Expanders: group `grp` builds the dense 128 x 64 tiles of every other column tile in shared memory. Warp wg
         // owns rows 16 wg .. 16 wg + 15 of the tile: it zeroes them and writes their entries at the offsets the words
         // carry, apart from the other warps (no barrier between them), then arrives on the slot's barrier. The words
-        // come straight from HBM into registers in 16-byte loads, two of the group's tiles ahead (a ring of three
-        // register buffers), never through shared memory.
+        // come straight from HBM into registers in 16-byte loads, one of the group's tiles ahead (two register
+        // buffers), never through shared memory.
         const int grp = warp / kGroupWarps, wg = warp % kGroupWarps;
         const uint16_t* hdr = reinterpret_cast<const uint16_t*>(s_hdr);
         int s = grp % SA;
         uint32_t ph = 0;
         const uint32_t* wbase = p.words + s_offs[0];        // 16-byte aligned: segments start on 4-word boundaries
-        uint4 b0[kChunks], b1[kChunks], b2[kChunks];
-        int l0 = 0, h0 = 0, l1 = 0, h1 = 0, l2 = 0, h2 = 0;
+        uint4 b0[kChunks], b1[kChunks];
+        int l0 = 0, h0 = 0, l1 = 0, h1 = 0;
         // With few tokens (the loads, not the tensor cores or the x tiles, set the pace), each group also pulls its tile
         // kL2Ahead tiles past the one it loads into L2 (one bulk prefetch a segment), so the register loads, a few
         // tiles later, wait on L2 rather than HBM. (Measured on gate_up, 2 x 14336 x 4096: 6% faster at 17 tokens,
@@ -488,17 +488,15 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             advance(s, ph, kGroups, SA);
         };
         constexpr int G = kGroups;
+        // Two register buffers: the group's next tile loads while this one is written. (A third buffer, two tiles
+        // ahead, measured 1-1.5% slower on the bench layer at both token counts: the loads are not what waits.)
         fetch(grp, b0, l0, h0);
-        fetch(grp + G, b1, l1, h1);
-        for (int i = grp; i < nk; i += 3 * G) {
-            fetch(i + 2 * G, b2, l2, h2);
+        for (int i = grp; i < nk; i += 2 * G) {
+            fetch(i + G, b1, l1, h1);
             expand(i, b0, l0, h0);
             if (i + G >= nk) break;
-            fetch(i + 3 * G, b0, l0, h0);
+            fetch(i + 2 * G, b0, l0, h0);
             expand(i + G, b1, l1, h1);
-            if (i + 2 * G >= nk) break;
-            fetch(i + 4 * G, b1, l1, h1);
-            expand(i + 2 * G, b2, l2, h2);
         }
 
         // Epilogue: D[row, token] out of TMEM. Warp w reads lanes 32 (w % 4) .. + 31, every other 16-column chunk.
