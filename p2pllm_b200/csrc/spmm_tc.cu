@@ -7,15 +7,17 @@
 //
 //   warp 16 (producer)  per column tile: TMA of the x tile [tokens x 64] (128-byte swizzle) into the x ring, one
 //                       producer lane per ring slot.
-//   warps 0-15 (expand) two groups of 8 warps take alternate column tiles. A group zeroes a 128 x 64 bf16 tile in the
-//                       A ring (each warp 16 rows), meets at a named barrier, and each warp writes its piece of the
-//                       segment's words at the swizzled byte offsets they carry. The words come straight from HBM into
-//                       registers (coalesced, read one tile ahead), never through shared memory.
-//   warp 17 (MMA)       one elected thread issues tcgen05.mma (M = 128, N = tokens rounded to 16, K = 16 a step)
-//                       with the accumulator D[128 x N] fp32 in TMEM; tcgen05.commit frees both rings' slots.
-//   warps 0-15 (epilogue) tcgen05.ld D out of TMEM, round, and write y[t, row] (coalesced along rows), or write fp32
-//                       partials when the columns are split; the last CTA of a row tile adds the partials in split
-//                       order (a ticket per row tile), so results do not depend on scheduling.
+//   warps 0-15 (expand) two groups of 8 warps take alternate column tiles. Each warp zeroes its 16 rows of a
+//                       128 x 64 bf16 tile in the A ring and writes its slice of the segment's words at the swizzled
+//                       byte offsets they carry, with no barrier between warps. The words come straight from HBM into
+//                       registers (coalesced, 16 bytes a lane), never through shared memory.
+//   warps 17-18 (MMA)   one elected thread each issues tcgen05.mma (M = 128, N = tokens rounded to 16, K = 16 a step)
+//                       with fp32 accumulators in TMEM (alternate tiles, or halves of N past 256 tokens);
+//                       tcgen05.commit frees the rings' slots.
+//   warps 0-15 (epilogue) tcgen05.ld D out of TMEM, round, and write y[t, row] (through shared memory and TMA stores
+//                       when unsplit), or reduce the column splits: in a thread-block cluster over DSMEM, or through
+//                       fp32 partials and a ticket per row tile; both add in split order, so results do not depend on
+//                       scheduling.
 //
 // Every mbarrier wait is bounded (about 2 s of %globaltimer): past it the kernel records where it gave up in *err and
 // runs on, so a broken pipeline ends the kernel with an error status instead of hanging the GPU.
@@ -408,15 +410,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         // Expanders: group `grp` builds the dense 128 x 64 tiles of every other column tile in shared memory. Warp wg
         // owns rows 16 wg .. 16 wg + 15 of the tile: it zeroes them and writes their entries at the offsets the words
         // carry, apart from the other warps (no barrier between them), then arrives on the slot's barrier. The words
-        // come straight from HBM into registers in 16-byte loads, one of the group's tiles ahead (two register
-        // buffers), never through shared memory.
+        // come straight from HBM (or L2, see below) into registers in 16-byte loads, never through shared memory.
         const int grp = warp / kGroupWarps, wg = warp % kGroupWarps;
         const uint16_t* hdr = reinterpret_cast<const uint16_t*>(s_hdr);
         int s = grp % SA;
         uint32_t ph = 0;
         const uint32_t* wbase = p.words + s_offs[0];        // 16-byte aligned: segments start on 4-word boundaries
-        uint4 b0[kChunks], b1[kChunks];
-        int l0 = 0, h0 = 0, l1 = 0, h1 = 0;
+        uint4 b0[kChunks];
+        int l0 = 0, h0 = 0;
         // With few tokens (the loads, not the tensor cores or the x tiles, set the pace), each group also pulls its tile
         // kL2Ahead tiles past the one it loads into L2 (one bulk prefetch a segment), so the register loads, a few
         // tiles later, wait on L2 rather than HBM. (Measured on gate_up, 2 x 14336 x 4096: 6% faster at 17 tokens,
@@ -488,15 +489,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             advance(s, ph, kGroups, SA);
         };
         constexpr int G = kGroups;
-        // Two register buffers: the group's next tile loads while this one is written. (A third buffer, two tiles
-        // ahead, measured 1-1.5% slower on the bench layer at both token counts: the loads are not what waits.)
-        fetch(grp, b0, l0, h0);
-        for (int i = grp; i < nk; i += 2 * G) {
-            fetch(i + G, b1, l1, h1);
+        // Each tile's words are loaded just before they are written. Loading one or two of the group's tiles ahead
+        // into more register buffers measured 1-3% slower on the bench layer at 17 and 272 tokens: the other group's
+        // tile and the slot waits cover the loads, and the extra live registers cost the scheduler more.
+        for (int i = grp; i < nk; i += G) {
+            fetch(i, b0, l0, h0);
             expand(i, b0, l0, h0);
-            if (i + G >= nk) break;
-            fetch(i + 2 * G, b0, l0, h0);
-            expand(i + G, b1, l1, h1);
         }
 
         // Epilogue: D[row, token] out of TMEM. Warp w reads lanes 32 (w % 4) .. + 31, every other 16-column chunk.
