@@ -54,14 +54,21 @@ size_t p2p_sumsq_workspace(int64_t tokens, int64_t cols, int dtype);
 int p2p_sumsq_cols(const void* x, int dtype, int64_t tokens, int64_t cols, int64_t ldx, double* sums,
                    void* workspace, size_t workspace_bytes, void* stream);
 
-/* p2p_sumsq_cols for callers that cannot allocate device memory: the same reduction (same rounding, deterministic),
- * with its scratch held inside the library in one fixed device array of 4 MiB + 4 KiB per GPU (kept until the process
- * exits) instead of a caller-provided workspace. It allocates nothing. For a calibration hook running inside a serving
- * engine that has already reserved its share of GPU memory (SGLang's static fraction for weights and the KV pool),
- * where a fresh allocation can fail or fragment what is left. cols <= 16,384 (P2P_EUNSUPPORTED above). The first call
- * on each device looks up the array's device address; make that first call before any stream capture. Every call
- * uses the same array: calls that overlap on the GPU (other streams, other host threads) race and must be ordered by
- * the caller. No counterpart in the reference (p2pLLM allocates through torch). */
+/* p2p_sumsq_cols for callers that cannot allocate device memory: the same reduction (deterministic, each column
+ * total rounded to fp32 once), with its scratch held inside the library in one fixed device array of 4 MiB + 4 KiB per
+ * GPU (kept until the process exits) instead of a caller-provided workspace. It allocates nothing. For a calibration
+ * hook running inside a serving engine that has already reserved its share of GPU memory (SGLang's static fraction for
+ * weights and the KV pool), where a fresh allocation can fail or fragment what is left. cols <= 16,384
+ * (P2P_EUNSUPPORTED above).
+ * Every call looks up the array's device address in the current context. With CUDA's lazy module loading the
+ * library's device module -- and with it the array -- is committed on a device the first time any of its kernels
+ * or this array is used there: make a first call (tokens = 1 is enough) before the engine reserves its memory, and
+ * before any stream capture. Every call uses the same array: calls that overlap on the GPU (other streams, other
+ * host threads) race and must be ordered by the caller.
+ * Rounding: when tokens x cols is large enough that p2p_sumsq_cols would split the rows into more slabs than the
+ * fixed array holds (more than 4 MiB / (8 cols) slabs), this call uses fewer, taller slabs, so the fp64 partials are
+ * added in another grouping; the column totals then agree with p2p_sumsq_cols to within one fp32 rounding of the
+ * total, and are still deterministic. No counterpart in the reference (p2pLLM allocates through torch). */
 int p2p_sumsq_cols_noalloc(const void* x, int dtype, int64_t tokens, int64_t cols, int64_t ldx, double* sums,
                            void* stream);
 
@@ -201,8 +208,17 @@ int p2p_moe_combine(const void* y, int dtype, int64_t ldy, const int64_t* where,
                     int k, int64_t hidden, void* out, int64_t ldo, void* stream);
 
 /* P2P_OK unless a p2p_spmm_tc launch since the last reset gave up waiting on its pipeline (then P2P_ECUDA, naming
- * the site); reset != 0 clears the flag. Syncs the stream. */
+ * the site); reset != 0 clears the flag. Syncs the stream. A launch that gives up issues no further loads or MMAs,
+ * drains what it issued and exits; its y is then undefined. */
 int p2p_spmm_tc_status(int reset, void* stream);
+
+/* Test of that give-up path: p2p_spmm_tc (one launch, tokens <= 512) in which every CTA withholds the x tile of local
+ * index hold_tile (never loads it), so the waits for it run out after wait_us (1 ms .. 2 s) of %globaltimer and the
+ * launch gives up; p2p_spmm_tc_status then reports the site. y is undefined. No counterpart in the reference (its
+ * kernel has no waits to bound). */
+int p2p_spmm_tc_withhold(const void* x, int dtype, int64_t tokens, int64_t cols, int64_t ldx, const uint32_t* words,
+                         const int64_t* seg, int64_t rows, int64_t seg_cap_words, void* y, int64_t ldy, void* workspace,
+                         size_t workspace_bytes, int64_t hold_tile, int64_t wait_us, void* stream);
 
 /* ------------------------------------------------------------------------------------------------------------------
  * (3) Group combine epilogue

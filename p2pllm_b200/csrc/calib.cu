@@ -7,8 +7,6 @@
 // meet in the workspace: each writes its fp64 partial there, and the last slab to finish (a ticket counter per strip)
 // adds the partials in slab order, rounds the column total to fp32 as the reference's fp32 sum does, and adds it to
 // the caller's fp64 sums. The result therefore does not depend on which block finishes first.
-#include <mutex>
-
 #include "common.cuh"
 
 namespace p2p {
@@ -247,23 +245,15 @@ constexpr size_t kNoAllocPartialBytes = 4u << 20;
 static __device__ __align__(256) unsigned char g_sumsq_scratch[kNoAllocTicketBytes + kNoAllocPartialBytes];
 
 namespace {
-std::mutex g_scratch_mutex;
-void* g_scratch_addr[64] = {nullptr};
-
-// The device address of g_sumsq_scratch on the current device, looked up once per device (the host-side name of a
-// __device__ array is only a stand-in, not an address a kernel may use).
+// The device address of g_sumsq_scratch in the current device's context (the host-side name of a __device__ array is
+// only a stand-in, not an address a kernel may use). Looked up on every call: once the module is loaded the lookup
+// is cheap, and a cached address would go stale if the context were torn down and created again.
 int scratch_address(void** out) {
-    int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return fail(P2P_ECUDA, "no current CUDA device");
-    std::lock_guard<std::mutex> lock(g_scratch_mutex);
-    if (!g_scratch_addr[dev]) {
-        void* ptr = nullptr;
-        const cudaError_t e = cudaGetSymbolAddress(&ptr, g_sumsq_scratch);
-        if (e != cudaSuccess || !ptr)
-            return fail(P2P_ECUDA, "p2p_sumsq_cols_noalloc: scratch address lookup failed: %s", cudaGetErrorString(e));
-        g_scratch_addr[dev] = ptr;
-    }
-    *out = g_scratch_addr[dev];
+    void* ptr = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&ptr, g_sumsq_scratch);
+    if (e != cudaSuccess || !ptr)
+        return fail(P2P_ECUDA, "p2p_sumsq_cols_noalloc: scratch address lookup failed: %s", cudaGetErrorString(e));
+    *out = ptr;
     return P2P_OK;
 }
 }  // namespace

@@ -19,10 +19,13 @@
 //                       fp32 partials and a ticket per row tile; both add in split order, so results do not depend on
 //                       scheduling.
 //
-// Every mbarrier wait is bounded (about 2 s of %globaltimer): past it the kernel records where it gave up in *err and
-// runs on, so a broken pipeline ends the kernel with an error status instead of hanging the GPU.
+// Every mbarrier wait is bounded (about 2 s of %globaltimer): past it the kernel records where it gave up, the waits of
+// the same launch give up at once, no role issues further TMA loads or MMAs, and the CTA drains what it had issued
+// (the x loads landed, the MMAs completed) before it frees TMEM and exits, so a broken pipeline ends the kernel with
+// an error status (p2p_spmm_tc_status) instead of hanging the GPU or leaving copies in flight.
 #include <cuda.h>
 
+#include <atomic>
 #include <map>
 #include <mutex>
 #include <type_traits>
@@ -57,7 +60,8 @@ constexpr uint64_t kWaitNs = 2000000000ull;
 constexpr int64_t kMaxRowTiles = 16384;
 constexpr size_t kTicketRegion = kMaxRowTiles * sizeof(unsigned);
 
-__device__ int g_tc_error;            // first failed wait of the last launches (0: none); read back by the host
+__device__ int g_tc_error;            // site of the first wait that gave up since the last reset (0: none)
+__device__ unsigned g_tc_failed_seq;  // sequence number of the last launch in which a wait gave up
 
 struct TcParams {
     const uint32_t* words;            // the module's packed words
@@ -83,6 +87,9 @@ struct TcParams {
     // Unsplit plain launches: y leaves through shared memory and TMA stores (tmap_y: y [tokens, rows], boxes of 128
     // rows x box_rows tokens), instead of one 2-byte store per value.
     int y_tma;
+    uint64_t wait_ns;                 // how long a pipeline wait may take before the launch gives up
+    unsigned seq;                     // this launch's sequence number (nonzero), naming it in g_tc_failed_seq
+    int hold_tile;                    // a test's withheld x tile (each CTA's tile of that index is never loaded), or -1
 };
 
 __device__ __forceinline__ void cluster_sync_all() {
@@ -133,17 +140,36 @@ __device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
     return ok != 0;
 }
 
-// Waits for the phase of parity `parity`; past kWaitNs (or at once, once another wait has given up) it records
-// `where` in g_tc_error and returns, so a broken pipeline ends the kernel instead of hanging it.
-__device__ __forceinline__ void mbar_wait(uint32_t bar, uint32_t parity, int where) {
-    if (mbar_try(bar, parity)) return;
+__device__ __forceinline__ void give_up(int where, unsigned seq) {
+    atomicCAS(&g_tc_error, 0, where);
+    atomicExch(&g_tc_failed_seq, seq);
+}
+
+// Waits for the phase of parity `parity`; true once it completed. Past `limit_ns`, or at once when another wait of
+// the same launch has given up, it records `where` and returns false: the caller then issues no further work.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int where, uint64_t limit_ns, unsigned seq) {
+    if (mbar_try(bar, parity)) return true;
     const uint64_t t0 = now_ns();
     while (!mbar_try(bar, parity)) {
-        if (now_ns() - t0 > (*(volatile int*)&g_tc_error ? 0ull : kWaitNs)) {
-            atomicCAS(&g_tc_error, 0, where);
-            return;
+        if (*(volatile unsigned*)&g_tc_failed_seq == seq || now_ns() - t0 > limit_ns) {
+            give_up(where, seq);
+            return false;
         }
     }
+    return true;
+}
+
+// Waits for asynchronous work this CTA already issued (a TMA load landing, its MMAs completing), which finishes on its
+// own: bounded by `limit_ns` only, even after another wait gave up, so the CTA never exits with that work in flight.
+__device__ __forceinline__ bool mbar_drain(uint32_t bar, uint32_t parity, int where, uint64_t limit_ns, unsigned seq) {
+    const uint64_t t0 = now_ns();
+    while (!mbar_try(bar, parity)) {
+        if (now_ns() - t0 > limit_ns) {
+            give_up(where, seq);
+            return false;
+        }
+    }
+    return true;
 }
 
 // Ring position of the next item: `step` slots on (step <= n), the phase bit flipping at each wrap. Kept in
@@ -359,16 +385,22 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         if (lane < SX) {
             const int s = lane;
             uint32_t ph = 0;
+            int uses = 0;                                           // loads issued into slot s
             for (int i = lane; i < nk; i += SX) {
                 if (i >= SX) {
-                    mbar_wait(emptyx(s), ph, 1);
+                    if (!mbar_wait(emptyx(s), ph, 1, p.wait_ns, p.seq)) break;
                     ph ^= 1u;
                 }
+                if (i == p.hold_tile) break;                        // a test withholds this load
                 mbar_expect_tx(fullx(s), (uint32_t)p.b_bytes);
                 for (int b = 0; b < p.n_boxes; ++b)
                     tma_load_2d(x_ring + s * p.b_bytes + b * p.box_rows * 128, &tmap_x, (kt0 + i) * tc::kTileCols,
                                 (int)xrow0 + b * p.box_rows, fullx(s));
+                ++uses;
             }
+            // The slot's last load must have landed before the CTA exits (the TMA unit writes its shared memory): on
+            // a normal run the MMA consumed it long ago; after a give-up this waits for the copy itself.
+            if (uses) mbar_drain(fullx(s), (uint32_t)((uses - 1) & 1), 7, p.wait_ns, p.seq);
         }
         __syncwarp();
     } else if (warp == kMmaWarp || warp == kMmaWarp + 1) {
@@ -389,8 +421,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             int sa = by_tile ? j : 0, sx = sa;
             uint32_t pha = 0, phx = 0, acc = 0;
             for (int i = by_tile ? j : 0; i < nk; i += step) {
-                mbar_wait(fulla(sa), pha, 2);
-                mbar_wait(fullx(sx), phx, 3);
+                if (!mbar_wait(fulla(sa), pha, 2, p.wait_ns, p.seq)) break;     // no MMA on a tile not there
+                if (!mbar_wait(fullx(sx), phx, 3, p.wait_ns, p.seq)) break;
                 tc_fence_after();
                 const uint64_t a_desc = a0 + (uint64_t)((sa * kASlotBytes) >> 4);
                 const uint64_t b_desc = b0 + (uint64_t)((sx * p.b_bytes) >> 4);
@@ -403,7 +435,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 advance(sa, pha, step, SA);
                 advance(sx, phx, step, SX);
             }
-            umma_commit(done);
+            umma_commit(done);                          // arrives once every MMA this thread issued completed
         }
         __syncwarp();
     } else {
@@ -447,7 +479,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             zero_rows(s);                               // the group's first slot: no earlier use to wait for
             __syncwarp();
         }
-        auto expand = [&](int i, const uint4 (&cur)[kChunks], int lo, int hi) {
+        // false: a wait gave up, and the warp stops expanding (no further tiles for the MMAs to read)
+        auto expand = [&](int i, const uint4 (&cur)[kChunks], int lo, int hi) -> bool {
             if (zero_ahead) {
                 int sn = s + kGroups;
                 uint32_t pn = ph;
@@ -456,13 +489,15 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     pn ^= 1u;
                 }
                 if (i + kGroups < nk) {
-                    if (lane == 0 && i + kGroups >= SA) mbar_wait(emptya(sn), pn ^ 1u, 5);
-                    __syncwarp();
+                    int ok = 1;
+                    if (lane == 0 && i + kGroups >= SA) ok = mbar_wait(emptya(sn), pn ^ 1u, 5, p.wait_ns, p.seq);
+                    if (!__shfl_sync(0xffffffffu, ok, 0)) return false;
                     zero_rows(sn);                      // ordered before its scatter by this tile's fence + sync
                 }
             } else {
-                if (lane == 0 && i >= SA) mbar_wait(emptya(s), ph ^ 1u, 5);
-                __syncwarp();
+                int ok = 1;
+                if (lane == 0 && i >= SA) ok = mbar_wait(emptya(s), ph ^ 1u, 5, p.wait_ns, p.seq);
+                if (!__shfl_sync(0xffffffffu, ok, 0)) return false;
                 zero_rows(s);
                 __syncwarp();                                                // the warp's rows zeroed
             }
@@ -487,6 +522,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             __syncwarp();
             if (lane == 0) mbar_arrive(fulla(s));
             advance(s, ph, kGroups, SA);
+            return true;
         };
         constexpr int G = kGroups;
         // Each tile's words are loaded just before they are written. Loading one or two of the group's tiles ahead
@@ -494,11 +530,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         // tile and the slot waits cover the loads, and the extra live registers cost the scheduler more.
         for (int i = grp; i < nk; i += G) {
             fetch(i, b0, l0, h0);
-            expand(i, b0, l0, h0);
+            if (!expand(i, b0, l0, h0)) break;
         }
 
-        // Epilogue: D[row, token] out of TMEM. Warp w reads lanes 32 (w % 4) .. + 31, every other 16-column chunk.
-        if (lane == 0) mbar_wait(done, 0, 6);
+        // Epilogue: D[row, token] out of TMEM, once every MMA of both issuers has completed (also after a give-up:
+        // TMEM is freed below, and no MMA may still write it). Warp w reads lanes 32 (w % 4) .. + 31, every other
+        // 16-column chunk.
+        if (lane == 0) mbar_drain(done, 0, 6, p.wait_ns, p.seq);
         __syncwarp();
         tc_fence_after();
         const int quarter = warp & 3, cgroup = warp >> 2;          // 4 column groups of the 16 expander warps
@@ -831,6 +869,14 @@ int choose_split(int64_t row_tiles, int col_tiles, int tokens, int sms) {
     return best;
 }
 
+// A nonzero sequence number for each launch, so that a give-up in one launch cuts short only that launch's waits.
+unsigned next_seq() {
+    static std::atomic<unsigned> counter{0};
+    unsigned v = ++counter;
+    while (v == 0) v = ++counter;
+    return v;
+}
+
 // The column split of one launch: (splits, column tiles a split), at most kMaxTilesPerCta tiles a CTA.
 void plan_split(int64_t row_tiles, int col_tiles, int tokens, int sms, int* n_split, int* per) {
     int s = choose_split(row_tiles, col_tiles, tokens, sms);
@@ -865,9 +911,11 @@ extern "C" size_t p2p_spmm_tc_workspace(int64_t rows, int64_t cols, int64_t toke
     return need;
 }
 
-extern "C" int p2p_spmm_tc(const void* x, int dtype, int64_t tokens, int64_t cols, int64_t ldx, const uint32_t* words,
-                           const int64_t* seg, int64_t rows, int64_t seg_cap_words, void* y, int64_t ldy,
-                           void* workspace, size_t workspace_bytes, void* stream) {
+namespace {
+// p2p_spmm_tc, with the wait limit and withheld tile of p2p_spmm_tc_withhold (hold_tile < 0: none).
+int spmm_tc_impl(const void* x, int dtype, int64_t tokens, int64_t cols, int64_t ldx, const uint32_t* words,
+                 const int64_t* seg, int64_t rows, int64_t seg_cap_words, void* y, int64_t ldy, void* workspace,
+                 size_t workspace_bytes, void* stream, int hold_tile, uint64_t wait_ns) {
     P2P_REQUIRE(tokens >= 0 && rows >= 0 && cols >= 1, "p2p_spmm_tc: bad shape");
     if (tokens == 0 || rows == 0) return P2P_OK;
     if (dtype != P2P_BF16 && dtype != P2P_F16)
@@ -927,6 +975,9 @@ extern "C" int p2p_spmm_tc(const void* x, int dtype, int64_t tokens, int64_t col
         prm.items = nullptr;
         prm.item_bound_tiles = prm.item_bound_rows = 0;
         prm.item_row_tiles = 0;
+        prm.wait_ns = wait_ns;
+        prm.seq = next_seq();
+        prm.hold_tile = hold_tile;
         CUtensorMap map, ymap;
         const void* xt = reinterpret_cast<const char*>(x) + t0 * ldx * elem;
         if (int e = encode_x_map(&map, xt, dtype, tn, cols, ldx, pl.box_rows)) return e;
@@ -942,6 +993,26 @@ extern "C" int p2p_spmm_tc(const void* x, int dtype, int64_t tokens, int64_t col
             return e;
     }
     return P2P_OK;
+}
+}  // namespace
+
+extern "C" int p2p_spmm_tc(const void* x, int dtype, int64_t tokens, int64_t cols, int64_t ldx, const uint32_t* words,
+                           const int64_t* seg, int64_t rows, int64_t seg_cap_words, void* y, int64_t ldy,
+                           void* workspace, size_t workspace_bytes, void* stream) {
+    return spmm_tc_impl(x, dtype, tokens, cols, ldx, words, seg, rows, seg_cap_words, y, ldy, workspace,
+                        workspace_bytes, stream, -1, kWaitNs);
+}
+
+extern "C" int p2p_spmm_tc_withhold(const void* x, int dtype, int64_t tokens, int64_t cols, int64_t ldx,
+                                    const uint32_t* words, const int64_t* seg, int64_t rows, int64_t seg_cap_words,
+                                    void* y, int64_t ldy, void* workspace, size_t workspace_bytes, int64_t hold_tile,
+                                    int64_t wait_us, void* stream) {
+    P2P_REQUIRE(hold_tile >= 0 && hold_tile < 4096, "p2p_spmm_tc_withhold: tile %lld", (long long)hold_tile);
+    P2P_REQUIRE(wait_us >= 1000 && wait_us <= 2000000, "p2p_spmm_tc_withhold: a limit of 1 ms to 2 s (%lld us)",
+                (long long)wait_us);
+    P2P_REQUIRE(tokens <= 512, "p2p_spmm_tc_withhold: one launch (at most 512 tokens)");
+    return spmm_tc_impl(x, dtype, tokens, cols, ldx, words, seg, rows, seg_cap_words, y, ldy, workspace,
+                        workspace_bytes, stream, (int)hold_tile, (uint64_t)wait_us * 1000ull);
 }
 
 extern "C" int p2p_spmm_tc_grouped(const void* x, int dtype, int64_t x_rows, int64_t cols, int64_t ldx,
@@ -964,10 +1035,13 @@ extern "C" int p2p_spmm_tc_grouped(const void* x, int dtype, int64_t x_rows, int
                     seg_cap_words <= tc::kHeaderWords + tc::kTileRows * tc::kTileCols + 4,
                 "p2p_spmm_tc_grouped: segment capacity %lld words", (long long)seg_cap_words);
     P2P_REQUIRE(x_rows <= 0x7fffffff && n_items <= 65535, "p2p_spmm_tc_grouped: too large");
+    const int col_tiles = (int)((cols + tc::kTileCols - 1) / tc::kTileCols);
+    // An item takes whole rows in one CTA, which stages the offsets and headers of all its column tiles.
+    P2P_REQUIRE(col_tiles <= kMaxTilesPerCta, "p2p_spmm_tc_grouped: %lld columns; at most %d (%d column tiles a CTA)",
+                (long long)cols, kMaxTilesPerCta * tc::kTileCols, kMaxTilesPerCta);
     cudaStream_t st = as_stream(stream);
     TcPlan pl;
     if (int e = plan_tokens((int)max_tokens, pl)) return e;
-    const int col_tiles = (int)((cols + tc::kTileCols - 1) / tc::kTileCols);
     TcParams prm;
     prm.words = words;
     prm.seg = seg;
@@ -995,6 +1069,9 @@ extern "C" int p2p_spmm_tc_grouped(const void* x, int dtype, int64_t x_rows, int
     prm.item_row_tiles = (int)item_row_tiles;
     prm.y_tma = 0;
     prm.cluster = 0;
+    prm.wait_ns = kWaitNs;
+    prm.seq = next_seq();
+    prm.hold_tile = -1;
     CUtensorMap map;
     if (int e = encode_x_map(&map, x, dtype, x_rows, cols, ldx, pl.box_rows)) return e;
     const dim3 grid((unsigned)item_row_tiles, (unsigned)n_items);

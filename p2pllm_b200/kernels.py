@@ -3,6 +3,7 @@ stream of the inputs' device. Each function names the reference interface it ser
 from __future__ import annotations
 
 import ctypes
+import os
 
 import torch
 
@@ -10,6 +11,9 @@ from . import _lib
 from ._lib import P2PError, call, dtype_code, ptr, require_cuda, stream_of
 
 _workspaces: dict = {}
+# P2P_CHECK_WAITS=1: after every tensor-core GEMM launch, read back whether a pipeline wait gave up (and raise if one
+# did). It synchronizes the stream each time, so it is for debugging, not for serving.
+CHECK_WAITS = os.environ.get("P2P_CHECK_WAITS", "0") not in ("", "0")
 
 
 def _workspace(device: torch.device, nbytes: int, purpose: str = "sumsq") -> torch.Tensor:
@@ -256,6 +260,23 @@ def spmm_tc(x: torch.Tensor, words: torch.Tensor, seg: torch.Tensor, rows: int, 
     ws = _workspace(x.device, need, "spmm_tc") if need else None
     call("p2p_spmm_tc", ptr(x), dtype_code(x), x.shape[0], cols, x.stride(0), ptr(words), ptr(seg), rows, seg_cap,
          ptr(out), out.stride(0), ptr(ws), 0 if ws is None else ws.numel(), stream_of(x))
+    if CHECK_WAITS:
+        spmm_tc_status(x.device)
+    return out
+
+
+def spmm_tc_withhold(x: torch.Tensor, words: torch.Tensor, seg: torch.Tensor, rows: int, cols: int, seg_cap: int,
+                     hold_tile: int, wait_us: int) -> torch.Tensor:
+    """A launch of the tensor-core GEMM in which every CTA withholds its x tile number hold_tile, so the pipeline's
+    bounded waits run out after wait_us: the give-up path under test. y is undefined; spmm_tc_status reports it."""
+    require_cuda(x)
+    x = x.contiguous()
+    out = torch.zeros(x.shape[0], rows, dtype=x.dtype, device=x.device)
+    lib = _lib.load()
+    need = lib.p2p_spmm_tc_workspace(rows, cols, x.shape[0])
+    ws = _workspace(x.device, need, "spmm_tc") if need else None
+    call("p2p_spmm_tc_withhold", ptr(x), dtype_code(x), x.shape[0], cols, x.stride(0), ptr(words), ptr(seg), rows,
+         seg_cap, ptr(out), out.stride(0), ptr(ws), 0 if ws is None else ws.numel(), hold_tile, wait_us, stream_of(x))
     return out
 
 

@@ -60,6 +60,8 @@ class ExpertTiles:
         call("p2p_spmm_tc_grouped", ptr(x), dtype_code(x), x.shape[0], self.cols, x.stride(0), ptr(self.words),
              ptr(self.seg), self.layout_row_tiles, self.rows, self.item_row_tiles, self.seg_cap, ptr(items),
              items.shape[0], max_tokens, ptr(out), out.stride(0), stream_of(x))
+        if kernels.CHECK_WAITS:
+            kernels.spmm_tc_status(x.device)
         return out
 
     def nbytes(self) -> int:

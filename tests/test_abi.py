@@ -66,3 +66,21 @@ def test_cpu_tensors_are_refused():
     from p2pllm_b200 import P2PError, kernels
     with pytest.raises(P2PError, match="CUDA"):
         kernels.combine([torch.zeros(4), torch.zeros(4)], torch.zeros(4), torch.zeros(4))
+
+
+def test_grouped_launch_refuses_more_column_tiles_than_a_cta_stages(lib):
+    """An item of a grouped launch takes whole rows in one CTA, which stages at most 256 column tiles' offsets and
+    headers in shared memory: 16,384 + 64 columns are refused before any launch (no device memory is touched; the
+    pointers are placeholders with the alignment the earlier checks ask for)."""
+    fake = ctypes.c_void_p(256)
+    cols = 16384 + 64
+    st = lib.p2p_spmm_tc_grouped(fake, 0, 16, cols, cols, fake, fake, 1, 128, 1, 16, fake, 1, 16, fake, 128, None)
+    assert st == -1 and b"at most 16384" in lib.p2p_last_error()
+
+
+def test_withhold_test_entry_checks_its_limits(lib):
+    fake = ctypes.c_void_p(256)
+    st = lib.p2p_spmm_tc_withhold(fake, 0, 16, 64, 64, fake, fake, 128, 16, fake, 128, None, 0, 0, 10, None)
+    assert st == -1 and b"1 ms to 2 s" in lib.p2p_last_error()
+    st = lib.p2p_spmm_tc_withhold(fake, 0, 600, 64, 64, fake, fake, 128, 16, fake, 128, None, 0, 0, 5000, None)
+    assert st == -1 and b"one launch" in lib.p2p_last_error()

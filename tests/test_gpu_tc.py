@@ -208,3 +208,31 @@ def test_dependent_launches_see_the_previous_kernels_output():
         got = m.apply(None, x2)
         torch.cuda.synchronize()
         assert torch.equal(got, m.apply(None, (x * scale)))
+
+
+@pytest.mark.parametrize("tokens", [17, 272])
+def test_a_withheld_tile_ends_the_launch_with_an_error_status(tokens):
+    """Failure detection without a fault: every CTA withholds one x tile (it is never loaded), so the waits for it run
+    out after 20 ms of %globaltimer. The launch must end by itself (drained: no copy or MMA left in flight), the status
+    must name the wait that gave up, and the context must stay usable: the next ordinary launch gives the right
+    product, and a wait of that launch is not cut short by the earlier give-up."""
+    import time
+    from p2pllm_b200._lib import P2PError
+    values, idx = _module(256, 1024, 36, seed=5)
+    tiles = compact.Tiles([("compact", values, idx, 1024)])
+    x = torch.randn(tokens, 1024, device="cuda").bfloat16()
+    kernels.spmm_tc_status(reset=True)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    kernels.spmm_tc_withhold(x, tiles.words, tiles.seg, tiles.rows, tiles.cols, tiles.seg_cap, hold_tile=0,
+                             wait_us=20000)
+    torch.cuda.synchronize()
+    elapsed = time.perf_counter() - t0
+    assert elapsed < 1.0, elapsed                                   # the 20 ms limit, plus the drain, not 2 s
+    with pytest.raises(P2PError, match="timed out"):
+        kernels.spmm_tc_status(reset=True)
+    kernels.spmm_tc_status()                                        # reset: clean again
+    y = tiles(x)
+    kernels.spmm_tc_status()
+    want = oracle.forward(_bits(x), _bits(values), idx.cpu().numpy(), 1024, "bf16")
+    _check(y, want, torch.bfloat16)
