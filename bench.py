@@ -39,8 +39,7 @@ from p2pllm_b200 import workloads  # noqa: E402
 METRIC = "replica sparse-GEMM tokens/s (Llama-3-8B replica layer, keep 33/36, T=272)"
 UNIT = "tokens/s"
 # The layer's linear modules as SGLang holds them (fused q/k/v and gate/up), the input each reads, and their blocks.
-MODULES = {"qkv_proj": ("attn_in", ("q", "k", "v")), "o_proj": ("attn_out", ("o",)),
-           "gate_up_proj": ("mlp_in", ("gate", "up")), "down_proj": ("mlp_mid", ("down",))}
+MODULES = workloads.LAYER_MODULES
 INPUT_OF = {n: group for group, names in MODULES.values() for n in names}
 L2_BYTES = 126 * 1024 * 1024
 # A spin queued just before a device-timed region: the host enqueues the region's launches while the GPU spins, so
@@ -143,32 +142,23 @@ class ReplicaLayer:
         from p2pllm_b200 import compact, kernels, wanda
         self.device, self.tokens = device, tokens
         self.proj = {p.name: p for p in (projections or workloads.LLAMA3_8B)}
-        self.inputs, self.methods, self.k = {}, {}, {}
+        self.inputs, self.methods, self.k, self.selected = {}, {}, {}, {}
         calib_ms, select_ms, calib_bytes = 0.0, 0.0, 0
         ev = lambda: torch.cuda.Event(enable_timing=True)
-        for gi, (module, (group, names)) in enumerate(MODULES.items()):
+        seeds = workloads.layer_seeds(seed, tuple(self.proj.values()))
+        for module, (group, names) in MODULES.items():
             cols = self.proj[names[0]].cols
-            g = torch.Generator(device=device).manual_seed(seed * 1000 + gi)
+            g = torch.Generator(device=device).manual_seed(seeds[module][0])
             scale = workloads.channel_scale(cols, g, device)
             # Calibration: the hook's reduction over 128 x 2048 synthetic tokens, in 16 calls.
-            sums = torch.zeros(cols, dtype=torch.float64, device=device)
-            chunk = max(1, calib_tokens // 16)
-            for _ in range(max(1, calib_tokens // chunk)):
-                xc = (torch.randn(chunk, cols, generator=g, device=device) * scale).bfloat16()
-                a, b = ev(), ev()
-                a.record()
-                kernels.sumsq_cols(xc, sums)
-                b.record()
-                b.synchronize()
-                calib_ms += a.elapsed_time(b)
-                calib_bytes += xc.numel() * 2
-                del xc
+            sums, ms, nb = workloads.calibrate(cols, g, scale, calib_tokens, device)
+            calib_ms, calib_bytes = calib_ms + ms, calib_bytes + nb
             norms = kernels.channel_norms(sums)
             self.inputs[group] = (torch.randn(tokens, cols, generator=g, device=device) * scale).bfloat16()
             blocks = []
             for n in names:
                 p = self.proj[n]
-                w = workloads.projection_weights(p, seed * 1000 + 17 * (list(self.proj).index(n) + 1), device)
+                w = workloads.projection_weights(p, seeds[module][1][n], device)
                 a, b = ev(), ev()
                 a.record()
                 values, idx = wanda.select(w, p.keep, norms)
@@ -177,6 +167,7 @@ class ReplicaLayer:
                 select_ms += a.elapsed_time(b)
                 del w
                 self.k[n] = values.shape[1]
+                self.selected[n] = (values, idx)
                 blocks.append(("compact", values, idx, p.cols))
             self.methods[module] = compact.Compact(blocks)
         self.calib_ms, self.select_ms, self.calib_bytes = calib_ms, select_ms, calib_bytes

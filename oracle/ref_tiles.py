@@ -25,6 +25,16 @@ import torch
 RT, KCOLS, WARPS = 128, 64, 4            # compact.cu's defaults: P2P_WARPS 4, P2P_KCOLS 64
 
 
+def words_of(idx: torch.Tensor, cols: int) -> torch.Tensor:
+    """The reference's mask words of column indices [rows, k] (p2p/compact.py:36-45: bit c % 32 of word c // 32,
+    int32 two's complement), built with torch on idx's device."""
+    n_words = -(-cols // 32)
+    mask = torch.zeros(idx.shape[0], n_words * 32, dtype=torch.int64, device=idx.device)
+    mask.scatter_(1, idx.long(), 1)
+    w = (mask.view(idx.shape[0], n_words, 32) << torch.arange(32, device=idx.device)).sum(-1)
+    return torch.where(w >= 2 ** 31, w - 2 ** 32, w).to(torch.int32)
+
+
 def _dense_and_kept(blocks: list, cols: int, dtype, device):
     """The module as one dense matrix and its kept mask, from the reference's block list (p2p/compact.py:127-128):
     ("dense", W) keeps every weight; ("sparse", values [rows, k] in column order, words int32 [rows, ceil(C/32)], C)."""

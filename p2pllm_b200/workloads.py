@@ -78,3 +78,48 @@ def activations(cols: int, tokens: int, seed: int, device, dtype=torch.bfloat16,
     if scale is None:
         scale = channel_scale(cols, g, device)
     return (torch.randn(tokens, cols, generator=g, device=device) * scale).to(dtype)
+
+
+def selection_case(p: Projection, index: int, calib_tokens: int = 4096):
+    """(w [rows, cols] bf16 ~ N(0, 0.02), calibration activations [calib_tokens, cols] bf16, lognormal-scaled) of one
+    projection of the full-size selection check, from the CPU generator, so the reference's selection computed on one
+    machine and this package's on another see the same inputs."""
+    g = torch.Generator().manual_seed(7000 + index)
+    w = (torch.randn(p.rows, p.cols, generator=g) * 0.02).bfloat16()
+    scale = channel_scale(p.cols, g)
+    x = (torch.randn(calib_tokens, p.cols, generator=g) * scale).bfloat16()
+    return w, x
+
+
+def calibrate(cols: int, generator: torch.Generator, scale: torch.Tensor, calib_tokens: int, device, calls: int = 16):
+    """The benchmark's calibration of one projection input: calib_tokens lognormal-scaled bf16 tokens drawn from
+    `generator` on `device`, reduced by the package's calibration kernel in `calls` hook calls. Returns (sums fp64
+    [cols], the kernel's milliseconds, the bytes it read)."""
+    from . import kernels
+    sums = torch.zeros(cols, dtype=torch.float64, device=device)
+    chunk = max(1, calib_tokens // calls)
+    ms, nbytes = 0.0, 0
+    for _ in range(max(1, calib_tokens // chunk)):
+        xc = (torch.randn(chunk, cols, generator=generator, device=device) * scale).bfloat16()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        kernels.sumsq_cols(xc, sums)
+        b.record()
+        b.synchronize()
+        ms += a.elapsed_time(b)
+        nbytes += xc.numel() * 2
+        del xc
+    return sums, ms, nbytes
+
+
+# The benchmark layer's linear modules as SGLang holds them (fused q/k/v and gate/up), the input each reads, and the
+# projections they hold.
+LAYER_MODULES = {"qkv_proj": ("attn_in", ("q", "k", "v")), "o_proj": ("attn_out", ("o",)),
+                 "gate_up_proj": ("mlp_in", ("gate", "up")), "down_proj": ("mlp_mid", ("down",))}
+
+
+def layer_seeds(seed: int, projections=LLAMA3_8B) -> dict:
+    """{module: (calibration generator seed, {projection name: weight seed})} of the benchmark layer of rank seed."""
+    names = [p.name for p in projections]
+    return {module: (seed * 1000 + gi, {n: seed * 1000 + 17 * (names.index(n) + 1) for n in proj})
+            for gi, (module, (_, proj)) in enumerate(LAYER_MODULES.items())}

@@ -41,6 +41,11 @@ def expert_golden():
 
 
 @pytest.fixture(scope="session")
+def llama_select():
+    return golden("llama_select.npz")
+
+
+@pytest.fixture(scope="session")
 def tiles_golden():
     return golden("tiles_cases.npz")
 

@@ -234,6 +234,37 @@ def replica_case(out_dir: str) -> dict:
     return out
 
 
+def row_hashes(words: np.ndarray) -> np.ndarray:
+    """An 8-byte BLAKE2b digest of each row of mask words, as uint64 (a full-size selection stored compactly)."""
+    words = np.ascontiguousarray(words)
+    return np.array([int.from_bytes(hashlib.blake2b(r.tobytes(), digest_size=8).digest(), "little") for r in words],
+                    dtype=np.uint64)
+
+
+def llama_select_case(wanda, compact) -> dict:
+    """The reference's selection at BASELINE config 2's full sizes: each Llama-3-8B projection (keep 33 / 36) on
+    CPU-seeded weights, with norms from a lognormal-scaled calibration (wanda.py:39, channel_norms), pruned and packed
+    by the reference (wanda.prune with_mask, compact.pack). Stored: the norms, each row's mask-word digest and the rows
+    whose k-th and (k+1)-th scores tie (where torch.topk's choice is unspecified)."""
+    out = {}
+    for i, p in enumerate(workloads.LLAMA3_8B):
+        w, x = workloads.selection_case(p, i)
+        sums = x.float().pow(2).sum(0).double()
+        norms = wanda.channel_norms(sums, w)
+        pruned, mask = wanda.prune(w, p.keep, norms, with_mask=True)
+        _, words = compact.pack(pruned, mask)
+        score = w.float().abs() * norms
+        k = max(1, round(p.keep / 100 * p.cols))
+        srt = score.sort(dim=-1, descending=True).values
+        out[p.name + "_norms"] = norms.numpy()
+        out[p.name + "_sums"] = sums.numpy()
+        out[p.name + "_words_b2"] = row_hashes(words.numpy())
+        out[p.name + "_tie_rows"] = np.nonzero((srt[:, k - 1] == srt[:, k]).numpy())[0].astype(np.int64)
+        out[p.name + "_k"] = np.array(k)
+        print(p.name, "k", k, "tie rows", len(out[p.name + "_tie_rows"]), flush=True)
+    return out
+
+
 def main() -> None:
     wanda, compact, replica, route = _reference()
     torch.manual_seed(0)
@@ -243,6 +274,7 @@ def main() -> None:
     np.savez_compressed(os.path.join(HERE, "expert_case.npz"), **expert_case(wanda))
     np.savez_compressed(os.path.join(HERE, "tiles_cases.npz"), **tiles_cases(wanda, compact))
     np.savez_compressed(os.path.join(HERE, "replica_case.npz"), **replica_case(HERE))
+    np.savez_compressed(os.path.join(HERE, "llama_select.npz"), **llama_select_case(wanda, compact))
     for f in sorted(os.listdir(HERE)):
         if f.endswith(".npz"):
             print(f, os.path.getsize(os.path.join(HERE, f)))

@@ -41,14 +41,13 @@ def test_reference_kernel_on_its_own_layouts(ext, tiles_golden, name, tokens):
 
 @pytest.mark.parametrize("rows,cols,keep,tokens", [(1024, 4096, 33, 17), (640, 1024, 36, 272)])
 def test_reference_kernel_agrees_with_ours(ext, rows, cols, keep, tokens):
-    from oracle.time_ref_kernel import words_of
     from p2pllm_b200 import compact, wanda
     g = torch.Generator(device="cuda").manual_seed(rows)
     w = (torch.randn(rows, cols, generator=g, device="cuda") * 0.02).bfloat16()
     norms = torch.rand(cols, generator=g, device="cuda") + 0.1
     values, idx = wanda.select(w, keep, norms)
     x = torch.randn(tokens, cols, generator=g, device="cuda").bfloat16()
-    ref = ref_tiles.RefTiles([("sparse", values, words_of(idx, cols), cols)], ext)(x).double()
+    ref = ref_tiles.RefTiles([("sparse", values, ref_tiles.words_of(idx, cols), cols)], ext)(x).double()
     ours = compact.Compact([("compact", values, idx, cols)]).apply(None, x).double()
     bits = lambda t: t.cpu().view(torch.int16).numpy().view(np.uint16)
     want = oracle.forward(bits(x), bits(values), idx.cpu().numpy().astype(np.int64), cols, "bf16")

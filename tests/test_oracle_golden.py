@@ -161,3 +161,28 @@ def test_bf16_conversions_round_to_nearest_even():
     assert np.array_equal(oracle.f32_to_bf16(f), torch.tensor(f).bfloat16().view(torch.int16).numpy().view(np.uint16))
     r = np.random.default_rng(0).standard_normal(10000).astype(np.float32)
     assert np.array_equal(oracle.f32_to_bf16(r), torch.tensor(r).bfloat16().view(torch.int16).numpy().view(np.uint16))
+
+
+def test_oracle_selection_at_full_size_matches_the_reference_words(llama_select):
+    """The oracle against the reference's own full-size selection (tests/golden/llama_select.npz): on the k projection
+    (1024 x 4096, keep 33) every row's mask words, rebuilt from the oracle's indices, digest the same as the
+    reference's, except the rows that tie at the k-th score."""
+    import hashlib
+    import torch
+    from p2pllm_b200 import workloads
+    index = [p.name for p in workloads.LLAMA3_8B].index("k")
+    p = workloads.LLAMA3_8B[index]
+    w, _ = workloads.selection_case(p, index)
+    bits = w.view(torch.int16).numpy().view(np.uint16)
+    score = oracle.scores(bits, llama_select["k_norms"], "bf16")
+    k = int(llama_select["k_k"])
+    idx = oracle.select(score, k)
+    mask = np.zeros((p.rows, p.cols), bool)
+    np.put_along_axis(mask, idx, True, axis=1)
+    _, words = oracle.pack(bits, mask)
+    dig = np.array([int.from_bytes(hashlib.blake2b(np.ascontiguousarray(r).tobytes(), digest_size=8).digest(),
+                                   "little") for r in words], dtype=np.uint64)
+    ties = set(llama_select["k_tie_rows"].tolist())
+    same = dig == llama_select["k_words_b2"]
+    assert all(same[r] for r in range(p.rows) if r not in ties)
+    assert set(np.nonzero(oracle.tie_rows(score, k))[0].tolist()) == ties
