@@ -163,6 +163,38 @@ int p2p_tiles_plan(const p2p_row_block* blocks, int nblocks, int idx_bytes, int6
 int p2p_tiles_fill(const p2p_row_block* blocks, int nblocks, int idx_bytes, int64_t cols, int dtype, const int64_t* seg,
                    uint32_t* words, int64_t n_words, void* workspace, size_t workspace_bytes, void* stream);
 
+/* The bitmask layout of a module (values + one bit a weight, the reference's storage of p2p/compact.py:36-45) for
+ * p2p_spmm_mask, built on the GPU from row blocks as for p2p_tiles_*: 128-row x 64-column segments, each a 16-byte
+ * header of cumulative 16-row block counts, 1024 bytes of piece masks (8 blocks x 16 pieces x 64 bits) and the kept
+ * values piece by piece, padded to 16 bytes; seg[n_seg + 1] holds byte offsets. Load time, syncs.
+ *   p2p_mask_workspace: bytes of scratch p2p_mask_plan needs;
+ *   p2p_mask_plan: fills seg and returns the total bytes through *total_bytes;
+ *   p2p_mask_fill: writes the layout [total_bytes] (16-byte aligned); refuses indices out of ascending order.
+ * Replaces p2p/compact.py:124-174 (Tiles.__init__: the re-tiling into 8 x 8 pieces of masks and values). */
+size_t p2p_mask_workspace(const p2p_row_block* blocks, int nblocks, int64_t cols);
+int p2p_mask_plan(const p2p_row_block* blocks, int nblocks, int idx_bytes, int64_t cols, int64_t* seg,
+                  int64_t* total_bytes, void* workspace, size_t workspace_bytes, void* stream);
+int p2p_mask_fill(const p2p_row_block* blocks, int nblocks, int idx_bytes, int64_t cols, int dtype, const int64_t* seg,
+                  void* data, int64_t total_bytes, void* stream);
+
+/* Bytes of workspace p2p_spmm_mask needs for this shape (0 if it does not split the columns). */
+size_t p2p_spmm_mask_workspace(int64_t rows, int64_t cols, int64_t tokens);
+
+/* y [tokens, ldy] = x [tokens, cols] (row stride ldx, 16-byte aligned rows) times the module in the bitmask layout, on
+ * tcgen05 tensor cores: segments streamed into shared memory by bulk copies, each 128 x 64 weight tile rebuilt in
+ * registers and stored into tensor memory, the MMAs reading it from there (fp32 accumulation in TMEM, x by TMA).
+ * bf16 or f16; cols a multiple of 8; any token count (288 a launch). workspace: zeroed once before its first use (left
+ * zeroed again); calls sharing it must not overlap on the GPU. Each launch is a programmatic dependent of the stream's
+ * previous kernel, as p2p_spmm_tc (x may be that kernel's output; data and seg must not be).
+ * Replaces p2p/compact.cu:82-278 (spmm_kernel, sum_parts, spmm) on the reference's own storage format. */
+int p2p_spmm_mask(const void* x, int dtype, int64_t tokens, int64_t cols, int64_t ldx, const void* data,
+                  const int64_t* seg, int64_t rows, void* y, int64_t ldy, void* workspace, size_t workspace_bytes,
+                  void* stream);
+
+/* P2P_OK unless a p2p_spmm_mask launch since the last reset gave up waiting on its pipeline (then P2P_ECUDA, naming
+ * the site); reset != 0 clears it. Syncs the stream. */
+int p2p_spmm_mask_status(int reset, void* stream);
+
 /* Bytes of workspace p2p_spmm_tc needs for this shape (0 if it does not split the columns). */
 size_t p2p_spmm_tc_workspace(int64_t rows, int64_t cols, int64_t tokens);
 

@@ -44,6 +44,12 @@ SIGNATURES = {
     "p2p_tiles_workspace": ([ctypes.POINTER(RowBlock), _int, _i64], _sz),
     "p2p_tiles_plan": ([ctypes.POINTER(RowBlock), _int, _int, _i64, _vp, ctypes.POINTER(_i64), _vp, _sz, _vp], _int),
     "p2p_tiles_fill": ([ctypes.POINTER(RowBlock), _int, _int, _i64, _int, _vp, _vp, _i64, _vp, _sz, _vp], _int),
+    "p2p_mask_workspace": ([ctypes.POINTER(RowBlock), _int, _i64], _sz),
+    "p2p_mask_plan": ([ctypes.POINTER(RowBlock), _int, _int, _i64, _vp, ctypes.POINTER(_i64), _vp, _sz, _vp], _int),
+    "p2p_mask_fill": ([ctypes.POINTER(RowBlock), _int, _int, _i64, _int, _vp, _vp, _i64, _vp], _int),
+    "p2p_spmm_mask_workspace": ([_i64, _i64, _i64], _sz),
+    "p2p_spmm_mask": ([_vp, _int, _i64, _i64, _i64, _vp, _vp, _i64, _vp, _i64, _vp, _sz, _vp], _int),
+    "p2p_spmm_mask_status": ([_int, _vp], _int),
     "p2p_spmm_tc_workspace": ([_i64, _i64, _i64], _sz),
     "p2p_spmm_tc": ([_vp, _int, _i64, _i64, _i64, _vp, _vp, _i64, _i64, _vp, _i64, _vp, _sz, _vp], _int),
     "p2p_spmm_tc_grouped": ([_vp, _int, _i64, _i64, _i64, _vp, _vp, _i64, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _i64,

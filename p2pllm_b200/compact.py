@@ -14,12 +14,19 @@ each with an optional leading expert dimension for routed experts.
 """
 from __future__ import annotations
 
+import os
+
 import torch
 
 from . import kernels
 from ._lib import P2PError, idx_dtype
 
 __all__ = ["pack", "unpack", "expand", "to_compact", "Tiles", "Compact", "CompactMoE"]
+
+# The layout bf16 / f16 modules take unless asked otherwise: "tc" (values + positions, 4 bytes a kept weight, one
+# 16-bit store a weight into a shared-memory tile) or "mask" (values + one bit a weight, the reference's storage,
+# tiles rebuilt in registers into tensor memory). P2P_LAYOUT=tc|mask overrides it.
+DEFAULT_LAYOUT = os.environ.get("P2P_LAYOUT", "tc")
 
 
 def pack(w: torch.Tensor, mask: torch.Tensor) -> tuple:
@@ -110,11 +117,14 @@ class Tiles:
             rows_blocks = [(r, v, None if i is None else i.to(want)) for r, v, i in rows_blocks]
         self.rows = row0
         tc_ok = self.dtype in (torch.bfloat16, torch.float16) and self.cols % 8 == 0
-        self.layout = layout or ("tc" if tc_ok else "rows")
+        self.layout = layout or (DEFAULT_LAYOUT if tc_ok else "rows")
+        if self.layout in ("tc", "mask") and not tc_ok:
+            raise P2PError("the tensor-core layouts hold bf16 / f16 modules with columns in multiples of 8")
         if self.layout == "tc":
-            if not tc_ok:
-                raise P2PError("the tensor-core layout holds bf16 / f16 modules with columns in multiples of 8")
             self.words, self.seg, self.seg_cap = kernels.tiles_build(rows_blocks, self.cols)
+            self.blocks = None
+        elif self.layout == "mask":
+            self.data, self.seg = kernels.mask_build(rows_blocks, self.cols)
             self.blocks = None
         elif self.layout == "rows":
             self.blocks = rows_blocks
@@ -125,11 +135,15 @@ class Tiles:
         """x [T, cols] @ W.T: [T, rows]. Any T (the reference launches at most 64 tokens at a time)."""
         if x.dtype != self.dtype:
             raise P2PError(f"x is {x.dtype}, the weights {self.dtype}")
+        if self.layout == "mask":
+            return kernels.spmm_mask(x, self.data, self.seg, self.rows, self.cols, out=out)
         if self.layout == "tc":
             return kernels.spmm_tc(x, self.words, self.seg, self.rows, self.cols, self.seg_cap, out=out)
         return kernels.spmm_rows(x, self.blocks, self.cols, self.rows, out=out)
 
     def nbytes(self) -> int:
+        if self.layout == "mask":
+            return self.data.numel() + self.seg.numel() * 8
         if self.layout == "tc":
             return self.words.numel() * 4 + self.seg.numel() * 8
         return sum(t.numel() * t.element_size() for _, v, i in self.blocks for t in (v, i) if t is not None)

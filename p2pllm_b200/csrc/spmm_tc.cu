@@ -32,10 +32,14 @@
 #include <utility>
 
 #include "common.cuh"
+#include "sm100.cuh"
 #include "tc_layout.cuh"
+#include "tma_host.cuh"
 
 namespace p2p {
 namespace {
+
+using namespace sm100;
 
 constexpr int kGroupWarps = 8;                                     // warps expanding one tile (16 rows each)
 constexpr int kGroups = 2;                                         // groups taking alternate column tiles
@@ -92,157 +96,6 @@ struct TcParams {
     int hold_tile;                    // a test's withheld x tile (each CTA's tile of that index is never loaded), or -1
 };
 
-__device__ __forceinline__ void cluster_sync_all() {
-    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
-
-// The shared::cluster address of `saddr` (this CTA's shared memory) in cluster CTA `rank`.
-__device__ __forceinline__ uint32_t cluster_addr(uint32_t saddr, int rank) {
-    uint32_t r;
-    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
-    return r;
-}
-
-__device__ __forceinline__ float4 ld_cluster_f4(uint32_t addr) {
-    float4 v;
-    asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
-                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
-                 : "r"(addr)
-                 : "memory");
-    return v;
-}
-
-__device__ __forceinline__ uint32_t smem_u32(const void* p) {
-    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-
-__device__ __forceinline__ uint64_t now_ns() {
-    uint64_t t;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-    return t;
-}
-
-__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
-}
-
-// One test of the phase; a thread whose phase is not complete sleeps in hardware (up to the suspend-time hint, in ns)
-// until it completes, instead of spinning on the issue slots its warp scheduler shares with working warps.
-__device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
-    uint32_t ok;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(ok)
-        : "r"(bar), "r"(parity), "r"(1000000u)
-        : "memory");
-    return ok != 0;
-}
-
-__device__ __forceinline__ void give_up(int where, unsigned seq) {
-    atomicCAS(&g_tc_error, 0, where);
-    atomicExch(&g_tc_failed_seq, seq);
-}
-
-// Waits for the phase of parity `parity`; true once it completed. Past `limit_ns`, or at once when another wait of
-// the same launch has given up, it records `where` and returns false: the caller then issues no further work.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int where, uint64_t limit_ns, unsigned seq) {
-    if (mbar_try(bar, parity)) return true;
-    const uint64_t t0 = now_ns();
-    while (!mbar_try(bar, parity)) {
-        if (*(volatile unsigned*)&g_tc_failed_seq == seq || now_ns() - t0 > limit_ns) {
-            give_up(where, seq);
-            return false;
-        }
-    }
-    return true;
-}
-
-// Waits for asynchronous work this CTA already issued (a TMA load landing, its MMAs completing), which finishes on its
-// own: bounded by `limit_ns` only, even after another wait gave up, so the CTA never exits with that work in flight.
-__device__ __forceinline__ bool mbar_drain(uint32_t bar, uint32_t parity, int where, uint64_t limit_ns, unsigned seq) {
-    const uint64_t t0 = now_ns();
-    while (!mbar_try(bar, parity)) {
-        if (now_ns() - t0 > limit_ns) {
-            give_up(where, seq);
-            return false;
-        }
-    }
-    return true;
-}
-
-// Ring position of the next item: `step` slots on (step <= n), the phase bit flipping at each wrap. Kept in
-// registers, so the single-thread roles do no divisions by the runtime ring sizes.
-__device__ __forceinline__ void advance(int& slot, uint32_t& phase, int step, int n) {
-    slot += step;
-    if (slot >= n) {
-        slot -= n;
-        phase ^= 1u;
-    }
-}
-
-__device__ __forceinline__ void sts_u16(uint32_t addr, uint32_t v) {
-    asm volatile("st.shared.u16 [%0], %1;" ::"r"(addr), "h"((unsigned short)v) : "memory");
-}
-
-__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
-}
-
-__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
-}
-
-__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int c0, int c1, uint32_t bar) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
-        "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(bar)
-        : "memory");
-}
-
-// Shared-memory matrix descriptor of a K-major tile in the 128-byte swizzle layout: rows of 128 bytes, 8-row atoms of
-// 1024 bytes (stride byte offset), version 1, swizzle mode 2 (128B).
-__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
-    return (uint64_t)((saddr & 0x3FFFFu) >> 4) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
-           ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
-}
-
-// Instruction descriptor of kind::f16: D fp32, A and B bf16 (or both f16), both K-major, M = 128, N.
-template <typename T> __device__ __forceinline__ uint32_t idesc_f16(int n) {
-    constexpr uint32_t ab = std::is_same<T, __nv_bfloat16>::value ? 1u : 0u;
-    return (1u << 4) | (ab << 7) | (ab << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
-}
-
-__device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accumulate) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-        "l"(a), "l"(b), "r"(idesc), "r"(accumulate)
-        : "memory");
-}
-
-__device__ __forceinline__ void umma_commit(uint32_t bar) {
-    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
-}
-
-__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
-    uint32_t r[16];
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, "
-        "[%16];"
-        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
-          "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-        : "r"(taddr));
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-    for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
-}
-
 // A warp's share of one segment's words: the entries of its 16 rows (8-row groups 2 wg and 2 wg + 1), [lo, hi) in
 // words from the CTA's first segment, from the segment's header (cumulative counts of its 8-row groups).
 __device__ __forceinline__ void warp_piece(const int64_t* offs, const uint16_t* hdr, int i, int wg, int& lo, int& hi) {
@@ -283,12 +136,6 @@ __device__ __forceinline__ void l2_prefetch(const void* src, uint32_t bytes) {
     asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
 }
 
-__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, uint32_t src, int c0, int c1) {
-    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
-                     reinterpret_cast<uint64_t>(map)),
-                 "r"(c0), "r"(c1), "r"(src)
-                 : "memory");
-}
 
 // kL2: the launch prefetches segments into L2 ahead of the register loads (few tokens; see the expanders).
 template <typename T, bool kL2>
@@ -317,6 +164,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const uint32_t done = bars + 8u * (2 * kMaxASlots + 2 * kMaxXSlots);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const WaitCtl wc{&g_tc_error, &g_tc_failed_seq, p.wait_ns, p.seq};
     // This CTA's row tile, column split, tokens, and where its rows start in x and y (a plain launch: every token,
     // row tile blockIdx.x of the module; a grouped one: its item's tokens, row tile blockIdx.x of its expert).
     int rt, split, tokens, n_total;
@@ -388,7 +236,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             int uses = 0;                                           // loads issued into slot s
             for (int i = lane; i < nk; i += SX) {
                 if (i >= SX) {
-                    if (!mbar_wait(emptyx(s), ph, 1, p.wait_ns, p.seq)) break;
+                    if (!mbar_wait(emptyx(s), ph, 1, wc)) break;
                     ph ^= 1u;
                 }
                 if (i == p.hold_tile) break;                        // a test withholds this load
@@ -400,7 +248,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             }
             // The slot's last load must have landed before the CTA exits (the TMA unit writes its shared memory): on
             // a normal run the MMA consumed it long ago; after a give-up this waits for the copy itself.
-            if (uses) mbar_drain(fullx(s), (uint32_t)((uses - 1) & 1), 7, p.wait_ns, p.seq);
+            if (uses) mbar_drain(fullx(s), (uint32_t)((uses - 1) & 1), 7, wc);
         }
         __syncwarp();
     } else if (warp == kMmaWarp || warp == kMmaWarp + 1) {
@@ -421,8 +269,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             int sa = by_tile ? j : 0, sx = sa;
             uint32_t pha = 0, phx = 0, acc = 0;
             for (int i = by_tile ? j : 0; i < nk; i += step) {
-                if (!mbar_wait(fulla(sa), pha, 2, p.wait_ns, p.seq)) break;     // no MMA on a tile not there
-                if (!mbar_wait(fullx(sx), phx, 3, p.wait_ns, p.seq)) break;
+                if (!mbar_wait(fulla(sa), pha, 2, wc)) break;     // no MMA on a tile not there
+                if (!mbar_wait(fullx(sx), phx, 3, wc)) break;
                 tc_fence_after();
                 const uint64_t a_desc = a0 + (uint64_t)((sa * kASlotBytes) >> 4);
                 const uint64_t b_desc = b0 + (uint64_t)((sx * p.b_bytes) >> 4);
@@ -490,13 +338,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 }
                 if (i + kGroups < nk) {
                     int ok = 1;
-                    if (lane == 0 && i + kGroups >= SA) ok = mbar_wait(emptya(sn), pn ^ 1u, 5, p.wait_ns, p.seq);
+                    if (lane == 0 && i + kGroups >= SA) ok = mbar_wait(emptya(sn), pn ^ 1u, 5, wc);
                     if (!__shfl_sync(0xffffffffu, ok, 0)) return false;
                     zero_rows(sn);                      // ordered before its scatter by this tile's fence + sync
                 }
             } else {
                 int ok = 1;
-                if (lane == 0 && i >= SA) ok = mbar_wait(emptya(s), ph ^ 1u, 5, p.wait_ns, p.seq);
+                if (lane == 0 && i >= SA) ok = mbar_wait(emptya(s), ph ^ 1u, 5, wc);
                 if (!__shfl_sync(0xffffffffu, ok, 0)) return false;
                 zero_rows(s);
                 __syncwarp();                                                // the warp's rows zeroed
@@ -536,7 +384,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         // Epilogue: D[row, token] out of TMEM, once every MMA of both issuers has completed (also after a give-up:
         // TMEM is freed below, and no MMA may still write it). Warp w reads lanes 32 (w % 4) .. + 31, every other
         // 16-column chunk.
-        if (lane == 0) mbar_drain(done, 0, 6, p.wait_ns, p.seq);
+        if (lane == 0) mbar_drain(done, 0, 6, wc);
         __syncwarp();
         tc_fence_after();
         const int quarter = warp & 3, cgroup = warp >> 2;          // 4 column groups of the 16 expander warps
@@ -685,31 +533,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     if (threadIdx.x == 0) p.tickets[rt] = 0u;            // the workspace is zeroed again for the next call
 }
 
-typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-EncodeTiledFn encode_fn() {
-    static EncodeTiledFn fn = nullptr;
-    if (!fn) {
-        void* ptr = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
-            q == cudaDriverEntryPointSuccess)
-            fn = reinterpret_cast<EncodeTiledFn>(ptr);
-    }
-    return fn;
-}
-
 struct TcPlan {
     int n_total, box_rows, n_boxes, tmem_cols, acc_stride, a_slots, x_slots, b_bytes, n_split, kt_per_split, smem;
 };
-
-int pow2_at_least(int v) {
-    int p = 32;
-    while (p < v) p <<= 1;
-    return p;
-}
 
 // Token-dependent part of a launch plan: MMA N, x boxes, TMEM columns, ring depths, shared memory. Fails when the
 // tokens do not fit shared memory.
@@ -736,37 +562,6 @@ int plan_tokens(int tn, TcPlan& pl) {
     pl.a_slots &= ~1;
     if (pl.a_slots < 2) return fail(P2P_EUNSUPPORTED, "p2p_spmm_tc: %d tokens exceed shared memory", tn);
     pl.smem = fixed + pl.a_slots * kASlotBytes + pl.x_slots * pl.b_bytes;
-    return P2P_OK;
-}
-
-// The TMA map of x [rows, cols] (row stride ldx elements): boxes of 64 columns x box_rows rows, 128-byte swizzle.
-int encode_x_map(CUtensorMap* map, const void* x, int dtype, int64_t rows, int64_t cols, int64_t ldx, int box_rows) {
-    EncodeTiledFn encode = encode_fn();
-    if (!encode) return fail(P2P_ECUDA, "p2p_spmm_tc: cuTensorMapEncodeTiled unavailable");
-    const cuuint64_t gdim[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
-    const cuuint64_t gstride[1] = {(cuuint64_t)(ldx * 2)};
-    const cuuint32_t box[2] = {(cuuint32_t)tc::kTileCols, (cuuint32_t)box_rows};
-    const cuuint32_t estride[2] = {1, 1};
-    CUresult r = encode(map, dtype == P2P_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
-                        const_cast<void*>(x), gdim, gstride, box, estride, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    if (r != CUDA_SUCCESS) return fail(P2P_ECUDA, "p2p_spmm_tc: tensor map encode failed (%d)", (int)r);
-    return P2P_OK;
-}
-
-// The TMA map of y [tokens, rows] (row stride ldy elements) for the epilogue's stores: boxes of 128 rows x box_rows
-// tokens, no swizzle.
-int encode_y_map(CUtensorMap* map, void* y, int dtype, int64_t tokens, int64_t rows, int64_t ldy, int box_rows) {
-    EncodeTiledFn encode = encode_fn();
-    if (!encode) return fail(P2P_ECUDA, "p2p_spmm_tc: cuTensorMapEncodeTiled unavailable");
-    const cuuint64_t gdim[2] = {(cuuint64_t)rows, (cuuint64_t)tokens};
-    const cuuint64_t gstride[1] = {(cuuint64_t)(ldy * 2)};
-    const cuuint32_t box[2] = {(cuuint32_t)tc::kTileRows, (cuuint32_t)box_rows};
-    const cuuint32_t estride[2] = {1, 1};
-    CUresult r = encode(map, dtype == P2P_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, y,
-                        gdim, gstride, box, estride, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
-                        CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    if (r != CUDA_SUCCESS) return fail(P2P_ECUDA, "p2p_spmm_tc: y tensor map encode failed (%d)", (int)r);
     return P2P_OK;
 }
 

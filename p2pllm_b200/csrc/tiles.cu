@@ -4,7 +4,14 @@
 //
 //   p2p_tiles_plan: per (row, column tile) counts -> per segment prefix of rows -> padded segment sizes -> seg[]
 //   p2p_tiles_fill: every kept weight to seg[segment] + (rows above it in the segment) + (its rank in its row's part)
+//
+// It also builds the bitmask layout of mask_layout.cuh (the reference's storage, p2p/compact.py:36-45, re-tiled for
+// spmm_mask.cu), one CTA a segment:
+//   p2p_mask_plan: each segment's kept weights -> its byte size -> seg[]
+//   p2p_mask_fill: the segment's 128 x 64 tile in shared memory -> piece masks, their counts and offsets -> header,
+//                  masks and values
 #include "common.cuh"
+#include "mask_layout.cuh"
 #include "tc_layout.cuh"
 
 namespace p2p {
@@ -314,6 +321,120 @@ __global__ void __launch_bounds__(kOrderWarps * 32) bank_order_kernel(const int6
     }
 }
 
+// ---- the bitmask layout (mask_layout.cuh) ---------------------------------------------------------------------------
+
+// [lo, hi): row lr's entries of block b in columns [c0, c0 + 64), by binary search of its ascending indices.
+template <typename I>
+__device__ __forceinline__ void row_range(const p2p_row_block& b, int64_t lr, int c0, int64_t& lo, int64_t& hi) {
+    if (!b.idx) {
+        lo = c0;
+        hi = c0 + mk::kTileCols < b.k ? c0 + mk::kTileCols : b.k;
+        return;
+    }
+    const I* ix = reinterpret_cast<const I*>(b.idx) + lr * b.ld;
+    auto lower = [&](int v) {
+        int64_t a = 0, z = b.k;
+        while (a < z) {
+            const int64_t m = (a + z) >> 1;
+            if ((int)ix[m] < v) a = m + 1; else z = m;
+        }
+        return a;
+    };
+    lo = lower(c0);
+    hi = lower(c0 + mk::kTileCols);
+}
+
+// segbytes[segment] = the segment's size in bytes (one CTA of 128 threads a segment, a thread a row).
+template <typename I>
+__global__ void __launch_bounds__(mk::kTileRows) mask_count_kernel(Blocks bl, int64_t rows, int n_ct, int64_t n_seg,
+                                                                    int64_t* __restrict__ segbytes) {
+    __shared__ int total;
+    for (int64_t sg = blockIdx.x; sg < n_seg; sg += gridDim.x) {
+        if (threadIdx.x == 0) total = 0;
+        __syncthreads();
+        const int64_t row = (sg / n_ct) * mk::kTileRows + threadIdx.x;
+        const int c0 = (int)(sg % n_ct) * mk::kTileCols;
+        const int bi = row < rows ? block_of(bl, row) : -1;
+        if (bi >= 0) {
+            int64_t lo, hi;
+            row_range<I>(bl.b[bi], row - bl.b[bi].row0, c0, lo, hi);
+            if (hi > lo) atomicAdd(&total, (int)(hi - lo));
+        }
+        __syncthreads();
+        if (threadIdx.x == 0) segbytes[sg] = mk::segment_bytes(total);
+        __syncthreads();
+    }
+}
+
+// Writes every segment: its tile gathered into shared memory (values and keep bits by row), then thread t builds
+// piece t % 16 of block t / 16 (its mask, its count), the counts are scanned in piece order, and each thread writes its
+// piece's mask and values. Indices out of ascending order within a tile, or past the columns, are counted as errors.
+template <typename I>
+__global__ void __launch_bounds__(mk::kTileRows) mask_fill_kernel(Blocks bl, int64_t rows, int64_t cols, int n_ct,
+                                                                   int64_t n_seg, const int64_t* __restrict__ seg,
+                                                                   uint8_t* __restrict__ data, int64_t n_bytes) {
+    __shared__ uint16_t tile[mk::kTileRows][mk::kTileCols];
+    __shared__ uint32_t keep[mk::kTileRows][2];
+    __shared__ int off[mk::kTileRows + 1];
+    const int t = threadIdx.x;
+    for (int64_t sg = blockIdx.x; sg < n_seg; sg += gridDim.x) {
+        const int64_t row = (sg / n_ct) * mk::kTileRows + t;
+        const int c0 = (int)(sg % n_ct) * mk::kTileCols;
+        uint32_t k0 = 0, k1 = 0;
+        const int bi = row < rows ? block_of(bl, row) : -1;
+        if (bi >= 0) {
+            const p2p_row_block& b = bl.b[bi];
+            const int64_t lr = row - b.row0;
+            int64_t lo, hi;
+            row_range<I>(b, lr, c0, lo, hi);
+            const uint16_t* vals = reinterpret_cast<const uint16_t*>(b.vals) + lr * b.ld;
+            int prev = -1;
+            for (int64_t j = lo; j < hi; ++j) {
+                const int c = b.idx ? (int)reinterpret_cast<const I*>(b.idx)[lr * b.ld + j] : (int)j;
+                if (c <= prev || c < c0 || c >= c0 + mk::kTileCols || c >= cols) {
+                    atomicAdd(&g_fill_errors, 1);
+                    continue;
+                }
+                prev = c;
+                tile[t][c - c0] = vals[j];
+                if (c - c0 < 32) k0 |= 1u << (c - c0); else k1 |= 1u << (c - c0 - 32);
+            }
+        }
+        keep[t][0] = k0;
+        keep[t][1] = k1;
+        __syncthreads();
+        const int blk = t >> 4, p = t & 15;
+        uint32_t m[2] = {0u, 0u};
+        for (int bit = 0; bit < 64; ++bit) {
+            const int r = blk * mk::kBlockRows + mk::piece_row(p, bit), c = mk::piece_col(p, bit);
+            if ((keep[r][c >> 5] >> (c & 31)) & 1u) m[bit >> 5] |= 1u << (bit & 31);
+        }
+        const int n = __popc(m[0]) + __popc(m[1]);
+        off[t + 1] = n;
+        __syncthreads();
+        if (t == 0) {
+            off[0] = 0;
+            for (int q = 1; q <= mk::kTileRows; ++q) off[q] += off[q - 1];
+        }
+        __syncthreads();
+        const int64_t base = seg[sg];
+        const int64_t end = mk::segment_bytes(off[mk::kTileRows]);
+        if (base + end <= n_bytes && seg[sg + 1] - base == end) {
+            uint8_t* d = data + base;
+            if (t < mk::kBlocks) reinterpret_cast<uint16_t*>(d)[t] = (uint16_t)off[16 * (t + 1)];
+            reinterpret_cast<uint2*>(d + mk::kHeaderBytes)[t] = make_uint2(m[0], m[1]);
+            uint16_t* v = reinterpret_cast<uint16_t*>(d + mk::kValuesAt) + off[t];
+            for (int bit = 0; bit < 64; ++bit)
+                if ((m[bit >> 5] >> (bit & 31)) & 1u)
+                    *v++ = tile[blk * mk::kBlockRows + mk::piece_row(p, bit)][mk::piece_col(p, bit)];
+            for (int64_t z = mk::kValuesAt + 2 * (int64_t)off[mk::kTileRows] + t; z < end; z += mk::kTileRows) d[z] = 0;
+        } else if (t == 0) {
+            atomicAdd(&g_fill_errors, 1);                       // seg[] does not fit this module: write nothing
+        }
+        __syncthreads();
+    }
+}
+
 int check_blocks(const p2p_row_block* blocks, int nblocks, int idx_bytes, int64_t cols, Blocks& bl, const char* who) {
     if (!blocks || nblocks < 1 || nblocks > kMaxBlocks) return fail(P2P_EINVAL, "%s: 1 to %d row blocks", who, kMaxBlocks);
     if (idx_bytes != 2 && idx_bytes != 4) return fail(P2P_EINVAL, "%s: idx_bytes %d", who, idx_bytes);
@@ -434,5 +555,66 @@ extern "C" int p2p_tiles_fill(const p2p_row_block* blocks, int nblocks, int idx_
         cudaStreamSynchronize(st) != cudaSuccess)
         return launch_status("p2p_tiles_fill read-back");
     if (bad) return fail(P2P_EDATA, "p2p_tiles_fill: %d column indices out of ascending order", bad);
+    return P2P_OK;
+}
+
+extern "C" size_t p2p_mask_workspace(const p2p_row_block* blocks, int nblocks, int64_t cols) {
+    if (!blocks || nblocks < 1 || cols < 1) return 0;
+    const Shape s = shape_of(blocks, nblocks, cols);
+    return (size_t)s.n_seg * sizeof(int64_t) + 256;
+}
+
+extern "C" int p2p_mask_plan(const p2p_row_block* blocks, int nblocks, int idx_bytes, int64_t cols, int64_t* seg,
+                             int64_t* total_bytes, void* workspace, size_t workspace_bytes, void* stream) {
+    Blocks bl;
+    if (int e = check_blocks(blocks, nblocks, idx_bytes, cols, bl, "p2p_mask_plan")) return e;
+    P2P_REQUIRE(seg && total_bytes && workspace, "p2p_mask_plan: null seg, total or workspace");
+    P2P_REQUIRE(workspace_bytes >= p2p_mask_workspace(blocks, nblocks, cols), "p2p_mask_plan: workspace too small");
+    const Shape s = shape_of(blocks, nblocks, cols);
+    cudaStream_t st = as_stream(stream);
+    int64_t* segbytes = reinterpret_cast<int64_t*>(workspace);
+    const int grid = (int)(s.n_seg < sm_count() * 16 ? s.n_seg : sm_count() * 16);
+    if (s.n_seg > 0) {
+        if (idx_bytes == 2)
+            mask_count_kernel<int16_t><<<grid, mk::kTileRows, 0, st>>>(bl, s.rows, (int)s.col_tiles, s.n_seg, segbytes);
+        else
+            mask_count_kernel<int32_t><<<grid, mk::kTileRows, 0, st>>>(bl, s.rows, (int)s.col_tiles, s.n_seg, segbytes);
+    }
+    scan_kernel<<<1, 1024, 0, st>>>(segbytes, s.n_seg, seg);
+    if (int e = launch_status("p2p_mask_plan")) return e;
+    if (cudaMemcpyAsync(total_bytes, seg + s.n_seg, sizeof(int64_t), cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+        cudaStreamSynchronize(st) != cudaSuccess)
+        return launch_status("p2p_mask_plan read-back");
+    return P2P_OK;
+}
+
+extern "C" int p2p_mask_fill(const p2p_row_block* blocks, int nblocks, int idx_bytes, int64_t cols, int dtype,
+                             const int64_t* seg, void* data, int64_t n_bytes, void* stream) {
+    Blocks bl;
+    if (int e = check_blocks(blocks, nblocks, idx_bytes, cols, bl, "p2p_mask_fill")) return e;
+    if (dtype != P2P_BF16 && dtype != P2P_F16)
+        return fail(P2P_EUNSUPPORTED, "p2p_mask_fill: the bitmask layout holds bf16 or f16 values");
+    P2P_REQUIRE(seg && data && n_bytes >= 0, "p2p_mask_fill: null pointer");
+    P2P_REQUIRE(aligned16(data), "p2p_mask_fill: data must start on a 16-byte boundary");
+    const Shape s = shape_of(blocks, nblocks, cols);
+    cudaStream_t st = as_stream(stream);
+    const int zero = 0;
+    if (cudaMemcpyToSymbolAsync(g_fill_errors, &zero, sizeof(int), 0, cudaMemcpyHostToDevice, st) != cudaSuccess)
+        return launch_status("p2p_mask_fill reset");
+    const int grid = (int)(s.n_seg < sm_count() * 16 ? s.n_seg : sm_count() * 16);
+    if (s.n_seg > 0) {
+        if (idx_bytes == 2)
+            mask_fill_kernel<int16_t><<<grid, mk::kTileRows, 0, st>>>(bl, s.rows, cols, (int)s.col_tiles, s.n_seg, seg,
+                                                                       reinterpret_cast<uint8_t*>(data), n_bytes);
+        else
+            mask_fill_kernel<int32_t><<<grid, mk::kTileRows, 0, st>>>(bl, s.rows, cols, (int)s.col_tiles, s.n_seg, seg,
+                                                                       reinterpret_cast<uint8_t*>(data), n_bytes);
+    }
+    if (int e = launch_status("p2p_mask_fill")) return e;
+    int bad = 0;
+    if (cudaMemcpyFromSymbolAsync(&bad, g_fill_errors, sizeof(int), 0, cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+        cudaStreamSynchronize(st) != cudaSuccess)
+        return launch_status("p2p_mask_fill read-back");
+    if (bad) return fail(P2P_EDATA, "p2p_mask_fill: %d column indices out of ascending order or range", bad);
     return P2P_OK;
 }

@@ -244,6 +244,54 @@ def tiles_build(blocks: list, cols: int) -> tuple:
     return words, seg, seg_cap
 
 
+def mask_build(blocks: list, cols: int) -> tuple:
+    """The bitmask layout (data uint8, seg int64 byte offsets) of a module's row blocks [(row0, values, idx | None)],
+    bf16 or f16 values, ascending column indices. Load time; syncs."""
+    dev = blocks[0][1].device
+    table, idx_bytes = _row_table(blocks)
+    lib = _lib.load()
+    need = lib.p2p_mask_workspace(table, len(blocks), cols)
+    ws = torch.empty(max(need, 1), dtype=torch.uint8, device=dev)
+    rows = max(r0 + v.shape[0] for r0, v, _ in blocks)
+    n_seg = -(-rows // 128) * -(-cols // 64)
+    seg = torch.empty(n_seg + 1, dtype=torch.int64, device=dev)
+    total = ctypes.c_int64(0)
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    call("p2p_mask_plan", table, len(blocks), idx_bytes, cols, ptr(seg), ctypes.byref(total), ptr(ws), ws.numel(),
+         stream)
+    data = torch.empty(max(total.value, 16), dtype=torch.uint8, device=dev)
+    call("p2p_mask_fill", table, len(blocks), idx_bytes, cols, dtype_code(blocks[0][1]), ptr(seg), ptr(data),
+         total.value, stream)
+    return data, seg
+
+
+def spmm_mask(x: torch.Tensor, data: torch.Tensor, seg: torch.Tensor, rows: int, cols: int,
+              out: torch.Tensor | None = None) -> torch.Tensor:
+    """y [tokens, rows] = x [tokens, cols] times a module in the bitmask layout (tcgen05, weights in TMEM)."""
+    require_cuda(x)
+    if x.dim() != 2 or x.shape[1] != cols:
+        raise P2PError(f"x of {tuple(x.shape)} does not have {cols} columns")
+    if x.stride(1) != 1 or x.stride(0) % 8 or x.data_ptr() % 16:
+        x = x.contiguous()
+        if x.data_ptr() % 16:
+            x = x.clone()
+    out = _out(out, (x.shape[0], rows), x)
+    lib = _lib.load()
+    need = lib.p2p_spmm_mask_workspace(rows, cols, x.shape[0])
+    ws = _workspace(x.device, need, "spmm_mask") if need else None
+    call("p2p_spmm_mask", ptr(x), dtype_code(x), x.shape[0], cols, x.stride(0), ptr(data), ptr(seg), rows, ptr(out),
+         out.stride(0), ptr(ws), 0 if ws is None else ws.numel(), stream_of(x))
+    if CHECK_WAITS:
+        spmm_mask_status(x.device)
+    return out
+
+
+def spmm_mask_status(device=None, reset: bool = True) -> None:
+    """Raises if a bitmask-layout GEMM launch gave up waiting on its pipeline since the last reset. Syncs."""
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    call("p2p_spmm_mask_status", int(reset), torch.cuda.current_stream(dev).cuda_stream)
+
+
 def spmm_tc(x: torch.Tensor, words: torch.Tensor, seg: torch.Tensor, rows: int, cols: int, seg_cap: int,
             out: torch.Tensor | None = None) -> torch.Tensor:
     """y [tokens, rows] = x [tokens, cols] times a module in the tensor-core layout (tcgen05, bf16/f16)."""
