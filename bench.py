@@ -56,10 +56,14 @@ def parse():
     p.add_argument("--tokens", type=int, default=272)
     p.add_argument("--calib-tokens", type=int, default=128 * 2048)
     p.add_argument("--no-cpu-baseline", action="store_true")
-    p.add_argument("--workload", default="cfg2", choices=["cfg2", "cfg1", "cfg3", "cfg5"],
+    p.add_argument("--workload", default="cfg2", choices=["cfg2", "cfg1", "cfg3", "cfg5", "module"],
                    help="cfg2 (default): the headline line. cfg1, cfg3, cfg5: one extra line each on one GPU (config "
                         "1's fp32 projection; config 3's replica block + group combine at T = 1, 8, 32, 64; a "
-                        "Qwen2.5-32B replica layer at keep 40)")
+                        "Qwen2.5-32B replica layer at keep 40). module: one module of the cfg2 layer (--module, "
+                        "--layout), --steps launches, for profiling")
+    p.add_argument("--module", default="gate_up_proj", choices=list(MODULES))
+    p.add_argument("--layout", default=None, choices=["tc", "mask"],
+                   help="the tensor-core layout of the compact modules (default: the package's)")
     return p.parse_args()
 
 
@@ -533,6 +537,23 @@ def run_extra(args):
         line.update(metric="config-3 replica member + combine tokens/s (keep 40 MLP block, hidden 4096)",
                     value=per_t[64]["tokens_per_s"], unit="tokens/s", per_tokens=per_t, dtype="bf16",
                     note="synthetic residual-MLP block stands in for a decoder layer (no KV cache here)")
+    elif args.workload == "module":
+        # one module of the cfg2 layer, --steps launches at --tokens tokens (each behind a spin), for profiling
+        from p2pllm_b200 import compact as cp
+        layer = ReplicaLayer(seed=0, tokens=args.tokens, calib_tokens=args.calib_tokens, device=device)
+        names = MODULES[args.module][1]
+        blocks = [("compact", *layer.selected[n], layer.proj[n].cols) for n in names]
+        tiles = cp.Tiles(blocks, layout=args.layout)
+        x = layer.inputs[MODULES[args.module][0]]
+        us = _timed_us(lambda: tiles(x), max(3, args.steps))
+        alg = layer.algorithmic_bytes(args.module, args.tokens)
+        fmt = layer.mask_format_bytes(args.module) + args.tokens * (layer.cols(args.module) + layer.rows(args.module)) * 2
+        line.update(metric=f"{args.module} launch us (cfg2 layer, T={args.tokens}, layout {tiles.layout})", value=us,
+                    unit="us", higher_is_better=False, layout=tiles.layout, tokens=args.tokens,
+                    bytes_read_and_written=tiles.nbytes() + args.tokens * (layer.cols(args.module)
+                                                                           + layer.rows(args.module)) * 2,
+                    hbm_gbs=(tiles.nbytes() + args.tokens * (layer.cols(args.module) + layer.rows(args.module)) * 2)
+                    / us / 1e3, index_format_bytes=alg, mask_format_bytes=fmt, dtype="bf16")
     else:
         # a Qwen2.5-32B replica layer (keep 40 everywhere), T = 17
         layer = ReplicaLayer(seed=0, tokens=17, calib_tokens=args.calib_tokens, device=device,

@@ -261,8 +261,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int blk = 2 * (wb & 3) + (wb >> 2);                 // (w % 4) == blk / 2: the lanes this warp may write
         const int g = lane >> 2;
         const uint32_t q = 8u * (g & 3) + 2u * (lane & 3);        // this lane's first bit in its 32-bit mask word
-        const bool hi_lane = g >= 4;                              // rows 4..7 of a piece: its mask's upper word
         const uint32_t below = (1u << q) - 1u;
+        // Rows 0..3 of a piece (g < 4) read the lo words and offsets, rows 4..7 the hi ones.
+        const uint32_t words_at = (uint32_t)(mk::kHeaderBytes + mk::kBlockBytes * blk + (g >= 4 ? mk::kHiAt : 0));
+        const uint32_t offs_at = (uint32_t)(mk::kHeaderBytes + mk::kBlockBytes * blk + (g >= 4 ? mk::kOhiAt : mk::kOloAt));
         const uint32_t t_lanes = (uint32_t)(16 * blk) << 16;
         int ticket = grp, sa = grp % SA;
         uint32_t tph = 0, aph = 0;
@@ -274,26 +276,28 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (!__all_sync(0xffffffffu, ok)) break;
             tc_fence_after();                                           // TMEM stores after the MMAs' reads
             const uint32_t segp = ring + s_ring_off[ticket];
-            const uint32_t hdr = blk ? lds_u16(segp + 2u * (blk - 1)) : 0u;
-            uint32_t vb = segp + (uint32_t)mk::kValuesAt + 2u * hdr;   // this block's first value
-            const uint32_t mb = segp + (uint32_t)mk::kHeaderBytes + 128u * blk;
+            const uint32_t vals = segp + (uint32_t)mk::kValuesAt;
+            uint32_t w[16], o[8];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const uint4 v = lds_v4(segp + words_at + 16u * k);    // two addresses a warp: broadcasts
+                w[4 * k] = v.x; w[4 * k + 1] = v.y; w[4 * k + 2] = v.z; w[4 * k + 3] = v.w;
+            }
+#pragma unroll
+            for (int k = 0; k < 2; ++k) {
+                const uint4 v = lds_v4(segp + offs_at + 16u * k);
+                o[4 * k] = v.x; o[4 * k + 1] = v.y; o[4 * k + 2] = v.z; o[4 * k + 3] = v.w;
+            }
             uint32_t r[16];
 #pragma unroll
-            for (int pp = 0; pp < 16; pp += 2) {
-                const uint4 m = lds_v4(mb + 8u * pp);                 // pieces pp and pp + 1 (every lane: a broadcast)
-#pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                    const uint32_t lo = h ? m.z : m.x, hi = h ? m.w : m.y;
-                    const uint32_t clo = __popc(lo);
-                    const uint32_t w = hi_lane ? hi : lo;
-                    const uint32_t at = (hi_lane ? clo : 0u) + __popc(w & below);   // this lane's first value
-                    const uint32_t a0 = vb + 2u * at;
-                    const uint32_t k0 = bfe_s(w, q), k1 = bfe_s(w, q + 1);
-                    const uint32_t va = lds_u16(a0);
-                    const uint32_t vbv = lds_u16(a0 - 2u * k0);             // the next value if bit q is set
-                    r[pp + h] = __byte_perm(va, vbv, 0x5410) & ((k0 & 0x0000ffffu) | (k1 & 0xffff0000u));
-                    vb += 2u * (clo + __popc(hi));
-                }
+            for (int pp = 0; pp < 16; ++pp) {
+                const uint32_t start = (pp & 1) ? (o[pp >> 1] >> 16) : (o[pp >> 1] & 0xffffu);   // bytes
+                const uint32_t a0 = vals + start + 2u * __popc(w[pp] & below);   // this lane's first value
+                const uint32_t x = w[pp] >> q;
+                const uint32_t b0 = x & 1u;                             // its two weights kept? (bits 0, 1 of x)
+                const uint32_t va = lds_u16(a0);
+                const uint32_t vn = lds_u16(a0 + 2u * b0);              // the next value if the first is kept
+                r[pp] = va * b0 + vn * ((x & 2u) << 15);                // (va if kept) | (vn if kept) << 16
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(sempty(ticket));                 // this warp is done with the segment

@@ -368,7 +368,7 @@ __global__ void __launch_bounds__(mk::kTileRows) mask_count_kernel(Blocks bl, in
 
 // Writes every segment: its tile gathered into shared memory (values and keep bits by row), then thread t builds
 // piece t % 16 of block t / 16 (its mask, its count), the counts are scanned in piece order, and each thread writes its
-// piece's mask and values. Indices out of ascending order within a tile, or past the columns, are counted as errors.
+// piece's mask words, the start offsets of its two halves and its values. Indices out of ascending order within a tile, or past the columns, are counted as errors.
 template <typename I>
 __global__ void __launch_bounds__(mk::kTileRows) mask_fill_kernel(Blocks bl, int64_t rows, int64_t cols, int n_ct,
                                                                    int64_t n_seg, const int64_t* __restrict__ seg,
@@ -422,7 +422,11 @@ __global__ void __launch_bounds__(mk::kTileRows) mask_fill_kernel(Blocks bl, int
         if (base + end <= n_bytes && seg[sg + 1] - base == end) {
             uint8_t* d = data + base;
             if (t < mk::kBlocks) reinterpret_cast<uint16_t*>(d)[t] = (uint16_t)off[16 * (t + 1)];
-            reinterpret_cast<uint2*>(d + mk::kHeaderBytes)[t] = make_uint2(m[0], m[1]);
+            uint8_t* bd = d + mk::kHeaderBytes + blk * mk::kBlockBytes;
+            reinterpret_cast<uint32_t*>(bd)[p] = m[0];
+            reinterpret_cast<uint32_t*>(bd + mk::kHiAt)[p] = m[1];
+            reinterpret_cast<uint16_t*>(bd + mk::kOloAt)[p] = (uint16_t)(2 * off[t]);
+            reinterpret_cast<uint16_t*>(bd + mk::kOhiAt)[p] = (uint16_t)(2 * (off[t] + __popc(m[0])));
             uint16_t* v = reinterpret_cast<uint16_t*>(d + mk::kValuesAt) + off[t];
             for (int bit = 0; bit < 64; ++bit)
                 if ((m[bit >> 5] >> (bit & 31)) & 1u)

@@ -38,7 +38,8 @@ def _check(got, want):
 
 
 def decode(data: np.ndarray, seg: np.ndarray, rows: int, cols: int):
-    """(values [rows, cols] uint16, kept [rows, cols] bool) of a bitmask layout, checking its header and sizes."""
+    """(values [rows, cols] uint16, kept [rows, cols] bool) of a bitmask layout, checking its header, the start
+    offsets of every half-piece and the sizes."""
     n_ct = -(-cols // 64)
     n_rt = -(-rows // 128)
     vals = np.zeros((n_rt * 128, n_ct * 64), np.uint16)
@@ -48,14 +49,22 @@ def decode(data: np.ndarray, seg: np.ndarray, rows: int, cols: int):
         assert seg[sg] % 16 == 0
         b = data[seg[sg]:seg[sg + 1]]
         hdr = b[:16].view(np.uint16).astype(np.int64)
-        masks = b[16:1040].view(np.uint8).reshape(8, 16, 8)
-        bits = np.unpackbits(masks, axis=-1, bitorder="little").astype(bool)        # [block, piece, bit]
-        counts = bits.reshape(8, -1).sum(-1)
-        assert np.array_equal(np.cumsum(counts), hdr)
+        blocks = b[16:1552].reshape(8, 192)
+        lo = blocks[:, :64].copy().view(np.uint32)                                 # [block, piece]
+        hi = blocks[:, 64:128].copy().view(np.uint32)
+        olo = blocks[:, 128:160].copy().view(np.uint16).astype(np.int64)
+        ohi = blocks[:, 160:192].copy().view(np.uint16).astype(np.int64)
+        words = np.stack([lo, hi], axis=-1).copy().view(np.uint8).reshape(8, 16, 8)
+        bits = np.unpackbits(words, axis=-1, bitorder="little").astype(bool)      # [block, piece, bit]
+        n_lo = bits[:, :, :32].sum(-1)
+        n_all = bits.sum(-1)
+        starts = np.concatenate([[0], np.cumsum(n_all.reshape(-1))[:-1]]).reshape(8, 16)
+        assert np.array_equal(olo, 2 * starts) and np.array_equal(ohi, 2 * (starts + n_lo))     # byte offsets
+        assert np.array_equal(np.cumsum(n_all.sum(-1)), hdr)
         n = int(hdr[-1])
-        assert len(b) == (1040 + 2 * n + 15) // 16 * 16
-        assert not b[1040 + 2 * n:].any()                                          # zero padding
-        v = b[1040:1040 + 2 * n].view(np.uint16)
+        assert len(b) == (1552 + 2 * n + 15) // 16 * 16
+        assert not b[1552 + 2 * n:].any()                                          # zero padding
+        v = b[1552:1552 + 2 * n].view(np.uint16)
         blk, p, bit = np.nonzero(bits)                                             # in the layout's value order
         r = rt * 128 + 16 * blk + PIECE_ROW[p, bit]
         c = ct * 64 + PIECE_COL[p, bit]
@@ -80,13 +89,15 @@ def test_mask_layout_decodes_to_the_selection(rows, cols, keep):
     assert data.numel() >= int(seg[-1])
 
 
-def test_mask_layout_is_the_references_bytes_per_weight():
-    """2 bytes a kept weight plus one bit a weight (and a 16-byte header a 128 x 64 segment, its padding)."""
+def test_mask_layout_bytes_per_weight():
+    """2 bytes a kept weight plus one bit a weight (the reference's storage), plus a 16-bit offset per 32 bits of mask,
+    a 16-byte header a 128 x 64 segment and its padding."""
     values, idx = _module(4096, 4096, 33)
     data, seg = kernels.mask_build([(0, values, idx)], 4096)
     kept = values.numel()
     ref = kept * 2 + 4096 * 4096 // 8
-    assert ref <= int(seg[-1]) <= ref + 32 * (seg.numel() - 1)
+    n_seg = seg.numel() - 1
+    assert ref + 512 * n_seg <= int(seg[-1]) <= ref + (512 + 32) * n_seg
 
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
