@@ -208,47 +208,75 @@ class ReplicaLayer:
         return outs
 
 
+def cpu_model() -> str:
+    """The host CPU's model name (from /proc/cpuinfo), or the platform's processor string."""
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    import platform
+    return platform.processor() or "unknown"
+
+
 class ReferenceCPU:
-    """The reference's CPU forward of a Llama-3-8B replica layer (the oracle port of compact.unpack's CPU branch +
-    F.linear, p2p/compact.py:57-61, in bf16) on all host cores, on a sample of each projection's rows (1/16, >= 64)
-    with a random k-subset kept in each row (the CPU cost does not depend on which), scaled to all rows. Used by both
-    the headline's cpu_baseline and the --impl reference arm, so the two report the same measurement."""
+    """The reference's CPU path for a whole Llama-3-8B replica layer, on all host cores: at load, per projection, the
+    Wanda selection (torch.topk of |w| * norms, p2p/wanda.py:76-87), the packing into values + mask words
+    (p2p/compact.py:36-45) and the expansion back to a dense matrix (compact.unpack's CPU branch, p2p/compact.py:57-61)
+    -- timed once, as `setup` -- and per step the forward F.linear(x, W) of every projection (the reference's only CPU
+    forward: compact.Tiles needs CUDA). All 218 M weights of the layer, bf16, seeded synthetic weights and norms. Used by
+    both the headline's cpu_baseline and the --impl reference arm, so the two report the same measurement."""
 
     def __init__(self, tokens: int):
         from oracle import cpu_ref
         self.cpu_ref = cpu_ref
         torch.set_num_threads(os.cpu_count() or 1)
         self.cores = torch.get_num_threads()
+        self.cpu = cpu_model()
         self.tokens = tokens
         g = torch.Generator().manual_seed(0)
         self.projs = list(workloads.LLAMA3_8B)
         self.mats, self.xs = {}, {}
+        setup = {"prune_s": 0.0, "pack_s": 0.0, "unpack_s": 0.0}
         for p in self.projs:
-            rows = max(64, int(p.rows / 16))
-            k = max(1, round(p.keep / 100 * p.cols))
-            w = (torch.randn(rows, p.cols, generator=g) * 0.02).bfloat16()
-            idx = torch.rand(rows, p.cols, generator=g).topk(k, dim=1).indices.sort(dim=1).values
-            self.mats[p.name] = (cpu_ref.unpack_rows(torch.gather(w, 1, idx), idx, p.cols), p.rows / rows)
+            w = (torch.randn(p.rows, p.cols, generator=g) * 0.02).bfloat16()
+            norms = torch.rand(p.cols, generator=g) * workloads.channel_scale(p.cols, g) + 1e-3
+            t0 = time.perf_counter()
+            pruned, mask = cpu_ref.prune(w, p.keep, norms)
+            t1 = time.perf_counter()
+            values, words = cpu_ref.pack(pruned, mask)
+            t2 = time.perf_counter()
+            self.mats[p.name] = cpu_ref.unpack_words(values, words, p.cols)
+            t3 = time.perf_counter()
+            setup["prune_s"] += t1 - t0
+            setup["pack_s"] += t2 - t1
+            setup["unpack_s"] += t3 - t2
+            del w, pruned, mask, values, words
             if INPUT_OF[p.name] not in self.xs:
                 self.xs[INPUT_OF[p.name]] = (torch.randn(tokens, p.cols, generator=g)
                                              * workloads.channel_scale(p.cols, g)).bfloat16()
-        self.sample = (f"rows 1/16 of each projection (>= 64), {tokens} tokens, bf16 F.linear of the unpacked rows, "
-                       "scaled to all rows; median over steps")
+        self.setup = setup
+        self.sample = (f"the whole layer (all {sum(p.rows * p.cols for p in self.projs) / 1e6:.0f} M weights of the 7 "
+                       f"projections), {tokens} tokens, bf16 F.linear of the unpacked matrices; median of the steps "
+                       "after warm-up")
 
     def step(self) -> float:
-        """Seconds of one layer pass (scaled from the sample)."""
-        total = 0.0
+        """Seconds of one layer pass."""
+        t0 = time.perf_counter()
         for p in self.projs:
-            dense, scale = self.mats[p.name]
-            t0 = time.perf_counter()
-            self.cpu_ref.forward(self.xs[INPUT_OF[p.name]], dense)
-            total += (time.perf_counter() - t0) * scale
-        return total
+            self.cpu_ref.forward(self.xs[INPUT_OF[p.name]], self.mats[p.name])
+        return time.perf_counter() - t0
 
     def layer_seconds(self, steps: int, warmup: int) -> float:
-        for _ in range(warmup):
+        for _ in range(max(1, warmup)):
             self.step()
-        return statistics.median(self.step() for _ in range(steps))
+        return statistics.median(self.step() for _ in range(max(10, steps)))
+
+    def summary(self, value: float) -> dict:
+        return {"value": value, "unit": UNIT, "cores": self.cores, "cpu": self.cpu, "kind": "port",
+                "sample": self.sample, "setup": {k: round(v, 3) for k, v in self.setup.items()}}
 
 
 # ---------------------------------------------------------------------------------------------------------- driver --
@@ -289,7 +317,7 @@ def run_reference(args, rank, world):
         "config": {"workload": "cfg2 Llama-3-8B replica layer (q,k,v,o keep 33; gate,up,down keep 36), T=%d"
                                % args.tokens,
                    "tokens": args.tokens, "path": "reference CPU forward (oracle port of compact.unpack + F.linear)"},
-        "cpu_baseline": {"value": value, "unit": UNIT, "cores": ref.cores, "kind": "port", "sample": ref.sample},
+        "cpu_baseline": ref.summary(value),
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }), flush=True)
 
@@ -422,8 +450,8 @@ def run_b200(args, rank, world, local):
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         ref = ReferenceCPU(args.tokens)
-        layer_s = ref.layer_seconds(steps=5, warmup=2)
-        cpu = {"value": args.tokens / layer_s, "unit": UNIT, "cores": ref.cores, "kind": "port", "sample": ref.sample}
+        layer_s = ref.layer_seconds(steps=10, warmup=2)
+        cpu = ref.summary(args.tokens / layer_s)
 
     if rank == 0:
         weights = sum(layer.proj[n].rows * layer.k[n] * 4 for n in layer.proj)

@@ -58,8 +58,9 @@ def shard_blocks(blocks: list, start: int, stop: int) -> list:
 
 
 class ShardedCompact:
-    """One rank's share of a compact module: its rows as a Compact, and apply() returning the whole y on every rank
-    (an all-gather of the ranks' row runs over the process group, NCCL on GPUs)."""
+    """One rank's share of a compact module: its rows as a Compact, and apply() returning the whole y on every rank.
+    The rank's GEMM writes its rows straight into its slot of the all-gather buffer; one all_gather_into_tensor over the
+    process group (NCCL on GPUs) collects every rank's slot, and the slots are laid side by side into y [T, rows]."""
 
     def __init__(self, blocks: list, group=None):
         self.group = group
@@ -70,19 +71,31 @@ class ShardedCompact:
         start, stop = self.ranges[self.rank]
         self.local = compact.Compact(shard_blocks(blocks, start, stop)) if stop > start else None
         self.width = max(b - a for a, b in self.ranges)
+        self.mine = stop - start
+
+    def local_part(self, x2: torch.Tensor, part: torch.Tensor) -> torch.Tensor:
+        """This rank's rows of y into part [T, width] (columns past its rows zeroed)."""
+        if self.local is not None:
+            self.local.tiles(x2, out=part[:, :self.mine])
+        if self.mine < self.width:
+            part[:, self.mine:].zero_()
+        return part
+
+    def gather(self, part: torch.Tensor) -> torch.Tensor:
+        """y [T, rows] from every rank's part."""
+        if self.world == 1:
+            return part[:, :self.rows]
+        T = part.shape[0]
+        slots = torch.empty(self.world, T, self.width, dtype=part.dtype, device=part.device)
+        dist.all_gather_into_tensor(slots, part, group=self.group)
+        if all(b - a == self.width for a, b in self.ranges):
+            return slots.permute(1, 0, 2).reshape(T, self.world * self.width)
+        return torch.cat([slots[r, :, :b - a] for r, (a, b) in enumerate(self.ranges)], dim=1)
 
     def apply(self, layer, x: torch.Tensor, bias=None) -> torch.Tensor:
         x2 = x.reshape(-1, x.shape[-1])
-        start, stop = self.ranges[self.rank]
-        part = torch.zeros(x2.shape[0], self.width, dtype=x.dtype, device=x.device)
-        if self.local is not None:
-            part[:, :stop - start] = self.local.apply(None, x2)
-        if self.world == 1:
-            y = part[:, :self.rows]
-        else:
-            pieces = [torch.empty_like(part) for _ in range(self.world)]
-            dist.all_gather(pieces, part, group=self.group)
-            y = torch.cat([p[:, :b - a] for p, (a, b) in zip(pieces, self.ranges)], dim=1)
+        part = torch.empty(x2.shape[0], self.width, dtype=x.dtype, device=x.device)
+        y = self.gather(self.local_part(x2, part))
         if bias is not None:
             y = y + bias
         return y.reshape(*x.shape[:-1], self.rows)

@@ -94,19 +94,24 @@ def test_shard_blocks_cut_mixed_blocks():
 
 
 def _gather(rank, world):
-    # the all-gather assembly of ShardedCompact.apply, on CPU pieces: each rank's padded run of rows
-    rows = 300
-    ranges = shard.row_ranges(rows, world)
-    width = max(b - a for a, b in ranges)
-    a, b = ranges[rank]
-    part = torch.zeros(2, width)
-    part[:, :b - a] = torch.arange(a, b, dtype=torch.float32)
-    pieces = [torch.empty_like(part) for _ in range(world)]
-    dist.all_gather(pieces, part)
-    return torch.cat([p[:, :e - s] for p, (s, e) in zip(pieces, ranges)], dim=1).tolist()
+    # ShardedCompact.gather on CPU parts: each rank's run of rows, padded to the widest run; 300 rows split unevenly
+    # (256 + 44), 256 rows evenly (128 + 128)
+    out = {}
+    for rows in (300, 256):
+        sc = object.__new__(shard.ShardedCompact)
+        sc.group, sc.world, sc.rank, sc.rows = None, world, rank, rows
+        sc.ranges = shard.row_ranges(rows, world)
+        sc.width = max(b - a for a, b in sc.ranges)
+        a, b = sc.ranges[rank]
+        part = torch.zeros(2, sc.width)
+        part[:, :b - a] = torch.arange(a, b, dtype=torch.float32)
+        y = sc.gather(part)
+        out[rows] = (tuple(y.shape), y.tolist())
+    return out
 
 
 def test_gather_assembles_rows_in_order():
     out = _spawn(_gather)
-    want = torch.arange(300.0).expand(2, 300).tolist()
-    assert out[0] == want and out[1] == want
+    for rows in (300, 256):
+        want = torch.arange(float(rows)).expand(2, rows).tolist()
+        assert out[0][rows] == ((2, rows), want) and out[1][rows] == ((2, rows), want)
