@@ -86,8 +86,9 @@ class ShardedCompact:
         if self.world == 1:
             return part[:, :self.rows]
         T = part.shape[0]
-        slots = torch.empty(self.world, T, self.width, dtype=part.dtype, device=part.device)
-        dist.all_gather_into_tensor(slots, part, group=self.group)
+        slots = torch.empty(self.world * T, self.width, dtype=part.dtype, device=part.device)
+        dist.all_gather_into_tensor(slots, part.contiguous(), group=self.group)
+        slots = slots.view(self.world, T, self.width)
         if all(b - a == self.width for a, b in self.ranges):
             return slots.permute(1, 0, 2).reshape(T, self.world * self.width)
         return torch.cat([slots[r, :, :b - a] for r, (a, b) in enumerate(self.ranges)], dim=1)
