@@ -18,14 +18,16 @@ TABLE = {"qkv_proj": ("q", "k", "v"), "in_proj_qkvz": ("q", "k", "v", "z"), "o_p
 
 
 class Projection(NamedTuple):
-    path: str                # the module inside its layer
-    rows: "slice | tuple"    # where it is in that module's tensor, on this rank
-    shape: list              # [rows, cols] over all ranks
-    param: str = "weight"    # that module's tensor
+    """One projection of a decoder layer. The field names and `key` are the calib.pt interface shared with p2p/family.py
+    (calibration sums and replica files are keyed by them)."""
+    path: str                # dotted path of the owning module, from the layer
+    rows: "slice | tuple"    # index of this projection's rows in the module's tensor as this rank holds it
+    shape: list              # [rows, cols] of the whole projection, every rank's share together
+    param: str = "weight"    # attribute name of the module's tensor
 
     @property
     def key(self) -> str:
-        """What its calibration sums are stored under."""
+        """The calib.pt key: the module path for a linear module's weight, "<path>.<tensor>" for routed experts."""
         return self.path if self.param == "weight" else f"{self.path}.{self.param}"
 
 

@@ -10,7 +10,6 @@ in fp32, each difference rounded to the model's dtype first (p2p/replica.py:1-13
 """
 from __future__ import annotations
 
-import copy
 import functools
 
 import torch
@@ -24,19 +23,23 @@ def combine(parts: list, h: torch.Tensor, h_copy: torch.Tensor) -> torch.Tensor:
     return kernels.combine(parts, h, h_copy)
 
 
-def _copy_tree(m: nn.Module) -> nn.Module:
-    """A module tree that shares every tensor with m until one is replaced."""
-    c = copy.copy(m)
-    c._parameters, c._buffers = dict(m._parameters), dict(m._buffers)
-    c._modules = {k: _copy_tree(v) for k, v in m._modules.items()}
-    return c
+def _sharing_clone(module: nn.Module) -> nn.Module:
+    """A new tree of module objects over the same tensors: every clone has parameter, buffer and child tables of its
+    own, so replacing a tensor (or installing a quant_method) in the clone leaves the original untouched, while no
+    tensor is copied."""
+    twin = nn.Module.__new__(type(module))
+    twin.__dict__.update(module.__dict__)
+    for table in ("_parameters", "_buffers"):
+        twin.__dict__[table] = dict(module.__dict__[table])
+    twin.__dict__["_modules"] = {name: _sharing_clone(child) for name, child in module.__dict__["_modules"].items()}
+    return twin
 
 
 def shrink(layer: nn.Module, keep: dict, sums: dict, i: int, form: str = "dense") -> nn.Module:
     """A copy of layer i keeping `keep[projection]` percent of each projection's weights (p2p/replica.py:34-49).
     form "dense": pruned weights in place, as the reference's scan does; "compact": each pruned projection module
     multiplies through a Compact (values + column indices) instead of its dense weight."""
-    c = _copy_tree(layer)
+    c = _sharing_clone(layer)
     c.__dict__.pop("forward", None)
     modules = dict(c.named_modules())
     blocks: dict = {}

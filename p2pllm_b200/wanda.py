@@ -37,54 +37,73 @@ def expert_inputs(m, x: torch.Tensor, ids: torch.Tensor) -> tuple:
 
 
 class Calibration:
-    """Per-channel sums of squares of every projection's input, collected through forward pre-hooks
-    (p2p/wanda.py:23-60). Each hook call adds x.float().pow(2).sum(0).double() on the GPU."""
+    """Calibration of a model's layers for Wanda: while it is active, every module a projection reads its input from
+    adds the per-channel sum of squares of that input, in fp64, to an accumulator on the GPU (the package's calibration
+    kernel, one call per forward). Routed-expert modules add their per-expert sums (expert_inputs).
+
+    Accumulators are keyed as p2p/wanda.py:23-60 keys them, so finish() returns what calib.pt holds: (layer index,
+    projection key), the key being the module's path for a linear module and "<path>.w13_weight" /
+    "<path>.w2_weight" for the routed experts' two tensors."""
 
     def __init__(self, layers):
-        self.sums, self.handles = {}, []
-        for i, layer in enumerate(layers):
-            modules = dict(layer.named_modules())
-            for path in {p.path for p in family.projections(layer).values()}:
-                hook = self._experts if hasattr(modules[path], "w13_weight") else self._linear
-                self.handles.append(modules[path].register_forward_pre_hook(hook(i, path)))
+        self._acc: dict = {}
+        self._hooks: list = []
+        for index, layer in enumerate(layers):
+            by_path = dict(layer.named_modules())
+            for path in sorted({proj.path for proj in family.projections(layer).values()}):
+                module = by_path[path]
+                make = self._routed_hook if hasattr(module, "w13_weight") else self._input_hook
+                self._hooks.append(module.register_forward_pre_hook(make(index, path)))
 
-    def _linear(self, i, path):
+    def _accumulator(self, key: tuple, shape, device) -> torch.Tensor:
+        acc = self._acc.get(key)
+        if acc is None:
+            acc = self._acc[key] = torch.zeros(shape, dtype=torch.float64, device=device)
+        return acc
+
+    def _input_hook(self, index: int, path: str):
         def hook(module, args):
             x = args[0]
-            sums = self.sums.get((i, path))
-            if sums is None:
-                sums = self.sums[i, path] = torch.zeros(x.shape[-1], dtype=torch.float64, device=x.device)
-            kernels.sumsq_cols(x, sums)
+            kernels.sumsq_cols(x, self._accumulator((index, path), (x.shape[-1],), x.device))
         return hook
 
-    def _experts(self, i, path):
+    def _routed_hook(self, index: int, path: str):
         def hook(module, args):
             into, gated = expert_inputs(module, args[0], args[1].topk_ids)
-            for key, v in (((i, f"{path}.w13_weight"), into), ((i, f"{path}.w2_weight"), gated)):
-                self.sums[key] = self.sums[key] + v if key in self.sums else v
+            for tensor_name, sums in (("w13_weight", into), ("w2_weight", gated)):
+                self._accumulator((index, f"{path}.{tensor_name}"), sums.shape, sums.device).add_(sums)
         return hook
 
     def finish(self, layers) -> dict:
-        """Stop collecting. {(layer, projection key): sums over all ranks} on the CPU."""
-        for h in self.handles:
-            h.remove()
-        out = {}
-        for i, layer in enumerate(layers):
-            modules = dict(layer.named_modules())
-            for key, p in {p.key: p for p in family.projections(layer).values()}.items():
-                if (i, key) in self.sums:
-                    x, group = self.sums[i, key], family.split_group(modules[p.path], p)
-                    out[i, key] = (group.all_gather(x, dim=x.dim() - 1) if group else x).cpu()
-        return out
+        """Removes the hooks and returns {(layer index, projection key): fp64 sums on the CPU}; a projection whose
+        columns are split over a TP group gets the sums of all its columns (gathered from the group's ranks)."""
+        for handle in self._hooks:
+            handle.remove()
+        self._hooks = []
+        result = {}
+        for index, layer in enumerate(layers):
+            by_path = dict(layer.named_modules())
+            for proj in family.projections(layer).values():
+                key = (index, proj.key)
+                if key in result or key not in self._acc:
+                    continue
+                sums = self._acc[key]
+                group = family.split_group(by_path[proj.path], proj)
+                if group:
+                    sums = group.all_gather(sums, dim=sums.dim() - 1)
+                result[key] = sums.cpu()
+        return result
 
 
 def channel_norms(sums: torch.Tensor, w: torch.Tensor, group=None) -> torch.Tensor:
-    """||x_j|| for the columns of w this rank holds: [columns], or [expert, 1, columns] for experts, where an expert no
-    token reached gets norms of one. group: as family.split_group. p2p/wanda.py:63-73."""
+    """The input-channel norms sqrt(sums) (fp32) that w's columns on this rank are scored with: [cols], or
+    [experts, 1, cols] for routed experts, an expert that saw no token getting norms of one. With a TP group splitting
+    w's columns (family.split_group), this rank's share of the sums is taken first (p2p/wanda.py:63-73)."""
     sums = sums.to(w.device)
     if group:
-        cols = w.shape[-1]
-        sums = sums[..., group.rank_in_group * cols: (group.rank_in_group + 1) * cols]
+        width = w.shape[-1]
+        first = group.rank_in_group * width
+        sums = sums[..., first:first + width]
     return kernels.channel_norms(sums)
 
 
@@ -106,9 +125,10 @@ def select(w: torch.Tensor, keep: float, norms: torch.Tensor, group=None, idx_dt
 
 
 def prune(w: torch.Tensor, keep: float, norms: torch.Tensor, group=None, with_mask: bool = False):
-    """w with zeros everywhere but the `keep` percent of each row's weights that score highest (and, with_mask, which
-    those are: the same number in every row). A projection split across ranks compares scores across them, so the
-    choice does not depend on the TP size. p2p/wanda.py:76-87."""
+    """The dense form of the selection (p2p/wanda.py:76-87): w where a weight is among its row's k = k_of(keep, cols)
+    best scores |w| * norms and zero elsewhere, plus, with_mask, the bool mask of the kept weights (k in every row).
+    For columns split over a TP group the scores of the whole row decide, and each rank gets its own columns back, so
+    the result does not depend on how many ranks hold the projection."""
     full_w, full_n = _full_rows(w, norms, group)
     k = k_of(keep, full_w.shape[-1])
     out = kernels.wanda_select(full_w, full_n, k, values=False, idx=False, mask=True, pruned=True)
