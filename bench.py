@@ -588,18 +588,23 @@ def _e2e(layer, T: int, steps: int, warmup: int, device, stream) -> dict:
 
 def run_sharded(args, layer, rank, world, device, peaks):
     """The cfg2 layer row-sharded over `world` GPUs (shard.ShardedCompact: each rank whole 128-row tiles of every
-    module, the full x, one NCCL all-gather of y a module)."""
+    module and the full x). Headline: the all-gather fused into the GEMM (each rank's bitmask-layout GEMM stores its
+    rows of y into every rank's y over NVLink, one bounded peer barrier a step). Beside it: the same split with the
+    GEMM writing its slot and one NCCL all-gather a module."""
     import hashlib
     import torch.distributed as dist
     from p2pllm_b200 import shard
     stream = torch.cuda.current_stream(device)
     names = list(MODULES)
-    sharded = {m: shard.ShardedCompact([("compact", *layer.selected[n], layer.proj[n].cols) for n in MODULES[m][1]])
-               for m in names}
+    blocks = {m: [("compact", *layer.selected[n], layer.proj[n].cols) for n in MODULES[m][1]] for m in names}
+    peers = shard.PeerGroup(None, device)
+    sharded = {m: shard.ShardedCompact(blocks[m], fused=True, peers=peers) for m in names}
+    for m in names:
+        sharded[m].prepare(args.tokens, torch.bfloat16, device)
     xs = {m: layer.inputs[MODULES[m][0]] for m in names}
 
-    # In-run parity: every module's gathered y against the unsharded module on rank 0 (rel-L2 <= 1e-2: the shards may
-    # split their columns differently, so sums can differ in the last bf16 bit), and the same bits on every rank.
+    # In-run parity: every module's y against the unsharded module on rank 0 (rel-L2 <= 1e-2: the shards may split
+    # their columns differently, so sums can differ in the last bf16 bit), and the same bits on every rank.
     checks, ok = {}, True
     for m in names:
         y = sharded[m].apply(None, xs[m])
@@ -616,6 +621,7 @@ def run_sharded(args, layer, rank, world, device, peaks):
         dist.broadcast(flag, 0)
         checks[m] = {"rel_l2_vs_one_gpu": rel, "same_bits_on_every_rank": same}
         ok = ok and bool(flag.item())
+    peers.status()
     if not ok:
         if rank == 0:
             print(json.dumps({"metric": METRIC, "error": "row-sharded parity check failed", "checks": checks}),
@@ -624,19 +630,15 @@ def run_sharded(args, layer, rank, world, device, peaks):
 
     # per-rank weights: from 4 GPUs on they fit in L2, so each step is timed alone after a write larger than L2
     flush = torch.empty(2 * L2_BYTES, dtype=torch.uint8, device=device)
-    parts = {m: torch.empty(args.tokens, sharded[m].width, dtype=torch.bfloat16, device=device) for m in names}
 
     def step():
         for m in names:
-            sharded[m].gather(sharded[m].local_part(xs[m], parts[m]))
+            sharded[m].apply_fused(xs[m], sync=False)
+        peers.barrier()
 
     def kernels_only():
         for m in names:
-            sharded[m].local_part(xs[m], parts[m])
-
-    def gathers_only():
-        for m in names:
-            sharded[m].gather(parts[m])
+            sharded[m].apply_fused(xs[m], sync=False)
 
     for _ in range(args.warmup):
         step()
@@ -649,10 +651,31 @@ def run_sharded(args, layer, rank, world, device, peaks):
     total_ms = max_over_ranks(local_ms, world, device)
     kern_ms = max_over_ranks(_flushed_ms(kernels_only, args.steps, stream, flush), world, device)
     dist.barrier()
-    gath_ms = max_over_ranks(_flushed_ms(gathers_only, args.steps, stream, flush), world, device)
-    dist.barrier()
+    peers.status()
     ms_per_step = total_ms / args.steps
     value = args.tokens * args.steps / (total_ms / 1e3)
+
+    # the NCCL path: the rank's GEMM writes its slot, one all-gather a module
+    nccl = {m: shard.ShardedCompact(blocks[m], fused=False) for m in names}
+    parts = {m: torch.empty(args.tokens, nccl[m].width, dtype=torch.bfloat16, device=device) for m in names}
+
+    def nccl_step():
+        for m in names:
+            nccl[m].gather(nccl[m].local_part(xs[m], parts[m]))
+
+    def nccl_gathers():
+        for m in names:
+            nccl[m].gather(parts[m])
+
+    for _ in range(3):
+        nccl_step()
+    torch.cuda.synchronize(device)
+    dist.barrier()
+    nccl_ms = max_over_ranks(_flushed_ms(nccl_step, args.steps, stream, flush), world, device)
+    dist.barrier()
+    gath_ms = max_over_ranks(_flushed_ms(nccl_gathers, args.steps, stream, flush), world, device)
+    dist.barrier()
+    del nccl, parts
 
     # independent replicas (each rank the whole layer on its own tokens): the weak-scaling figure, kept beside
     for _ in range(3):
@@ -661,8 +684,8 @@ def run_sharded(args, layer, rank, world, device, peaks):
     dist.barrier()
     rep_ms = max_over_ranks(_region_ms(layer.step, args.steps, stream), world, device)
 
-    # e2e: rank 0 copies the step's inputs in from pinned memory and broadcasts them; every rank runs its shards and
-    # the all-gathers; rank 0 copies y back
+    # e2e: rank 0 copies the step's inputs in from pinned memory and broadcasts them; every rank runs its shards,
+    # storing into every rank's y; rank 0 copies y back
     host_x = {m: xs[m].cpu().pin_memory() for m in names} if rank == 0 else None
     host_y = {m: torch.empty(args.tokens, sharded[m].rows, dtype=torch.bfloat16).pin_memory() for m in names} \
         if rank == 0 else None
@@ -673,16 +696,18 @@ def run_sharded(args, layer, rank, world, device, peaks):
             if rank == 0:
                 dev_x[m].copy_(host_x[m], non_blocking=True)
             dist.broadcast(dev_x[m], 0)
-        for m in names:
-            y = sharded[m].apply(None, dev_x[m])
-            if rank == 0:
-                host_y[m].copy_(y, non_blocking=True)
+        ys = {m: sharded[m].apply_fused(dev_x[m], sync=False) for m in names}
+        peers.barrier()
+        if rank == 0:
+            for m in names:
+                host_y[m].copy_(ys[m], non_blocking=True)
 
     for _ in range(3):
         e2e_step()
     torch.cuda.synchronize(device)
     dist.barrier()
     e2e_ms = max_over_ranks(_region_ms(e2e_step, args.steps, stream), world, device)
+    peers.status()
     h2d = sum(t.numel() * 2 for t in xs.values())
     d2h = sum(args.tokens * sharded[m].rows * 2 for m in names)
 
@@ -690,32 +715,36 @@ def run_sharded(args, layer, rank, world, device, peaks):
         sum(args.tokens * (layer.cols(m) + sharded[m].mine) * 2 for m in names)
     achieved = local_bytes / (kern_ms / args.steps / 1e3) / 1e9
     if rank == 0:
-        layout = next(sharded[m].local.tiles.layout for m in names if sharded[m].local is not None)
         out = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (seeded N(0,0.02) weights, lognormal-scaled N(0,1) activations; no checkpoint or dataset)",
             "config": {"workload": "cfg2 Llama-3-8B replica layer (q,k,v,o keep 33; gate,up,down keep 36), "
-                                   f"T={args.tokens}", "tokens": args.tokens, "layout": layout,
+                                   f"T={args.tokens}", "tokens": args.tokens, "layout": "mask",
                        "parallelism": f"row-sharded over {world} GPUs (whole 128-row tiles of every module a rank, "
-                                      "full x, one NCCL all-gather of y a module)",
+                                      "full x); y gathered in the GEMM's epilogue by peer stores over NVLink, one "
+                                      "bounded peer barrier a step",
                        "l2": "per-rank weights may fit L2: every step timed alone after a %d MB write"
                              % (2 * L2_BYTES >> 20)},
             "parity": {"passed": True, "checks": checks},
-            "breakdown_us_per_step": {"kernels": kern_ms / args.steps * 1e3, "all_gathers": gath_ms / args.steps * 1e3,
-                                      "step": ms_per_step * 1e3,
-                                      "limiter": "all_gathers" if gath_ms > kern_ms else "kernels"},
+            "breakdown_us_per_step": {"fused_gemms": kern_ms / args.steps * 1e3,
+                                      "barrier_and_skew": (total_ms - kern_ms) / args.steps * 1e3,
+                                      "step": ms_per_step * 1e3},
+            "nccl_path": {"ms_per_step": nccl_ms / args.steps, "all_gathers_us": gath_ms / args.steps * 1e3,
+                          "tokens_per_s": args.tokens * args.steps / (nccl_ms / 1e3),
+                          "how": "the rank's GEMM writes its slot, one NCCL all_gather_into_tensor a module, then the "
+                                 "slots laid side by side"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                          "frac": achieved / peaks["hbm_gbs"], "traffic": None, "peak_source": peaks["source"],
-                         "kernel": "the rank's local compact GEMMs (bytes of its shards over their time)"},
+                         "kernel": "the rank's fused GEMMs (bytes of its shards and x, y once, over their time)"},
             "replicas": {"value": args.tokens * world * args.steps / (rep_ms / 1e3), "unit": UNIT, "scaling": "weak",
                          "how": "each rank the whole layer on its own tokens, no data-path collective"},
             "e2e": {"value": args.tokens * args.steps / (e2e_ms / 1e3), "unit": UNIT, "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h,
-                    "how": "rank 0: pinned-host inputs in, NCCL broadcast, every rank its shards + all-gathers, "
-                           "rank 0: y back to pinned host memory"},
-            "gpu_launches": args.steps * len(names),
+                    "how": "rank 0: pinned-host inputs in, NCCL broadcast, every rank its fused shards + a peer "
+                           "barrier, rank 0: y back to pinned host memory"},
+            "gpu_launches": args.steps * (len(names) + 1),
             "clocks": clocks.summary(),
         }
         print(json.dumps(out), flush=True)

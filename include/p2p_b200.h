@@ -191,6 +191,16 @@ int p2p_spmm_mask(const void* x, int dtype, int64_t tokens, int64_t cols, int64_
                   const int64_t* seg, int64_t rows, void* y, int64_t ldy, void* workspace, size_t workspace_bytes,
                   void* stream);
 
+/* p2p_spmm_mask with the all-gather of a row-sharded module fused into its epilogue: this rank's `rows` rows of y go
+ * to columns y_col0 .. y_col0 + rows - 1 of each of the n_ys (1..8) buffers ys[k] [tokens, ldy] -- the y of every
+ * rank of the node, peers' buffers addressed through CUDA IPC / symmetric memory, written with plain stores over
+ * NVLink. The other ranks read their y only after a p2p_peer_barrier that follows this launch on every rank.
+ * Replaces the NCCL all-gather that p2p/wanda.py:81's column split needs in SGLang (here rows are split, so each rank's
+ * rows are final and only need placing). */
+int p2p_spmm_mask_peers(const void* x, int dtype, int64_t tokens, int64_t cols, int64_t ldx, const void* data,
+                        const int64_t* seg, int64_t rows, void* const* ys, int n_ys, int64_t y_col0, int64_t ldy,
+                        void* workspace, size_t workspace_bytes, void* stream);
+
 /* P2P_OK unless a p2p_spmm_mask launch since the last reset gave up waiting on its pipeline (then P2P_ECUDA, naming
  * the site); reset != 0 clears it. Syncs the stream. */
 int p2p_spmm_mask_status(int reset, void* stream);
@@ -251,6 +261,18 @@ int p2p_spmm_tc_status(int reset, void* stream);
 int p2p_spmm_tc_withhold(const void* x, int dtype, int64_t tokens, int64_t cols, int64_t ldx, const uint32_t* words,
                          const int64_t* seg, int64_t rows, int64_t seg_cap_words, void* y, int64_t ldy, void* workspace,
                          size_t workspace_bytes, int64_t hold_tile, int64_t wait_us, void* stream);
+
+/* A barrier of the node's ranks over peer memory, on `stream`, after which every store this rank's stream made before
+ * it (into its own or peers' memory) is visible to every rank. flags[r]: rank r's array of 8 uint32 slots, as this GPU
+ * addresses it (zeroed before first use; epochs start at 1 and grow by one a barrier). Each wait is bounded by
+ * timeout_us (1 ms .. 60 s): past it the barrier gives up and p2p_peer_status reports the rank it waited for.
+ * The ranks' barriers wait on each other, so they must run on different GPUs, one process each.
+ * No counterpart in the reference (its hops go through NCCL send/recv, p2p/route.py:798-831). */
+int p2p_peer_barrier(void* const* flags, int n_ranks, int me, uint32_t epoch, int64_t timeout_us, void* stream);
+
+/* P2P_OK unless a p2p_peer_barrier since the last reset gave up (P2P_ECUDA, naming the rank); reset != 0 clears it.
+ * Syncs the stream. */
+int p2p_peer_status(int reset, void* stream);
 
 /* ------------------------------------------------------------------------------------------------------------------
  * (3) Group combine epilogue

@@ -50,6 +50,10 @@ SIGNATURES = {
     "p2p_spmm_mask_workspace": ([_i64, _i64, _i64], _sz),
     "p2p_spmm_mask": ([_vp, _int, _i64, _i64, _i64, _vp, _vp, _i64, _vp, _i64, _vp, _sz, _vp], _int),
     "p2p_spmm_mask_status": ([_int, _vp], _int),
+    "p2p_spmm_mask_peers": ([_vp, _int, _i64, _i64, _i64, _vp, _vp, _i64, ctypes.POINTER(_vp), _int, _i64, _i64, _vp,
+                             _sz, _vp], _int),
+    "p2p_peer_barrier": ([ctypes.POINTER(_vp), _int, _int, ctypes.c_uint32, _i64, _vp], _int),
+    "p2p_peer_status": ([_int, _vp], _int),
     "p2p_spmm_tc_workspace": ([_i64, _i64, _i64], _sz),
     "p2p_spmm_tc": ([_vp, _int, _i64, _i64, _i64, _vp, _vp, _i64, _i64, _vp, _i64, _vp, _sz, _vp], _int),
     "p2p_spmm_tc_grouped": ([_vp, _int, _i64, _i64, _i64, _vp, _vp, _i64, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _i64,
@@ -64,7 +68,10 @@ SIGNATURES = {
     "p2p_member_part": ([_vp, _vp, _vp, _int, _i64, _vp], _int),
 }
 
+OPS_PATH = os.path.join(HERE, "libp2p_torch_ops.so")
+
 _lib = None
+_ops = None
 _lock = threading.Lock()
 
 
@@ -77,12 +84,27 @@ def load() -> ctypes.CDLL:
                 if not os.path.exists(LIB_PATH):
                     raise P2PError(f"{LIB_PATH} is missing: build it with `python -m p2pllm_b200.build` "
                                    "(the replica path has no CPU fallback)")
-                lib = ctypes.CDLL(LIB_PATH)
+                lib = ctypes.CDLL(LIB_PATH, mode=ctypes.RTLD_GLOBAL)    # the torch ops resolve its symbols
                 for name, (args, res) in SIGNATURES.items():
                     fn = getattr(lib, name)
                     fn.argtypes, fn.restype = args, res
                 _lib = lib
     return _lib
+
+
+def ops():
+    """torch.ops.p2p_b200: the entry points as torch custom operators (libp2p_torch_ops.so over the C ABI). Raises if
+    either library was never built."""
+    global _ops
+    if _ops is None:
+        load()
+        with _lock:
+            if _ops is None:
+                if not os.path.exists(OPS_PATH):
+                    raise P2PError(f"{OPS_PATH} is missing: build it with `python -m p2pllm_b200.build`")
+                torch.ops.load_library(OPS_PATH)
+                _ops = torch.ops.p2p_b200
+    return _ops
 
 
 def call(name: str, *args) -> None:

@@ -36,6 +36,33 @@ def stale() -> bool:
     return any(os.path.getmtime(p) > built for p in DEPS)
 
 
+OPS_SRC = os.path.join(HERE, "torch_ops", "ops.cpp")
+OPS_LIB = os.path.join(HERE, "libp2p_torch_ops.so")
+
+
+def build_ops(force: bool = False, verbose: bool = False) -> str:
+    """Compiles the torch custom operators (torch_ops/ops.cpp, TORCH_LIBRARY p2p_b200) over the C ABI into
+    libp2p_torch_ops.so. It leaves the p2p_* symbols undefined: _lib loads libp2p_b200.so into the global scope first."""
+    deps = [OPS_SRC, os.path.join(ROOT, "include", "p2p_b200.h")]
+    if not force and os.path.exists(OPS_LIB) and all(os.path.getmtime(d) <= os.path.getmtime(OPS_LIB) for d in deps):
+        return OPS_LIB
+    import torch
+    from torch.utils import cpp_extension
+    cuda_home = os.environ.get("CUDA_HOME", "/usr/local/cuda")
+    torch_lib = os.path.join(os.path.dirname(torch.__file__), "lib")
+    cmd = ["g++", "-O2", "-std=c++17", "-shared", "-fPIC", f"-D_GLIBCXX_USE_CXX11_ABI={int(torch._C._GLIBCXX_USE_CXX11_ABI)}",
+           *[f"-I{p}" for p in cpp_extension.include_paths()], f"-I{os.path.join(cuda_home, 'include')}",
+           f"-I{os.path.join(ROOT, 'include')}", OPS_SRC, f"-L{torch_lib}", "-lc10", "-ltorch_cpu", "-ltorch",
+           "-lc10_cuda", f"-Wl,-rpath,{torch_lib}", "-o", OPS_LIB + ".tmp"]
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode:
+        raise RuntimeError(f"g++ failed on torch_ops/ops.cpp:\n{r.stderr[-6000:]}")
+    if verbose:
+        sys.stderr.write(r.stderr)
+    os.replace(OPS_LIB + ".tmp", OPS_LIB)
+    return OPS_LIB
+
+
 def build(force: bool = False, verbose: bool = False) -> str:
     """Compiles every csrc/*.cu into libp2p_b200.so (objects in _build/); returns the library path."""
     if not force and not stale():
@@ -62,3 +89,4 @@ def build(force: bool = False, verbose: bool = False) -> str:
 
 if __name__ == "__main__":
     print(build(force="--force" in sys.argv, verbose="-v" in sys.argv))
+    print(build_ops(force="--force" in sys.argv, verbose="-v" in sys.argv))

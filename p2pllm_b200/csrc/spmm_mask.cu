@@ -64,6 +64,7 @@ constexpr int kRingPad = 64;                           // slack past the ring: r
 constexpr int kSmemLimit = 227 * 1024 - (int)sizeof(int64_t) * (kMaxUnits + 1) - 8 * kTickets - 128;
 constexpr uint64_t kWaitNs = 2000000000ull;
 constexpr int64_t kMaxRowTiles = 16384;
+constexpr int kMaxPeers = 8;                           // y buffers a launch writes (the ranks of one node)
 constexpr size_t kTicketRegion = kMaxRowTiles * sizeof(unsigned);
 
 __device__ int g_mask_error;            // site of the first wait that gave up since the last reset (0: none)
@@ -85,13 +86,26 @@ struct MaskParams {
     // column tiles of row tile b / s; with cluster, the s CTAs of a row tile form a thread-block cluster and add their
     // partial tiles over DSMEM.
     int splits, per_split, cluster;
-    void* y;
+    // y [tokens, ldy]: every value of row r goes to column y_col0 + r of each of the n_ys buffers -- this rank's y and,
+    // when the module is row-sharded over a node's GPUs, every peer's (stores over NVLink: the gather fused into the
+    // GEMM's epilogue).
+    void* ys[kMaxPeers];
+    int n_ys;
+    int64_t y_col0;
     int64_t ldy;
     float* partial;                   // [ctas][2][tokens][128]: each CTA's first and last row tile, when shared
     unsigned* tickets;                // [row tiles], zero between calls
     uint64_t wait_ns;
     unsigned seq;
 };
+
+// y[t, row] = v in each of the launch's y buffers.
+template <typename T>
+__device__ __forceinline__ void store_y(const MaskParams& p, int64_t t, int64_t row, float v) {
+    const T val = from_f32<T>(v);
+    const int64_t at = t * p.ldy + p.y_col0 + row;
+    for (int k = 0; k < p.n_ys; ++k) reinterpret_cast<T*>(p.ys[k])[at] = val;
+}
 
 // 1 in every thread of the 4 epilogue warps if `ok` holds in all 128 of them (barrier 1), else 0.
 __device__ __forceinline__ int epilogue_all(int ok) {
@@ -350,7 +364,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const int t = c * 16 + q;
                     if (t < tokens) {
                         if (whole) {
-                            if (row < p.rows) reinterpret_cast<T*>(p.y)[t * p.ldy + row] = from_f32<T>(v[q]);
+                            if (row < p.rows) store_y<T>(p, t, row, v[q]);
                         } else if (p.cluster) {
                             reinterpret_cast<float*>(gbase)[t * mk::kTileRows + row_local] = v[q];   // rings free
                         } else {
@@ -402,11 +416,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                                 }
                         }
                         const int64_t row4 = r * mk::kTileRows + r4;
-                        T* yt = reinterpret_cast<T*>(p.y) + t * p.ldy;
                         const float vv[4] = {acc.x, acc.y, acc.z, acc.w};
 #pragma unroll
                         for (int c = 0; c < 4; ++c)
-                            if (row4 + c < p.rows) yt[row4 + c] = from_f32<T>(vv[c]);
+                            if (row4 + c < p.rows) store_y<T>(p, t, row4 + c, vv[c]);
                     }
                     if (e == 0 && lane == 0) p.tickets[r] = 0u;     // zero again for the next call
                 }
@@ -502,7 +515,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const int t = c * 16 + q;
                 if (t < tokens) {
                     if (ns == 1) {
-                        if (row < p.rows) reinterpret_cast<T*>(p.y)[t * p.ldy + row] = from_f32<T>(v[q]);
+                        if (row < p.rows) store_y<T>(p, t, row, v[q]);
                     } else if (p.cluster) {
                         reinterpret_cast<float*>(gbase)[t * mk::kTileRows + row_local] = v[q];   // rings free
                     } else {
@@ -544,11 +557,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                     acc.x += parts[sp].x; acc.y += parts[sp].y; acc.z += parts[sp].z; acc.w += parts[sp].w;
                 }
             const int64_t row = rt * mk::kTileRows + r4;
-            T* yt = reinterpret_cast<T*>(p.y) + t * p.ldy;
             const float v[4] = {acc.x, acc.y, acc.z, acc.w};
 #pragma unroll
             for (int c = 0; c < 4; ++c)
-                if (row + c < p.rows) yt[row + c] = from_f32<T>(v[c]);
+                if (row + c < p.rows) store_y<T>(p, t, row + c, v[c]);
         }
         cluster_sync_all();
         return;
@@ -578,11 +590,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             acc.x += a.x; acc.y += a.y; acc.z += a.z; acc.w += a.w;
         }
         const int64_t row = rt * mk::kTileRows + r4;
-        T* yt = reinterpret_cast<T*>(p.y) + t * p.ldy;
         const float v[4] = {acc.x, acc.y, acc.z, acc.w};
 #pragma unroll
         for (int c = 0; c < 4; ++c)
-            if (row + c < p.rows) yt[row + c] = from_f32<T>(v[c]);
+            if (row + c < p.rows) store_y<T>(p, t, row + c, v[c]);
     }
     if (threadIdx.x == 0) p.tickets[rt] = 0u;             // zero again for the next call
 }
@@ -767,17 +778,21 @@ extern "C" size_t p2p_spmm_mask_workspace(int64_t rows, int64_t cols, int64_t to
     return need;
 }
 
-extern "C" int p2p_spmm_mask(const void* x, int dtype, int64_t tokens, int64_t cols, int64_t ldx, const void* data,
-                             const int64_t* seg, int64_t rows, void* y, int64_t ldy, void* workspace,
-                             size_t workspace_bytes, void* stream) {
+namespace {
+int spmm_mask_impl(const void* x, int dtype, int64_t tokens, int64_t cols, int64_t ldx, const void* data,
+                   const int64_t* seg, int64_t rows, void* const* ys, int n_ys, int64_t y_col0, int64_t ldy,
+                   void* workspace, size_t workspace_bytes, void* stream) {
     P2P_REQUIRE(tokens >= 0 && rows >= 0 && cols >= 1, "p2p_spmm_mask: bad shape");
     if (tokens == 0 || rows == 0) return P2P_OK;
     if (dtype != P2P_BF16 && dtype != P2P_F16) return fail(P2P_EUNSUPPORTED, "p2p_spmm_mask: bf16 or f16");
-    P2P_REQUIRE(x && data && seg && y, "p2p_spmm_mask: null pointer");
+    P2P_REQUIRE(x && data && seg && ys && n_ys >= 1 && n_ys <= kMaxPeers, "p2p_spmm_mask: null pointer or %d outputs",
+                n_ys);
+    for (int k = 0; k < n_ys; ++k) P2P_REQUIRE(ys[k], "p2p_spmm_mask: null output %d", k);
     P2P_REQUIRE(aligned16(data), "p2p_spmm_mask: the layout must start on a 16-byte boundary");
     P2P_REQUIRE(cols % 8 == 0 && ldx % 8 == 0 && ldx >= cols && aligned16(x),
                 "p2p_spmm_mask: x needs 16-byte aligned rows (cols and ldx multiples of 8)");
-    P2P_REQUIRE(ldy >= rows, "p2p_spmm_mask: ldy %lld below rows %lld", (long long)ldy, (long long)rows);
+    P2P_REQUIRE(y_col0 >= 0 && ldy >= y_col0 + rows, "p2p_spmm_mask: ldy %lld below columns %lld + %lld",
+                (long long)ldy, (long long)y_col0, (long long)rows);
     P2P_REQUIRE(rows <= 0x7fffffff && cols <= 0x7fffffff, "p2p_spmm_mask: too large");
     const int64_t row_tiles = (rows + mk::kTileRows - 1) / mk::kTileRows;
     const int col_tiles = (int)((cols + mk::kTileCols - 1) / mk::kTileCols);
@@ -810,7 +825,10 @@ extern "C" int p2p_spmm_mask(const void* x, int dtype, int64_t tokens, int64_t c
         prm.ring_bytes = pl.ring_bytes;
         prm.units = row_tiles * col_tiles;
         plan_runs(row_tiles, col_tiles, tn, pl, &prm.splits, &prm.per_split, &prm.cluster, &prm.ctas);
-        prm.y = reinterpret_cast<char*>(y) + t0 * ldy * 2;
+        for (int k = 0; k < kMaxPeers; ++k)
+            prm.ys[k] = k < n_ys ? reinterpret_cast<char*>(ys[k]) + t0 * ldy * 2 : nullptr;
+        prm.n_ys = n_ys;
+        prm.y_col0 = y_col0;
         prm.ldy = ldy;
         prm.tickets = reinterpret_cast<unsigned*>(workspace);
         prm.partial = reinterpret_cast<float*>(reinterpret_cast<char*>(workspace) + kTicketRegion);
@@ -824,6 +842,23 @@ extern "C" int p2p_spmm_mask(const void* x, int dtype, int64_t tokens, int64_t c
             return e;
     }
     return P2P_OK;
+}
+}  // namespace
+
+extern "C" int p2p_spmm_mask(const void* x, int dtype, int64_t tokens, int64_t cols, int64_t ldx, const void* data,
+                             const int64_t* seg, int64_t rows, void* y, int64_t ldy, void* workspace,
+                             size_t workspace_bytes, void* stream) {
+    void* ys[1] = {y};
+    return spmm_mask_impl(x, dtype, tokens, cols, ldx, data, seg, rows, ys, 1, 0, ldy, workspace, workspace_bytes,
+                          stream);
+}
+
+extern "C" int p2p_spmm_mask_peers(const void* x, int dtype, int64_t tokens, int64_t cols, int64_t ldx,
+                                   const void* data, const int64_t* seg, int64_t rows, void* const* ys, int n_ys,
+                                   int64_t y_col0, int64_t ldy, void* workspace, size_t workspace_bytes,
+                                   void* stream) {
+    return spmm_mask_impl(x, dtype, tokens, cols, ldx, data, seg, rows, ys, n_ys, y_col0, ldy, workspace,
+                          workspace_bytes, stream);
 }
 
 extern "C" int p2p_spmm_mask_status(int reset, void* stream) {

@@ -38,14 +38,9 @@ def _rows2d(x: torch.Tensor) -> torch.Tensor:
 def sumsq_cols(x: torch.Tensor, sums: torch.Tensor) -> torch.Tensor:
     """sums += x.float().pow(2).sum(0).double() over x [..., cols] (p2p/wanda.py:37-40). sums: float64 [cols]."""
     require_cuda(x, sums)
-    x = _rows2d(x)
-    if sums.dtype != torch.float64 or sums.numel() != x.shape[1] or not sums.is_contiguous():
+    if sums.dtype != torch.float64 or sums.numel() != x.shape[-1] or not sums.is_contiguous():
         raise P2PError("sums must be a contiguous float64 vector of x's columns")
-    lib = _lib.load()
-    need = lib.p2p_sumsq_workspace(x.shape[0], x.shape[1], dtype_code(x))
-    ws = _workspace(x.device, need) if need else None
-    call("p2p_sumsq_cols", ptr(x), dtype_code(x), x.shape[0], x.shape[1], x.stride(0), ptr(sums), ptr(ws),
-         0 if ws is None else ws.numel(), stream_of(x))
+    _lib.ops().sumsq_cols(x, sums)
     return sums
 
 
@@ -267,23 +262,36 @@ def mask_build(blocks: list, cols: int) -> tuple:
 
 def spmm_mask(x: torch.Tensor, data: torch.Tensor, seg: torch.Tensor, rows: int, cols: int,
               out: torch.Tensor | None = None) -> torch.Tensor:
-    """y [tokens, rows] = x [tokens, cols] times a module in the bitmask layout (tcgen05, weights in TMEM)."""
+    """y [tokens, rows] = x [tokens, cols] times a module in the bitmask layout (tcgen05, weights in TMEM), through the
+    torch operator p2p_b200::spmm_mask."""
+    require_cuda(x)
+    if x.dim() != 2 or x.shape[1] != cols:
+        raise P2PError(f"x of {tuple(x.shape)} does not have {cols} columns")
+    if out is None:
+        out = _lib.ops().spmm_mask(x, data, seg, rows, cols)
+    else:
+        _lib.ops().spmm_mask_into(x, data, seg, rows, cols, _out(out, (x.shape[0], rows), x))
+    if CHECK_WAITS:
+        spmm_mask_status(x.device)
+    return out
+
+
+def spmm_mask_peers(x: torch.Tensor, data: torch.Tensor, seg: torch.Tensor, rows: int, cols: int, ys, n_ys: int,
+                    y_col0: int, ldy: int) -> None:
+    """This rank's rows of y = x times a module in the bitmask layout, stored at columns y_col0.. of each of the n_ys
+    y buffers (a ctypes array of device pointers: every rank's y, peers' through peer memory)."""
     require_cuda(x)
     if x.dim() != 2 or x.shape[1] != cols:
         raise P2PError(f"x of {tuple(x.shape)} does not have {cols} columns")
     if x.stride(1) != 1 or x.stride(0) % 8 or x.data_ptr() % 16:
         x = x.contiguous()
-        if x.data_ptr() % 16:
-            x = x.clone()
-    out = _out(out, (x.shape[0], rows), x)
     lib = _lib.load()
     need = lib.p2p_spmm_mask_workspace(rows, cols, x.shape[0])
     ws = _workspace(x.device, need, "spmm_mask") if need else None
-    call("p2p_spmm_mask", ptr(x), dtype_code(x), x.shape[0], cols, x.stride(0), ptr(data), ptr(seg), rows, ptr(out),
-         out.stride(0), ptr(ws), 0 if ws is None else ws.numel(), stream_of(x))
+    call("p2p_spmm_mask_peers", ptr(x), dtype_code(x), x.shape[0], cols, x.stride(0), ptr(data), ptr(seg), rows, ys,
+         n_ys, y_col0, ldy, ptr(ws), 0 if ws is None else ws.numel(), stream_of(x))
     if CHECK_WAITS:
         spmm_mask_status(x.device)
-    return out
 
 
 def spmm_mask_status(device=None, reset: bool = True) -> None:
@@ -294,20 +302,15 @@ def spmm_mask_status(device=None, reset: bool = True) -> None:
 
 def spmm_tc(x: torch.Tensor, words: torch.Tensor, seg: torch.Tensor, rows: int, cols: int, seg_cap: int,
             out: torch.Tensor | None = None) -> torch.Tensor:
-    """y [tokens, rows] = x [tokens, cols] times a module in the tensor-core layout (tcgen05, bf16/f16)."""
+    """y [tokens, rows] = x [tokens, cols] times a module in the tensor-core layout (tcgen05, bf16/f16), through the
+    torch operator p2p_b200::spmm_tc."""
     require_cuda(x)
     if x.dim() != 2 or x.shape[1] != cols:
         raise P2PError(f"x of {tuple(x.shape)} does not have {cols} columns")
-    if x.stride(1) != 1 or x.stride(0) % 8 or x.data_ptr() % 16:
-        x = x.contiguous()
-        if x.data_ptr() % 16:
-            x = x.clone()
-    out = _out(out, (x.shape[0], rows), x)
-    lib = _lib.load()
-    need = lib.p2p_spmm_tc_workspace(rows, cols, x.shape[0])
-    ws = _workspace(x.device, need, "spmm_tc") if need else None
-    call("p2p_spmm_tc", ptr(x), dtype_code(x), x.shape[0], cols, x.stride(0), ptr(words), ptr(seg), rows, seg_cap,
-         ptr(out), out.stride(0), ptr(ws), 0 if ws is None else ws.numel(), stream_of(x))
+    if out is None:
+        out = _lib.ops().spmm_tc(x, words, seg, rows, cols, seg_cap)
+    else:
+        _lib.ops().spmm_tc_into(x, words, seg, rows, cols, seg_cap, _out(out, (x.shape[0], rows), x))
     if CHECK_WAITS:
         spmm_tc_status(x.device)
     return out
@@ -352,9 +355,12 @@ def _same(ts, ref: torch.Tensor) -> list:
 
 
 def combine(parts: list, h: torch.Tensor, h_copy: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
-    """h' = l_0(h) + sum_mid dtype(l_k(h) - h) + dtype(l_last(h~) - h~), fp32 sums (p2p/replica.py:81-85)."""
+    """h' = l_0(h) + sum_mid dtype(l_k(h) - h) + dtype(l_last(h~) - h~), fp32 sums (p2p/replica.py:81-85), through
+    the torch operator p2p_b200::combine."""
     parts = _same(parts, h)
     h, h_copy = _same([h, h_copy], h)
+    if out is None:
+        return _lib.ops().combine(parts, h, h_copy)
     out = _out(out, tuple(h.shape), h, whole=True)
     call("p2p_combine", _ptr_array(parts), len(parts), ptr(h), ptr(h_copy), ptr(out), dtype_code(h), h.numel(),
          stream_of(h))
@@ -362,8 +368,11 @@ def combine(parts: list, h: torch.Tensor, h_copy: torch.Tensor, out: torch.Tenso
 
 
 def sum_parts(parts: list, out: torch.Tensor | None = None) -> torch.Tensor:
-    """dtype(sum of the parts in fp32, member order) (p2p/route.py:825-831)."""
+    """dtype(sum of the parts in fp32, member order) (p2p/route.py:825-831), through the torch operator
+    p2p_b200::sum_parts."""
     parts = _same(parts, parts[0])
+    if out is None:
+        return _lib.ops().sum_parts(parts)
     out = _out(out, tuple(parts[0].shape), parts[0], whole=True)
     call("p2p_sum_parts", _ptr_array(parts), len(parts), ptr(out), dtype_code(out), out.numel(), stream_of(out))
     return out

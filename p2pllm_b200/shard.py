@@ -2,19 +2,28 @@
 
 Wanda keeps the top-k of each output row on its own (p2p/wanda.py:83), so a module's rows split across ranks with no
 exchange at selection time: every rank holds a contiguous run of whole 128-row tiles (the GEMM's unit) and the full x,
-computes its rows of y, and one all-gather over NCCL (NVLink) assembles y [T, rows] on every rank. Runs of rows are as
-equal as whole tiles allow, earlier ranks taking the extra tile.
+computes its rows of y, and y [T, rows] is assembled on every rank. Runs of rows are as equal as whole tiles allow,
+earlier ranks taking the extra tile.
+
+Two ways to assemble y:
+  fused (the default on GPUs of one node): the bitmask-layout GEMM stores each of its rows of y straight into every
+      rank's y buffer (symmetric memory, plain stores over NVLink), and a bounded peer barrier (PeerGroup) makes them
+      visible -- the all-gather fused into the GEMM's epilogue, no separate collective, no copies;
+  "nccl": the rank's GEMM writes its slot of a gather buffer, one NCCL all_gather_into_tensor collects the slots.
 
     row_ranges(rows, world)          [(start, stop)] per rank
     shard_blocks(blocks, start, stop)  the part of a module's block list covering rows [start, stop)
-    ShardedCompact                   a rank's Compact over its rows, with the all-gather of y
+    PeerGroup                        flag arrays in peer memory and the barrier over them
+    ShardedCompact                   a rank's Compact over its rows, with y assembled on every rank
 """
 from __future__ import annotations
+
+import ctypes
 
 import torch
 import torch.distributed as dist
 
-from . import compact
+from . import _lib, compact, kernels
 
 TILE_ROWS = 128
 
@@ -38,6 +47,10 @@ def _rows(block: tuple) -> int:
     return block[1].shape[-2]
 
 
+def _cols(block: tuple) -> int:
+    return block[3] if block[0] in ("sparse", "compact") else block[1].shape[-1]
+
+
 def _take(block: tuple, a: int, b: int) -> tuple:
     if block[0] == "dense":
         return ("dense", block[1][..., a:b, :])
@@ -57,21 +70,92 @@ def shard_blocks(blocks: list, start: int, stop: int) -> list:
     return out
 
 
+def _symmetric(shape, dtype, device, group):
+    """A tensor in symmetric memory and the device addresses of every rank's copy of it (ctypes array, rank order)."""
+    import torch.distributed._symmetric_memory as symm_mem
+    t = symm_mem.empty(*shape, dtype=dtype, device=device)
+    handle = symm_mem.rendezvous(t, group if group is not None else dist.group.WORLD)
+    ptrs = list(handle.buffer_ptrs)
+    return t, (ctypes.c_void_p * len(ptrs))(*ptrs)
+
+
+class PeerGroup:
+    """Flag arrays in peer memory (one per rank, 8 slots each) and the barrier over them (p2p_peer_barrier): after
+    barrier(), every store the ranks' streams made before it is visible on every rank. Created by all ranks together."""
+
+    def __init__(self, group=None, device=None):
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+        self.flags, self.ptrs = _symmetric((8,), torch.int32, self.device, group)
+        self.flags.zero_()
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group)                         # every rank's flags are zero before the first barrier
+        self.epoch = 0
+
+    def barrier(self, timeout_us: int = 5_000_000) -> None:
+        self.epoch += 1
+        _lib.call("p2p_peer_barrier", self.ptrs, self.world, self.rank, self.epoch, timeout_us,
+                  torch.cuda.current_stream(self.device).cuda_stream)
+
+    def status(self) -> None:
+        """Raises if a barrier gave up waiting for a rank. Syncs."""
+        _lib.call("p2p_peer_status", 1, torch.cuda.current_stream(self.device).cuda_stream)
+
+
 class ShardedCompact:
     """One rank's share of a compact module: its rows as a Compact, and apply() returning the whole y on every rank.
-    The rank's GEMM writes its rows straight into its slot of the all-gather buffer; one all_gather_into_tensor over the
-    process group (NCCL on GPUs) collects every rank's slot, and the slots are laid side by side into y [T, rows]."""
 
-    def __init__(self, blocks: list, group=None):
+    fused (the default with more than one rank): the rank's GEMM (bitmask layout) stores its rows of y into every
+    rank's y buffer over NVLink, then a peer barrier; y is a view of one of two symmetric buffers, used in turn, so it
+    stays valid until this module's next-but-one apply. Otherwise ("nccl"): the GEMM writes its slot of a gather
+    buffer, and one all_gather_into_tensor over the process group collects the slots into y."""
+
+    def __init__(self, blocks: list, group=None, fused: bool | None = None, peers: PeerGroup | None = None):
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
         self.rows = sum(_rows(b) for b in blocks)
+        self.cols = _cols(blocks[0])
         self.ranges = row_ranges(self.rows, self.world)
         start, stop = self.ranges[self.rank]
-        self.local = compact.Compact(shard_blocks(blocks, start, stop)) if stop > start else None
+        self.fused = (self.world > 1) if fused is None else fused
+        mine = shard_blocks(blocks, start, stop)
+        self.local = None
+        if stop > start:
+            self.local = compact.Compact.__new__(compact.Compact)
+            self.local.tiles = compact.Tiles(mine, layout="mask" if self.fused else None)
         self.width = max(b - a for a, b in self.ranges)
         self.mine = stop - start
+        self.peers = peers
+        self._bufs, self._turn, self._cap = [], 0, 0
+
+    # ---- fused: y stored into every rank's buffer by the GEMM ----------------------------------------------------------
+
+    def prepare(self, tokens: int, dtype=torch.bfloat16, device=None) -> None:
+        """Symmetric y buffers for up to `tokens` rows (every rank calls it with the same tokens, together)."""
+        device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+        if self.peers is None:
+            self.peers = PeerGroup(self.group, device)
+        self._bufs = [_symmetric((tokens, self.rows), dtype, device, self.group) for _ in range(2)]
+        self._cap = tokens
+
+    def apply_fused(self, x2: torch.Tensor, sync: bool = True) -> torch.Tensor:
+        T = x2.shape[0]
+        if T > self._cap:
+            self.prepare(T, x2.dtype, x2.device)
+        buf, ptrs = self._bufs[self._turn]
+        self._turn ^= 1
+        if self.local is not None:
+            t = self.local.tiles
+            kernels.spmm_mask_peers(x2, t.data, t.seg, self.mine, self.cols, ptrs, self.world, self.ranges[self.rank][0],
+                                    self.rows)
+        if sync:
+            self.peers.barrier()
+        return buf[:T]
+
+    # ---- nccl: a gather buffer and one all-gather ----------------------------------------------------------------------
 
     def local_part(self, x2: torch.Tensor, part: torch.Tensor) -> torch.Tensor:
         """This rank's rows of y into part [T, width] (columns past its rows zeroed)."""
@@ -93,10 +177,13 @@ class ShardedCompact:
             return slots.permute(1, 0, 2).reshape(T, self.world * self.width)
         return torch.cat([slots[r, :, :b - a] for r, (a, b) in enumerate(self.ranges)], dim=1)
 
-    def apply(self, layer, x: torch.Tensor, bias=None) -> torch.Tensor:
+    def apply(self, layer, x: torch.Tensor, bias=None, sync: bool = True) -> torch.Tensor:
         x2 = x.reshape(-1, x.shape[-1])
-        part = torch.empty(x2.shape[0], self.width, dtype=x.dtype, device=x.device)
-        y = self.gather(self.local_part(x2, part))
+        if self.fused and self.world > 1:
+            y = self.apply_fused(x2, sync)
+        else:
+            part = torch.empty(x2.shape[0], self.width, dtype=x.dtype, device=x.device)
+            y = self.gather(self.local_part(x2, part))
         if bias is not None:
             y = y + bias
         return y.reshape(*x.shape[:-1], self.rows)

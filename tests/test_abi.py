@@ -84,3 +84,21 @@ def test_withhold_test_entry_checks_its_limits(lib):
     assert st == -1 and b"1 ms to 2 s" in lib.p2p_last_error()
     st = lib.p2p_spmm_tc_withhold(fake, 0, 600, 64, 64, fake, fake, 128, 16, fake, 128, None, 0, 0, 5000, None)
     assert st == -1 and b"one launch" in lib.p2p_last_error()
+
+
+def test_torch_ops_load_and_propagate_shapes_on_meta_tensors(lib):
+    """The entry points as torch custom operators (p2p_b200::*, over the same C ABI): they register with the dispatcher
+    and their Meta kernels give the output shapes without touching a device."""
+    import torch
+    from p2pllm_b200 import build
+    build.build_ops()
+    ops = _lib.ops()
+    meta = lambda *shape, dtype=torch.bfloat16: torch.empty(*shape, device="meta", dtype=dtype)
+    y = ops.spmm_tc(meta(17, 4096), meta(1000, dtype=torch.int32), meta(513, dtype=torch.int64), 6144, 4096, 600)
+    assert y.shape == (17, 6144) and y.device.type == "meta" and y.dtype == torch.bfloat16
+    y = ops.spmm_mask(meta(272, 4096), meta(1000, dtype=torch.uint8), meta(513, dtype=torch.int64), 1024, 4096)
+    assert y.shape == (272, 1024)
+    h = meta(8, 96)
+    assert ops.combine([h, h, h], h, h).shape == (8, 96) and ops.sum_parts([h, h]).shape == (8, 96)
+    names = {"spmm_tc", "spmm_tc_into", "spmm_mask", "spmm_mask_into", "sumsq_cols", "combine", "sum_parts"}
+    assert all(hasattr(ops, n) for n in names)

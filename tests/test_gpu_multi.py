@@ -33,16 +33,48 @@ def _module(seed=0, rows=(1024, 256, 256), cols=2048, keep=33):
     return blocks, x
 
 
-def _sharded(rank, world):
+def _sharded(rank, world, fused=None):
     """(rel-L2 of the sharded y against the whole module's, y's shape, a hash of y's bits). The shards may split their
     columns differently from the whole module, so sums can differ in the last bf16 bit."""
     import hashlib
     from p2pllm_b200 import compact, shard
     blocks, x = _module()
-    y = shard.ShardedCompact(blocks).apply(None, x)
+    sc = shard.ShardedCompact(blocks, fused=fused)
+    y = sc.apply(None, x)
+    y2 = sc.apply(None, x * 2)                          # the other of the two buffers (fused), then the first again
+    y3 = sc.apply(None, x)
     want = compact.Compact(blocks).apply(None, x).double()
-    rel = float((y.double() - want).norm() / want.norm())
-    return rel, tuple(y.shape), hashlib.sha256(y.cpu().view(torch.int16).numpy().tobytes()).hexdigest()
+    rel = float((y3.double() - want).norm() / want.norm())
+    rel2 = float((y2.double() - 2 * want).norm() / (2 * want).norm())
+    if sc.peers is not None:
+        sc.peers.status()
+    return max(rel, rel2), tuple(y3.shape), hashlib.sha256(y3.cpu().view(torch.int16).numpy().tobytes()).hexdigest()
+
+
+def _sharded_nccl(rank, world):
+    return _sharded(rank, world, fused=False)
+
+
+def _barrier_gives_up(rank, world):
+    """Rank 1 enters a peer barrier that rank 0 never joins: its wait runs out after 20 ms, the status names rank 0,
+    and a barrier both ranks then join completes."""
+    from p2pllm_b200 import shard
+    from p2pllm_b200._lib import P2PError
+    peers = shard.PeerGroup()
+    failed = False
+    if rank == 1:
+        peers.barrier(timeout_us=20_000)
+        torch.cuda.synchronize()
+        try:
+            peers.status()
+        except P2PError as e:
+            failed = "rank 0" in str(e)
+    dist.barrier()                                       # the host learns of it; both ranks move on together
+    peers.epoch = 1
+    peers.barrier()
+    torch.cuda.synchronize()
+    peers.status()
+    return failed if rank == 1 else True
 
 
 def _hop(rank, world):
@@ -91,12 +123,19 @@ def test_sharded_module_on_one_gpu_is_the_module():
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-def test_sharded_module_over_two_gpus():
-    out = _spawn(_sharded, 2)
+@pytest.mark.parametrize("fn", [_sharded, _sharded_nccl], ids=["fused_peer_stores", "nccl_all_gather"])
+def test_sharded_module_over_two_gpus(fn):
+    out = _spawn(fn, 2)
     for rank in range(2):
         rel, shape, _ = out[rank]
         assert shape == (17, 1536) and rel <= 1e-3
-    assert out[0][2] == out[1][2]                       # the all-gather leaves the same y on every rank
+    assert out[0][2] == out[1][2]                       # the same y on every rank
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_peer_barrier_gives_up_on_a_rank_that_never_comes():
+    out = _spawn(_barrier_gives_up, 2)
+    assert out[1] is True and out[0] is True
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
