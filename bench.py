@@ -64,6 +64,10 @@ def parse():
     p.add_argument("--module", default="gate_up_proj", choices=list(MODULES))
     p.add_argument("--layout", default=None, choices=["tc", "mask"],
                    help="the tensor-core layout of the compact modules (default: the package's)")
+    p.add_argument("--pass-tokens", type=int, default=17,
+                   help="cfg5: tokens of a pass (a draft pass of 16 + 1 by default)")
+    p.add_argument("--cfg5-single-layer", action="store_true",
+                   help="cfg5: time one replica layer on one GPU instead of the layer-parallel plan")
     return p.parse_args()
 
 
@@ -345,22 +349,6 @@ def _region_ms(fn, steps: int, stream) -> float:
     return a.elapsed_time(b)
 
 
-def _flushed_ms(fn, steps: int, stream, flush: torch.Tensor) -> float:
-    """Device milliseconds of `steps` calls of fn, each timed alone after a write of `flush` (larger than L2), summed:
-    for working sets that L2 could hold."""
-    total = 0.0
-    for _ in range(steps):
-        flush.zero_()
-        a, b = _events()
-        torch.cuda._sleep(HEAD_START_CYCLES // 20)
-        a.record(stream)
-        fn()
-        b.record(stream)
-        b.synchronize()
-        total += a.elapsed_time(b)
-    return total
-
-
 def _module_tiles(layer, layout: str) -> dict:
     """The layer's modules in one tensor-core layout: {module: Tiles}."""
     from p2pllm_b200 import compact
@@ -586,6 +574,20 @@ def _e2e(layer, T: int, steps: int, warmup: int, device, stream) -> dict:
                    "input / output streams overlapping the kernels (double-buffered inputs)"}
 
 
+def _clone_shard(sc):
+    """The same shard with its own copy of the weight bytes (another address range), sharing everything else."""
+    import copy
+    other = copy.copy(sc)
+    if sc.local is not None:
+        tiles = copy.copy(sc.local.tiles)
+        for name in ("data", "words", "seg"):
+            if hasattr(tiles, name) and torch.is_tensor(getattr(tiles, name)):
+                setattr(tiles, name, getattr(tiles, name).clone())
+        other.local = copy.copy(sc.local)
+        other.local.tiles = tiles
+    return other
+
+
 def run_sharded(args, layer, rank, world, device, peaks):
     """The cfg2 layer row-sharded over `world` GPUs (shard.ShardedCompact: each rank whole 128-row tiles of every
     module and the full x). Headline: the all-gather fused into the GEMM (each rank's bitmask-layout GEMM stores its
@@ -628,29 +630,40 @@ def run_sharded(args, layer, rank, world, device, peaks):
                   flush=True)
         raise SystemExit(3)
 
-    # per-rank weights: from 4 GPUs on they fit in L2, so each step is timed alone after a write larger than L2
-    flush = torch.empty(2 * L2_BYTES, dtype=torch.uint8, device=device)
+    # A rank's shard of the weights is smaller than L2 from 4 GPUs on: each rank cycles through `copies` clones of its
+    # shards' weight bytes, more than twice L2 in all, so every step streams its weights from HBM, and the K steps are
+    # timed as one region (the launches keep their overlap, the peer barriers keep the ranks in step).
+    shard_bytes = sum(sharded[m].local.nbytes() for m in names if sharded[m].local is not None)
+    copies = max(1, -(-2 * L2_BYTES // max(shard_bytes, 1)))
+    rotation = [sharded] + [{m: _clone_shard(sharded[m]) for m in names} for _ in range(copies - 1)]
+    turn = [0]
 
     def step():
+        mods = rotation[turn[0] % copies]
+        turn[0] += 1
         for m in names:
-            sharded[m].apply_fused(xs[m], sync=False)
+            mods[m].apply_fused(xs[m], sync=False)
         peers.barrier()
 
     def kernels_only():
+        mods = rotation[turn[0] % copies]
+        turn[0] += 1
         for m in names:
-            sharded[m].apply_fused(xs[m], sync=False)
+            mods[m].apply_fused(xs[m], sync=False)
 
-    for _ in range(args.warmup):
+    for _ in range(max(args.warmup, copies)):
         step()
     torch.cuda.synchronize(device)
     dist.barrier()
     clocks = ClockSampler(device.index)
     with clocks:
-        local_ms = _flushed_ms(step, args.steps, stream, flush)
+        local_ms = _region_ms(step, args.steps, stream)
     dist.barrier()
     total_ms = max_over_ranks(local_ms, world, device)
-    kern_ms = max_over_ranks(_flushed_ms(kernels_only, args.steps, stream, flush), world, device)
+    kern_ms = max_over_ranks(_region_ms(kernels_only, args.steps, stream), world, device)
+    torch.cuda.synchronize(device)
     dist.barrier()
+    peers.barrier()
     peers.status()
     ms_per_step = total_ms / args.steps
     value = args.tokens * args.steps / (total_ms / 1e3)
@@ -658,24 +671,27 @@ def run_sharded(args, layer, rank, world, device, peaks):
     # the NCCL path: the rank's GEMM writes its slot, one all-gather a module
     nccl = {m: shard.ShardedCompact(blocks[m], fused=False) for m in names}
     parts = {m: torch.empty(args.tokens, nccl[m].width, dtype=torch.bfloat16, device=device) for m in names}
+    nccl_rotation = [nccl] + [{m: _clone_shard(nccl[m]) for m in names} for _ in range(copies - 1)]
 
     def nccl_step():
+        mods = nccl_rotation[turn[0] % copies]
+        turn[0] += 1
         for m in names:
-            nccl[m].gather(nccl[m].local_part(xs[m], parts[m]))
+            mods[m].gather(mods[m].local_part(xs[m], parts[m]))
 
     def nccl_gathers():
         for m in names:
             nccl[m].gather(parts[m])
 
-    for _ in range(3):
+    for _ in range(max(3, copies)):
         nccl_step()
     torch.cuda.synchronize(device)
     dist.barrier()
-    nccl_ms = max_over_ranks(_flushed_ms(nccl_step, args.steps, stream, flush), world, device)
+    nccl_ms = max_over_ranks(_region_ms(nccl_step, args.steps, stream), world, device)
     dist.barrier()
-    gath_ms = max_over_ranks(_flushed_ms(nccl_gathers, args.steps, stream, flush), world, device)
+    gath_ms = max_over_ranks(_region_ms(nccl_gathers, args.steps, stream), world, device)
     dist.barrier()
-    del nccl, parts
+    del nccl, parts, nccl_rotation
 
     # independent replicas (each rank the whole layer on its own tokens): the weak-scaling figure, kept beside
     for _ in range(3):
@@ -684,29 +700,60 @@ def run_sharded(args, layer, rank, world, device, peaks):
     dist.barrier()
     rep_ms = max_over_ranks(_region_ms(layer.step, args.steps, stream), world, device)
 
-    # e2e: rank 0 copies the step's inputs in from pinned memory and broadcasts them; every rank runs its shards,
-    # storing into every rank's y; rank 0 copies y back
+    # e2e: rank 0 copies the step's inputs in from pinned memory (input stream, double-buffered) and broadcasts them;
+    # every rank runs its shards, storing into every rank's y; rank 0 copies y back on an output stream while the next
+    # step computes. y of step k sits in the symmetric buffer k % 2 that step k + 2 overwrites on every rank, so rank 0
+    # enters step k + 1's peer barrier only once step k's copy-out has finished.
     host_x = {m: xs[m].cpu().pin_memory() for m in names} if rank == 0 else None
     host_y = {m: torch.empty(args.tokens, sharded[m].rows, dtype=torch.bfloat16).pin_memory() for m in names} \
         if rank == 0 else None
-    dev_x = {m: torch.empty_like(xs[m]) for m in names}
+    s_in, s_out = torch.cuda.Stream(device), torch.cuda.Stream(device)
+    dev_x = [{m: torch.empty_like(xs[m]) for m in names} for _ in range(2)]
+    landed, consumed, copied = ([torch.cuda.Event() for _ in range(2)] for _ in range(3))
+    for ev in consumed + copied:
+        ev.record(stream)
 
-    def e2e_step():
-        for m in names:
+    def e2e_run(n):
+        for k in range(n):
+            buf = k % 2
             if rank == 0:
-                dev_x[m].copy_(host_x[m], non_blocking=True)
-            dist.broadcast(dev_x[m], 0)
-        ys = {m: sharded[m].apply_fused(dev_x[m], sync=False) for m in names}
-        peers.barrier()
-        if rank == 0:
+                with torch.cuda.stream(s_in):
+                    s_in.wait_event(consumed[buf])
+                    for m in names:
+                        dev_x[buf][m].copy_(host_x[m], non_blocking=True)
+                    landed[buf].record(s_in)
+                stream.wait_event(landed[buf])
             for m in names:
-                host_y[m].copy_(ys[m], non_blocking=True)
+                dist.broadcast(dev_x[buf][m], 0)
+            mods = rotation[k % copies]
+            ys = {}
+            for m in names:
+                mods[m]._turn = buf                    # y buffer by step parity, whichever weight copy runs
+                ys[m] = mods[m].apply_fused(dev_x[buf][m], sync=False)
+            consumed[buf].record(stream)
+            if rank == 0:
+                stream.wait_event(copied[buf ^ 1])     # step k - 1's y has reached the host
+            peers.barrier()
+            if rank == 0:
+                done = torch.cuda.Event()
+                done.record(stream)
+                with torch.cuda.stream(s_out):
+                    s_out.wait_event(done)
+                    for m in names:
+                        host_y[m].copy_(ys[m], non_blocking=True)
+                    copied[buf].record(s_out)
 
-    for _ in range(3):
-        e2e_step()
+    e2e_run(max(3, copies))
     torch.cuda.synchronize(device)
     dist.barrier()
-    e2e_ms = max_over_ranks(_region_ms(e2e_step, args.steps, stream), world, device)
+    a, b = _events()
+    a.record(stream)
+    s_in.wait_stream(stream)
+    e2e_run(args.steps)
+    stream.wait_stream(s_out)
+    b.record(stream)
+    torch.cuda.synchronize(device)
+    e2e_ms = max_over_ranks(a.elapsed_time(b), world, device)
     peers.status()
     h2d = sum(t.numel() * 2 for t in xs.values())
     d2h = sum(args.tokens * sharded[m].rows * 2 for m in names)
@@ -725,8 +772,9 @@ def run_sharded(args, layer, rank, world, device, peaks):
                        "parallelism": f"row-sharded over {world} GPUs (whole 128-row tiles of every module a rank, "
                                       "full x); y gathered in the GEMM's epilogue by peer stores over NVLink, one "
                                       "bounded peer barrier a step",
-                       "l2": "per-rank weights may fit L2: every step timed alone after a %d MB write"
-                             % (2 * L2_BYTES >> 20)},
+                       "l2": "inputs larger than L2: each rank cycles through %d copies of its %.0f MB of shard "
+                             "weights (%.0f MB) vs %d MB L2" % (copies, shard_bytes / 1e6, copies * shard_bytes / 1e6,
+                                                                L2_BYTES >> 20)},
             "parity": {"passed": True, "checks": checks},
             "breakdown_us_per_step": {"fused_gemms": kern_ms / args.steps * 1e3,
                                       "barrier_and_skew": (total_ms - kern_ms) / args.steps * 1e3,
@@ -742,9 +790,261 @@ def run_sharded(args, layer, rank, world, device, peaks):
                          "how": "each rank the whole layer on its own tokens, no data-path collective"},
             "e2e": {"value": args.tokens * args.steps / (e2e_ms / 1e3), "unit": UNIT, "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h,
-                    "how": "rank 0: pinned-host inputs in, NCCL broadcast, every rank its fused shards + a peer "
-                           "barrier, rank 0: y back to pinned host memory"},
+                    "how": "rank 0: pinned-host inputs in (input stream), NCCL broadcast, every rank its fused shards "
+                           "+ a peer barrier, rank 0: y back to pinned host memory on an output stream overlapping "
+                           "the next step",
+                    "d2h_mb_per_step": d2h / 1e6},
             "gpu_launches": args.steps * (len(names) + 1),
+            "clocks": clocks.summary(),
+        }
+        print(json.dumps(out), flush=True)
+
+
+CFG5_DENSE_LAYER_BYTES = sum(p.rows * p.cols * 2 for p in workloads.QWEN25_32B)
+
+
+def _bcast_from(v, src: int, world: int, device):
+    """A float from rank src on every rank."""
+    if world == 1:
+        return v
+    import torch.distributed as dist
+    t = torch.tensor([float(v)], dtype=torch.float64, device=device)
+    dist.broadcast(t, src)
+    return float(t.item())
+
+
+def _cfg5_down_sharded(args, rank, world, device, stream) -> dict:
+    """The replica's 5120 x 27648 down projection (keep 40) row-sharded over the ranks, y gathered in the GEMM's
+    epilogue by peer stores (shard.ShardedCompact): microseconds a call at the pass's T, against the same module on one
+    GPU (rel-L2, rank 0) and the same bits on every rank."""
+    import hashlib
+    import torch.distributed as dist
+    from p2pllm_b200 import compact, shard, wanda
+    T = args.pass_tokens
+    w = workloads.cfg5_weights(1, device)["down"]
+    norms = workloads.cfg5_norms(1, device)["down"]
+    values, idx = wanda.select(w, 40, norms)
+    del w
+    blocks = [("compact", values, idx, 27648)]
+    x = workloads.activations(27648, T, 77, device)
+    if world == 1:
+        whole = compact.Compact(blocks)
+        us = _region_ms(lambda: whole.apply(None, x), args.steps, stream) / args.steps * 1e3
+        return {"us_per_call": us, "ranks": 1, "layout": whole.tiles.layout, "weights_mb": whole.nbytes() / 1e6}
+    peers = shard.PeerGroup(None, device)
+    sc = shard.ShardedCompact(blocks, fused=True, peers=peers)
+    sc.prepare(T, torch.bfloat16, device)
+    y = sc.apply(None, x).clone()
+    digest = int.from_bytes(hashlib.sha256(y.cpu().view(torch.int16).numpy().tobytes()).digest()[:7], "little")
+    every = [torch.zeros(1, dtype=torch.int64, device=device) for _ in range(world)]
+    dist.all_gather(every, torch.tensor([digest], dtype=torch.int64, device=device))
+    same = all(int(e.item()) == digest for e in every)
+    rel = 0.0
+    if rank == 0:
+        want = compact.Compact(blocks).apply(None, x).double()
+        rel = float((y.double() - want).norm() / want.norm())
+    copies = max(1, -(-2 * L2_BYTES // max(sc.local.nbytes(), 1)))
+    rotation = [sc] + [_clone_shard(sc) for _ in range(copies - 1)]
+    turn = [0]
+
+    def call():
+        rotation[turn[0] % copies].apply_fused(x, sync=False)
+        turn[0] += 1
+        peers.barrier()
+
+    for _ in range(max(3, copies)):
+        call()
+    torch.cuda.synchronize(device)
+    dist.barrier()
+    ms = max_over_ranks(_region_ms(call, args.steps, stream), world, device)
+    peers.status()
+    return {"us_per_call": ms / args.steps * 1e3, "ranks": world, "layout": "mask", "rows_per_rank": sc.mine,
+            "shard_mb": sc.local.nbytes() / 1e6, "rel_l2_vs_one_gpu": _bcast_from(rel, 0, world, device),
+            "same_bits_on_every_rank": same, "l2": f"{copies} copies of each rank's shard in turn",
+            "how": "each rank its 128-row tiles of the module, y stored into every rank's y by the GEMM's epilogue, "
+                   "one peer barrier a call"}
+
+
+def run_cfg5(args, rank, world, device, peaks):
+    """Config 5: the 64-layer Qwen2.5-32B-shaped model (workloads.DecoderBlock, random bf16
+    weights) as 32 pair-steps, each with the keep-40 replica of its first layer, placed contiguously over `world` GPUs
+    (plan.place). Each rank's share of a pass is one CUDA graph (plan.GraphedPass); the hidden state crosses each GPU
+    boundary through the peer-memory hop with the step's group combine computed in the send (plan.PeerHop). Passes of
+    T tokens are pipelined: rank r works on pass p while rank r + 1 works on pass p - 1. Beside it: one pass alone
+    (latency), the hop's one-way time (peer memory and NCCL), and the row-sharded down projection."""
+    import hashlib
+    import torch.distributed as dist
+    from p2pllm_b200 import plan
+    T, H = args.pass_tokens, 5120
+    stream = torch.cuda.current_stream(device)
+    s = plan.steps(workloads.CFG5_GROUPS, workloads.CFG5_LAYERS)
+    stages = plan.place(s, world)
+    t0 = time.time()
+    hop = plan.PeerHop(T, H, device=device) if world > 1 else None
+    runner = plan.PlanRunner(s, stages, rank, None, None, hop)
+    exact_ids, rep_ids = runner.layers_needed()
+    exact = {i: workloads.cfg5_exact(i, device) for i in exact_ids}
+    reps, rep_bytes = {}, 0
+    for i in rep_ids:
+        reps[i], nb = workloads.cfg5_replica(i, device, layout=args.layout)
+        rep_bytes += nb
+    runner.layer, runner.replica = exact.__getitem__, reps.__getitem__
+    torch.cuda.synchronize(device)
+    build_s = time.time() - t0
+    like = torch.zeros(T, H, dtype=torch.bfloat16, device=device)
+    inputs = [workloads.cfg5_input(p, T, device) for p in range(4)]
+    last = world - 1
+
+    # parity: pass 0 eager through the peer hop, and through the NCCL hop: the same bits on the last rank
+    out0 = runner.pass_(0, inputs[0] if rank == 0 else None, like=like)
+    same_nccl = True
+    if world > 1:
+        nccl_runner = plan.PlanRunner(s, stages, rank, exact.__getitem__, reps.__getitem__, plan.NcclHop())
+        out_n = nccl_runner.pass_(0, inputs[0] if rank == 0 else None, like=like)
+        nccl_runner.hop.finish()
+        torch.cuda.synchronize(device)
+        if rank == last:
+            same_nccl = bool(torch.equal(out0, out_n))
+        hop.status()
+    digest = 0
+    if rank == last:
+        digest = int.from_bytes(hashlib.sha256(out0.cpu().view(torch.int16).numpy().tobytes()).digest()[:6], "little")
+    digest = int(_bcast_from(digest, last, world, device))
+    same_nccl = bool(_bcast_from(1.0 if same_nccl else 0.0, last, world, device))
+
+    graphed = plan.GraphedPass(runner, like, next_pass=1)
+    if rank == 0:
+        graphed.h_in.copy_(inputs[0])
+    graphed.run()                                      # pass 1 on pass 0's input: the graph gives the eager bits
+    torch.cuda.synchronize(device)
+    same_graph = bool(torch.equal(graphed.h_out, out0)) if rank == last else True
+    same_graph = bool(_bcast_from(1.0 if same_graph else 0.0, last, world, device))
+    done = [2]
+
+    def one_pass():
+        if rank == 0:
+            graphed.h_in.copy_(inputs[done[0] % 4])
+        graphed.run()
+        done[0] += 1
+
+    for _ in range(args.warmup):
+        one_pass()
+    torch.cuda.synchronize(device)
+    barrier(world)
+    # timed: K pipelined passes
+    clocks = ClockSampler(device.index)
+    with clocks:
+        ms = max_over_ranks(_region_ms(one_pass, args.steps, stream), world, device)
+    if hop is not None:
+        hop.status()
+    # one pass alone: the pipeline empty before and after it
+    torch.cuda.synchronize(device)
+    barrier(world)
+    latency_ms = max_over_ranks(_region_ms(one_pass, 1, stream), world, device)
+
+    # e2e: pinned-host inputs into rank 0, the pass's output back to pinned host memory on the last rank
+    host_in = [t.cpu().pin_memory() for t in inputs]
+    host_out = torch.empty(T, H, dtype=torch.bfloat16).pin_memory()
+
+    def e2e_pass():
+        if rank == 0:
+            graphed.h_in.copy_(host_in[done[0] % 4], non_blocking=True)
+        graphed.run()
+        if rank == last:
+            host_out.copy_(graphed.h_out, non_blocking=True)
+        done[0] += 1
+
+    for _ in range(3):
+        e2e_pass()
+    torch.cuda.synchronize(device)
+    barrier(world)
+    e2e_ms = max_over_ranks(_region_ms(e2e_pass, args.steps, stream), world, device)
+    if hop is not None:
+        hop.status()
+
+    # the hop alone: ping-pong of a [T, 5120] bf16 hidden state between ranks 0 and 1, one-way time
+    hop_us = {}
+    if world > 1:
+        ping = plan.PeerHop(T, H, device=device)
+        buf = torch.zeros_like(like)
+        x = inputs[0]
+        k = [0]
+
+        def peer_rt():
+            if rank == 0:
+                ping.send(plan.PART_SUM, [x], None, None, [1], k[0])
+                ping.recv([1], k[0], like, out=buf)
+            elif rank == 1:
+                ping.recv([0], k[0], like, out=buf)
+                ping.send(plan.PART_SUM, [buf], None, None, [0], k[0])
+            k[0] += 1
+
+        def nccl_rt():
+            if rank == 0:
+                dist.send(x, 1)
+                dist.recv(buf, 1)
+            elif rank == 1:
+                dist.recv(buf, 0)
+                dist.send(buf, 0)
+
+        for fn, name in ((peer_rt, "peer_memory"), (nccl_rt, "nccl")):
+            for _ in range(20):
+                fn()
+            torch.cuda.synchronize(device)
+            barrier(world)
+            rt_ms = _region_ms(fn, 200, stream) if rank < 2 else 0.0
+            hop_us[name] = _bcast_from(rt_ms / 200 / 2 * 1e3, 0, world, device)
+        ping.status()
+
+    down = _cfg5_down_sharded(args, rank, world, device, stream)
+
+    # bytes a pass reads on each rank: its dense layers' weights, its replicas' weights (activations are < 0.1%)
+    my_bytes = len(exact_ids) * CFG5_DENSE_LAYER_BYTES + rep_bytes
+    stage_bytes = max_over_ranks(float(my_bytes), world, device)
+    per_gpu_gbs = stage_bytes * args.steps / (ms / 1e3) / 1e9
+    st = stages[rank]
+    n_steps = st.last - st.first + 1
+    mine = n_steps * 4 + n_steps - (1 if runner.dsts else 0) + (1 if runner.dsts else 0) + (1 if runner.srcs else 0) \
+        + (1 if (runner.srcs or runner.dsts) else 0)
+    launches = mine
+    if world > 1:
+        t = torch.tensor([mine], dtype=torch.int64, device=device)
+        dist.all_reduce(t)
+        launches = int(t.item())
+    if rank == 0:
+        out = {
+            "metric": "config-5 layer-parallel plan tokens/s (Qwen2.5-32B shapes, 64 layers as 32 pair-steps with "
+                      f"keep-40 replicas, T={T})",
+            "value": T * args.steps / (ms / 1e3), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded N(0,0.02) bf16 weights; replicas selected with lognormal channel norms; "
+                    "RMS-normalised N(0,1) pass inputs; no checkpoint)",
+            "config": {"workload": f"cfg5 Qwen2.5-32B-shaped plan, T={T}", "layers": 64, "steps_per_gpu": n_steps,
+                       "placement": "contiguous runs of whole pair-steps, one run a GPU",
+                       "layer": "DecoderBlock: RMSNorm, qkv, causal attention of the pass's tokens (GQA 40/8, no KV "
+                                "cache, no rotary), o, RMSNorm, SiLU(gate)*up, down; dense layers on cuBLAS, replicas "
+                                "on the compact GEMM",
+                       "step": "K passes pipelined over the GPUs, each rank's share of a pass one CUDA graph replay",
+                       "l2": "inputs larger than L2: each rank reads %.1f GB of weights a pass" % (my_bytes / 1e9)},
+            "parity": {"output_sha256_48": "%012x" % digest, "peer_hop_vs_nccl_hop_same_bits": same_nccl,
+                       "graphed_vs_eager_same_bits": same_graph,
+                       "how": "pass 0 through the plan with the peer-memory hop and with the NCCL hop; the hash is "
+                              "the same at every GPU count when the plan is exact"},
+            "latency_ms_one_pass": latency_ms,
+            "hop_us_one_way": hop_us or None,
+            "hop_bytes": T * H * 2,
+            "down_row_sharded": down,
+            "roofline": {"bound": "hbm", "achieved": per_gpu_gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                         "frac": per_gpu_gbs / peaks["hbm_gbs"], "traffic": None, "peak_source": peaks["source"],
+                         "kernel": "the slowest rank's stage: dense-layer and replica weight bytes a pass over the "
+                                   "pipelined time a pass"},
+            "e2e": {"value": T * args.steps / (e2e_ms / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": T * H * 2,
+                    "d2h_bytes_per_step": T * H * 2,
+                    "how": "rank 0 copies each pass's input from pinned host memory, the last rank copies the output "
+                           "back, inside the timed region"},
+            "gpu_launches": launches * args.steps,
+            "build_s": build_s,
             "clocks": clocks.summary(),
         }
         print(json.dumps(out), flush=True)
@@ -855,6 +1155,22 @@ def run_extra(args):
 def main():
     args = parse()
     rank, world, local = dist_env()
+    if args.workload == "cfg5" and not args.cfg5_single_layer and args.impl == "b200":
+        if world > 1:
+            import datetime
+            import torch.distributed as dist
+            torch.cuda.set_device(local)
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                    device_id=torch.device("cuda", local))
+        try:
+            device = torch.device("cuda", local)
+            torch.cuda.set_device(device)
+            run_cfg5(args, rank, world, device, measured_peaks())
+        finally:
+            if world > 1:
+                import torch.distributed as dist
+                dist.destroy_process_group()
+        return
     if args.workload != "cfg2":
         if rank == 0:
             run_extra(args)

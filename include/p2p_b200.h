@@ -292,6 +292,49 @@ int p2p_sum_parts(const void* const* parts, int n, void* out, int dtype, int64_t
  * Replaces p2p/route.py:1268-1274 (_member's part). */
 int p2p_member_part(const void* y, const void* x, void* out, int dtype, int64_t n_elem, void* stream);
 
+/* ------------------------------------------------------------------------------------------------------------------
+ * (3b) The step hop of a layer-parallel plan over NVLink peer memory, part and sum fused in
+ * ------------------------------------------------------------------------------------------------------------------ */
+
+/* What p2p_hop_send stores: P2P_PART_SUM: dtype(sum of float(parts)) in member order (one part: the part itself);
+ * P2P_PART_DIFF: dtype(float(parts[0]) - float(h)), a middle or last member's part; P2P_PART_COMBINE: the whole group
+ * combine of p2p_combine over parts, h and h_copy. */
+enum { P2P_PART_SUM = 0, P2P_PART_DIFF = 1, P2P_PART_COMBINE = 2 };
+
+/* Bytes of one rank's hop inbox: 256 bytes of counters, then n_ranks x ring slots of cap_elems elements (each slot
+ * rounded up to 256 bytes). Allocate it where every rank of the node addresses it (symmetric memory or CUDA IPC),
+ * zeroed before the first hop; 0 for arguments out of range (1..8 ranks, 1..64 slots). */
+size_t p2p_hop_inbox_bytes(int n_ranks, int64_t cap_elems, int dtype, int ring);
+
+/* Sender side of the hop of pass `pass` (0, 1, 2, ... per sender and receiver pair; read from device memory at
+ * *pass_at instead when pass_at is not null, so a CUDA graph can replay the hop pass after pass): computes this
+ * rank's part (mode above) of n_elem elements and stores it into slot [me][pass % ring] of the inbox of every rank in dsts
+ * (inboxes[r]: rank r's inbox as this GPU addresses it), then signals each of them. Before storing it waits until
+ * each destination has consumed pass - ring of this rank. n_elem * element size a multiple of 16 bytes, at most
+ * cap_elems; parts, h, h_copy 16-byte aligned. Waits are bounded by wait_us (1 ms .. 60 s); a wait that gives up is
+ * reported by p2p_hop_status. Replaces p2p/route.py:800-810 (_send_piece, one NCCL isend per destination) with the
+ * part of p2p/route.py:1268-1274 (_member) or the combine of p2p/replica.py:81-85 computed in the same pass. */
+int p2p_hop_send(int mode, const void* const* parts, int n_parts, const void* h, const void* h_copy, int dtype,
+                 int64_t n_elem, void* const* inboxes, int n_ranks, int me, const int* dsts, int n_dst, uint32_t pass,
+                 const uint32_t* pass_at, int ring, int64_t cap_elems, int64_t wait_us, void* stream);
+
+/* Receiver side: waits until every rank in srcs (member order) has stored its part of pass `pass` (or *pass_at)
+ * into this rank's inbox, writes out = dtype(sum of float(parts)) in member order, and frees the slots for the senders. The same
+ * n_elem, ring and cap_elems as the senders'. Replaces p2p/route.py:365-402 (_recv) with p2p/route.py:825-831
+ * (_summed) in the same pass. A sender and receiver run on different GPUs, one process each, or on one GPU in stream
+ * order with the sends first. */
+int p2p_hop_recv(void* const* inboxes, int n_ranks, int me, const int* srcs, int n_src, uint32_t pass,
+                 const uint32_t* pass_at, int ring, int64_t cap_elems, int dtype, int64_t n_elem, void* out,
+                 int64_t wait_us, void* stream);
+
+/* Adds 1 to each of the n (1..32) uint32 counters in device memory, on `stream`: the pass number a graphed pass reads
+ * through pass_at moves on after the pass. No counterpart in the reference (it launches every pass from the host). */
+int p2p_hop_advance(uint32_t* counters, int n, void* stream);
+
+/* P2P_OK unless a hop wait since the last reset gave up (P2P_ECUDA, naming the side and the rank); reset != 0 clears
+ * it. Syncs the stream. */
+int p2p_hop_status(int reset, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

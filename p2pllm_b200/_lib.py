@@ -54,6 +54,13 @@ SIGNATURES = {
                              _sz, _vp], _int),
     "p2p_peer_barrier": ([ctypes.POINTER(_vp), _int, _int, ctypes.c_uint32, _i64, _vp], _int),
     "p2p_peer_status": ([_int, _vp], _int),
+    "p2p_hop_inbox_bytes": ([_int, _i64, _int, _int], _sz),
+    "p2p_hop_send": ([_int, ctypes.POINTER(_vp), _int, _vp, _vp, _int, _i64, ctypes.POINTER(_vp), _int, _int,
+                      ctypes.POINTER(_int), _int, ctypes.c_uint32, _vp, _int, _i64, _i64, _vp], _int),
+    "p2p_hop_recv": ([ctypes.POINTER(_vp), _int, _int, ctypes.POINTER(_int), _int, ctypes.c_uint32, _vp, _int, _i64,
+                      _int, _i64, _vp, _i64, _vp], _int),
+    "p2p_hop_advance": ([_vp, _int, _vp], _int),
+    "p2p_hop_status": ([_int, _vp], _int),
     "p2p_spmm_tc_workspace": ([_i64, _i64, _i64], _sz),
     "p2p_spmm_tc": ([_vp, _int, _i64, _i64, _i64, _vp, _vp, _i64, _i64, _vp, _i64, _vp, _sz, _vp], _int),
     "p2p_spmm_tc_grouped": ([_vp, _int, _i64, _i64, _i64, _vp, _vp, _i64, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _i64,

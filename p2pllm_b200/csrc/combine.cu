@@ -8,53 +8,12 @@
 // The reference runs these as 2n separate ATen elementwise ops, each re-reading h; here one kernel reads every
 // member's output once, 16 bytes a thread, and keeps the fp32 running sum in registers. Rounding follows the reference
 // step for step: each difference is rounded to the model dtype before it is added in fp32.
-#include "common.cuh"
+#include "elementwise.cuh"
 
 namespace p2p {
 namespace {
 
-constexpr int kMaxParts = 16;
 constexpr int kCombBlock = 256;
-
-struct Parts {
-    const void* p[kMaxParts];
-    int n;
-};
-
-enum Mode { kReplica = 0, kSum = 1, kDiff = 2 };
-
-template <typename T> __device__ __forceinline__ float rnd(float v) { return to_f32(from_f32<T>(v)); }
-
-template <typename T, int VEC> struct Pack {
-    T v[VEC];
-};
-
-template <typename T, int VEC>
-__device__ __forceinline__ void load_vec(const void* base, int64_t i, float (&out)[VEC]) {
-    const T* p = reinterpret_cast<const T*>(base) + i;
-    if constexpr (VEC == 1) {
-        out[0] = to_f32(p[0]);
-    } else {
-        const uint4 raw = __ldg(reinterpret_cast<const uint4*>(p));
-        const T* e = reinterpret_cast<const T*>(&raw);
-#pragma unroll
-        for (int q = 0; q < VEC; ++q) out[q] = to_f32(e[q]);
-    }
-}
-
-template <typename T, int VEC>
-__device__ __forceinline__ void store_vec(void* base, int64_t i, const float (&v)[VEC]) {
-    T* p = reinterpret_cast<T*>(base) + i;
-    if constexpr (VEC == 1) {
-        p[0] = from_f32<T>(v[0]);
-    } else {
-        uint4 raw;
-        T* e = reinterpret_cast<T*>(&raw);
-#pragma unroll
-        for (int q = 0; q < VEC; ++q) e[q] = from_f32<T>(v[q]);
-        *reinterpret_cast<uint4*>(p) = raw;
-    }
-}
 
 template <typename T, int VEC, int MODE>
 __global__ void __launch_bounds__(kCombBlock) combine_kernel(Parts parts, const void* __restrict__ h,
@@ -62,32 +21,8 @@ __global__ void __launch_bounds__(kCombBlock) combine_kernel(Parts parts, const 
                                                               int64_t n_vec, int64_t offset) {
     for (int64_t v = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; v < n_vec; v += (int64_t)gridDim.x * blockDim.x) {
         const int64_t i = offset + v * VEC;
-        float total[VEC], a[VEC];
-        load_vec<T, VEC>(parts.p[0], i, total);
-        if constexpr (MODE == kDiff) {
-            load_vec<T, VEC>(h, i, a);
-#pragma unroll
-            for (int q = 0; q < VEC; ++q) total[q] = total[q] - a[q];
-        } else if constexpr (MODE == kSum) {
-            for (int k = 1; k < parts.n; ++k) {
-                load_vec<T, VEC>(parts.p[k], i, a);
-#pragma unroll
-                for (int q = 0; q < VEC; ++q) total[q] += a[q];
-            }
-        } else {
-            float hv[VEC];
-            if (parts.n > 2) load_vec<T, VEC>(h, i, hv);
-            for (int k = 1; k < parts.n - 1; ++k) {
-                load_vec<T, VEC>(parts.p[k], i, a);
-#pragma unroll
-                for (int q = 0; q < VEC; ++q) total[q] += rnd<T>(a[q] - hv[q]);
-            }
-            float cv[VEC];
-            load_vec<T, VEC>(parts.p[parts.n - 1], i, a);
-            load_vec<T, VEC>(hc, i, cv);
-#pragma unroll
-            for (int q = 0; q < VEC; ++q) total[q] += rnd<T>(a[q] - cv[q]);
-        }
+        float total[VEC];
+        member_value<T, VEC, MODE>(parts, h, hc, i, total);
         store_vec<T, VEC>(out, i, total);
     }
 }
@@ -111,16 +46,6 @@ int launch_combine(const Parts& parts, const void* h, const void* hc, void* out,
                                                                                                   tail, n_vec * VEC);
     }
     return launch_status("p2p combine");
-}
-
-int fill_parts(Parts& p, const void* const* parts, int n) {
-    if (!parts || n < 1 || n > kMaxParts) return fail(P2P_EINVAL, "1 to %d parts", kMaxParts);
-    p.n = n;
-    for (int k = 0; k < n; ++k) {
-        if (!parts[k]) return fail(P2P_EINVAL, "part %d is null", k);
-        p.p[k] = parts[k];
-    }
-    return P2P_OK;
 }
 
 }  // namespace

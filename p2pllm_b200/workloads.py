@@ -123,3 +123,98 @@ def layer_seeds(seed: int, projections=LLAMA3_8B) -> dict:
     names = [p.name for p in projections]
     return {module: (seed * 1000 + gi, {n: seed * 1000 + 17 * (names.index(n) + 1) for n in proj})
             for gi, (module, (_, proj)) in enumerate(LAYER_MODULES.items())}
+
+
+# ---- config 5: a layer-parallel plan on a Qwen2.5-32B-shaped model ----------------------------------------------------
+
+CFG5_LAYERS = 64
+CFG5_GROUPS = [[2 * s, 2 * s + 1] for s in range(CFG5_LAYERS // 2)]     # 32 pair-steps, each with a keep-40 replica
+
+
+def rms_norm(h: torch.Tensor, eps: float = 1e-6) -> torch.Tensor:
+    """h / rms(h) per row, in fp32, back in h's dtype (unit norm weights)."""
+    hf = h.float()
+    return (hf * torch.rsqrt(hf.pow(2).mean(-1, keepdim=True) + eps)).to(h.dtype)
+
+
+class DecoderBlock:
+    """A Qwen2.5-32B-shaped decoder layer as a function of the hidden state h [T, hidden]: RMSNorm, q/k/v, causal
+    attention of the pass's own tokens (GQA: 40 query heads over 8 KV heads of 128; no KV cache of earlier tokens and no
+    rotary embedding -- this package has neither), o, residual; RMSNorm, SiLU(gate) * up, down, residual. Each of the
+    four linear modules (qkv, o, gate_up, down) is a callable x -> y: a dense bf16 weight (torch linear) for an exact
+    layer, a compact.Compact for a replica."""
+
+    def __init__(self, modules: dict, heads: int = 40, kv_heads: int = 8, head_dim: int = 128):
+        self.m = modules
+        self.heads, self.kv_heads, self.d = heads, kv_heads, head_dim
+
+    def __call__(self, h: torch.Tensor) -> torch.Tensor:
+        import torch.nn.functional as F
+        T = h.shape[0]
+        qkv = self.m["qkv"](rms_norm(h))
+        q, k, v = qkv.split([self.heads * self.d, self.kv_heads * self.d, self.kv_heads * self.d], dim=-1)
+        q = q.view(T, self.heads, self.d).transpose(0, 1).unsqueeze(0)
+        k = k.reshape(T, self.kv_heads, self.d).transpose(0, 1).unsqueeze(0)
+        v = v.reshape(T, self.kv_heads, self.d).transpose(0, 1).unsqueeze(0)
+        a = F.scaled_dot_product_attention(q, k, v, is_causal=True, enable_gqa=True)
+        h = h + self.m["o"](a.squeeze(0).transpose(0, 1).reshape(T, self.heads * self.d))
+        gu = self.m["gate_up"](rms_norm(h))
+        gate, up = gu.chunk(2, dim=-1)
+        return h + self.m["down"]((F.silu(gate.float()) * up.float()).to(h.dtype))
+
+
+CFG5_MODULES = {"qkv": ("q", "k", "v"), "o": ("o",), "gate_up": ("gate", "up"), "down": ("down",)}
+
+
+def cfg5_weights(layer: int, device, seed: int = 5, projections=QWEN25_32B) -> dict:
+    """{projection name: W [rows, cols] bf16 ~ N(0, 0.02)} of layer `layer` of the config-5 model, from its own seeds."""
+    return {p.name: projection_weights(p, seed * 100_000 + layer * 100 + i, device)
+            for i, p in enumerate(projections)}
+
+
+def cfg5_norms(layer: int, device, seed: int = 5, projections=QWEN25_32B) -> dict:
+    """{module: input-channel norms} that a layer's replica is selected with: a lognormal(0, 1) scale per channel
+    (the synthetic activations' spread), in place of calibration sums."""
+    by = {p.name: p for p in projections}
+    g = torch.Generator(device=device).manual_seed(seed * 100_000 + layer * 100 + 99)
+    return {m: channel_scale(by[names[0]].cols, g, device) for m, names in CFG5_MODULES.items()}
+
+
+def cfg5_exact(layer: int, device, seed: int = 5) -> DecoderBlock:
+    """Layer `layer` of the config-5 model with dense bf16 projections (fused qkv and gate_up weights)."""
+    import torch.nn.functional as F
+    w = cfg5_weights(layer, device, seed)
+    mods = {}
+    for m, names in CFG5_MODULES.items():
+        W = torch.cat([w.pop(n) for n in names]) if len(names) > 1 else w.pop(names[0])
+        mods[m] = (lambda W: lambda x: F.linear(x, W))(W)
+    return DecoderBlock(mods)
+
+
+def cfg5_replica(layer: int, device, seed: int = 5, layout: str | None = None) -> tuple:
+    """(the keep-40 replica of layer `layer` as a DecoderBlock over compact.Compact modules, its weight bytes): every
+    projection pruned by the Wanda selection on the GPU, the dense weights dropped."""
+    from . import compact, wanda
+    norms = cfg5_norms(layer, device, seed)
+    keep = {p.name: p.keep for p in QWEN25_32B}
+    mods, nbytes = {}, 0
+    w = cfg5_weights(layer, device, seed)
+    for m, names in CFG5_MODULES.items():
+        blocks = []
+        for n in names:
+            values, idx = wanda.select(w.pop(n), keep[n], norms[m])
+            blocks.append(("compact", values, idx, QWEN25_32B_COLS[n]))
+        c = compact.Compact.__new__(compact.Compact)
+        c.tiles = compact.Tiles(blocks, layout=layout)
+        nbytes += c.nbytes()
+        mods[m] = (lambda c: lambda x: c.apply(None, x))(c)
+    return DecoderBlock(mods), nbytes
+
+
+QWEN25_32B_COLS = {p.name: p.cols for p in QWEN25_32B}
+
+
+def cfg5_input(pass_index: int, tokens: int, device, seed: int = 5, hidden: int = 5120) -> torch.Tensor:
+    """The hidden state entering the first step on pass `pass_index`: N(0, 1) rows, RMS-normalised, bf16."""
+    g = torch.Generator(device=device).manual_seed(seed * 7919 + pass_index)
+    return rms_norm(torch.randn(tokens, hidden, generator=g, device=device)).bfloat16()
