@@ -144,10 +144,15 @@ typedef struct {
 
 /* y [tokens, ldy] (columns row0.. of each block) = x [tokens, cols] (row stride ldx) times the blocks' rows, fp32
  * sums, on CUDA cores straight from the row layout (values + column indices). Any token count. bf16, f16 or f32;
- * idx_bytes 2 or 4. cols * element size <= 200 KiB.
+ * idx_bytes 2 or 4. cols * element size <= 200 KiB. Up to 32 tokens whose x fits 200 KiB (rows 16-byte aligned),
+ * one block an SM stages all of x by bulk copies; otherwise blocks stage token tiles column-major.
  * Replaces p2p/compact.cu:265-278 (spmm) for row-layout weights; p2p/compact.py:192-199 (Tiles.__call__). */
 int p2p_spmm_rows(const void* x, int dtype, int64_t tokens, int64_t cols, int64_t ldx, const p2p_row_block* blocks,
                   int nblocks, int idx_bytes, void* y, int64_t ldy, void* stream);
+
+/* P2P_OK unless a p2p_spmm_rows launch of at most 32 tokens (x staged whole by bulk copies) gave up waiting for its
+ * copies since the last reset (P2P_ECUDA); reset != 0 clears it. Syncs the stream. No counterpart in the reference. */
+int p2p_spmm_rows_status(int reset, void* stream);
 
 /* The tensor-core layout of a module (bf16 / f16 weights): rows in tiles of 128, columns in tiles of 64; each
  * (row tile, column tile) segment holds its kept weights as 32-bit words (value bits << 16 | row << 6 | column, bit 13
@@ -233,6 +238,20 @@ int p2p_spmm_tc_grouped(const void* x, int dtype, int64_t x_rows, int64_t cols, 
                         const int64_t* seg, int64_t layout_row_tiles, int64_t rows, int64_t item_row_tiles,
                         int64_t seg_cap_words, const int32_t* items, int64_t n_items, int64_t max_tokens, void* y,
                         int64_t ldy, void* stream);
+
+/* The gated forms: a gate + up module whose rows are interleaved 64 and 64 (row tile k: gate rows 64k..64k+63, then
+ * up rows 64k..64k+63; rows = 2R, R a multiple of 64), and y [tokens, ldy >= R] = dtype(silu(g) * u), g and u the two
+ * projections' outputs rounded to dtype, computed in the GEMM's epilogue (the accumulators of a row tile meet in
+ * shared memory, in the cluster's, or in the workspace's partials first). Otherwise as p2p_spmm_tc /
+ * p2p_spmm_tc_grouped (the workspace as p2p_spmm_tc_workspace(rows, cols, tokens) gives). Replaces
+ * p2p/compact.py:205-224's gate_up projection followed by the model's SiluAndMul (two kernels and [T, 2R] in HBM). */
+int p2p_spmm_tc_gated(const void* x, int dtype, int64_t tokens, int64_t cols, int64_t ldx, const uint32_t* words,
+                      const int64_t* seg, int64_t rows, int64_t seg_cap_words, void* y, int64_t ldy, void* workspace,
+                      size_t workspace_bytes, void* stream);
+int p2p_spmm_tc_grouped_gated(const void* x, int dtype, int64_t x_rows, int64_t cols, int64_t ldx,
+                              const uint32_t* words, const int64_t* seg, int64_t layout_row_tiles, int64_t rows,
+                              int64_t item_row_tiles, int64_t seg_cap_words, const int32_t* items, int64_t n_items,
+                              int64_t max_tokens, void* y, int64_t ldy, void* stream);
 
 /* The routing of a routed-experts pass, on the GPU: ids [n_pairs] int64 (a token's slots consecutive; < 0: no expert).
  * order [n_pairs]: the routed pairs sorted by expert, and within an expert by pair index (stable); where [n_pairs]:

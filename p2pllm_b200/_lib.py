@@ -41,6 +41,7 @@ SIGNATURES = {
     "p2p_unpack": ([_vp, _int, _i64, _i64, _i64, _vp, _i64, _vp, _int, _i64, _i64, _vp, _i64, _vp], _int),
     "p2p_check_idx": ([_vp, _int, _i64, _i64, _i64, _i64, _vp], _int),
     "p2p_spmm_rows": ([_vp, _int, _i64, _i64, _i64, ctypes.POINTER(RowBlock), _int, _int, _vp, _i64, _vp], _int),
+    "p2p_spmm_rows_status": ([_int, _vp], _int),
     "p2p_tiles_workspace": ([ctypes.POINTER(RowBlock), _int, _i64], _sz),
     "p2p_tiles_plan": ([ctypes.POINTER(RowBlock), _int, _int, _i64, _vp, ctypes.POINTER(_i64), _vp, _sz, _vp], _int),
     "p2p_tiles_fill": ([ctypes.POINTER(RowBlock), _int, _int, _i64, _int, _vp, _vp, _i64, _vp, _sz, _vp], _int),
@@ -66,6 +67,9 @@ SIGNATURES = {
     "p2p_spmm_tc_grouped": ([_vp, _int, _i64, _i64, _i64, _vp, _vp, _i64, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _i64,
                              _vp], _int),
     "p2p_spmm_tc_status": ([_int, _vp], _int),
+    "p2p_spmm_tc_gated": ([_vp, _int, _i64, _i64, _i64, _vp, _vp, _i64, _i64, _vp, _i64, _vp, _sz, _vp], _int),
+    "p2p_spmm_tc_grouped_gated": ([_vp, _int, _i64, _i64, _i64, _vp, _vp, _i64, _i64, _i64, _i64, _vp, _i64, _i64,
+                                   _vp, _i64, _vp], _int),
     "p2p_spmm_tc_withhold": ([_vp, _int, _i64, _i64, _i64, _vp, _vp, _i64, _i64, _vp, _i64, _vp, _sz, _i64, _i64,
                               _vp], _int),
     "p2p_moe_route": ([_vp, _i64, _int, _vp, _vp, _vp, _vp, _i64, _vp, _vp], _int),

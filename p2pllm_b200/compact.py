@@ -21,7 +21,7 @@ import torch
 from . import kernels
 from ._lib import P2PError, idx_dtype
 
-__all__ = ["pack", "unpack", "expand", "to_compact", "Tiles", "Compact", "CompactMoE"]
+__all__ = ["pack", "unpack", "expand", "to_compact", "Tiles", "GatedTiles", "Compact", "CompactMoE"]
 
 # The layout bf16 / f16 modules take unless asked otherwise: "tc" (values + positions, 4 bytes a kept weight, one
 # 16-bit store a weight into a shared-memory tile) or "mask" (values + one bit a weight, the reference's storage,
@@ -147,6 +147,52 @@ class Tiles:
         if self.layout == "tc":
             return self.words.numel() * 4 + self.seg.numel() * 8
         return sum(t.numel() * t.element_size() for _, v, i in self.blocks for t in (v, i) if t is not None)
+
+
+def interleave_gate_up(t: torch.Tensor) -> torch.Tensor:
+    """Rows [.., 2R, k] of a gated MLP's input projection (gate rows, then up rows) reordered so that every 128 rows
+    hold 64 gate rows and the same 64 units' up rows: the layout of the gated GEMM."""
+    r2, k = t.shape[-2], t.shape[-1]
+    lead = t.shape[:-2]
+    return t.reshape(*lead, 2, r2 // 128, 64, k).transpose(-4, -3).reshape(*lead, r2, k)
+
+
+def gate_up_rows(blocks: list) -> tuple:
+    """(values [.., 2R, k], idx [.., 2R, k] or None for dense rows) of a gate + up module's row blocks, in row order
+    (all compact with one k, or all dense), interleaved for the gated GEMM. Raises if the blocks do not fit it."""
+    blocks = [to_compact(b) for b in blocks]
+    kinds = {b[0] for b in blocks}
+    if len(kinds) != 1 or len({b[1].shape[-1] for b in blocks}) != 1:
+        raise P2PError("a gated module's blocks are all compact with one k, or all dense")
+    values = torch.cat([b[1] for b in blocks], dim=-2)
+    idx = torch.cat([b[2] for b in blocks], dim=-2) if blocks[0][0] == "compact" else None
+    if values.shape[-2] % 128 or values.dtype not in (torch.bfloat16, torch.float16) or _cols(blocks[0]) % 8:
+        raise P2PError("a gated module needs bf16 / f16 rows, 2R with R a multiple of 64, columns in multiples of 8")
+    return interleave_gate_up(values).contiguous(), None if idx is None else interleave_gate_up(idx).contiguous()
+
+
+class GatedTiles:
+    """A gated MLP's gate and up projections as one tensor-core module whose GEMM also applies the gate: calling it on
+    x [T, cols] returns dtype(silu(g) * u) [T, R], g and u being the projections' outputs rounded to the model dtype
+    -- what SGLang's SiluAndMul makes of the gate_up projection's output, without writing it (p2p/compact.py:205-224
+    multiplies the two projections; the activation is the model's own). Blocks: the gate rows, then the up rows."""
+
+    def __init__(self, blocks: list):
+        values, idx = gate_up_rows(blocks)
+        self.cols = _cols(to_compact(blocks[0]))
+        self.dtype, self.device = values.dtype, values.device
+        self.layout_rows = values.shape[-2]
+        self.rows = self.layout_rows // 2
+        self.layout = "tc"
+        self.words, self.seg, self.seg_cap = kernels.tiles_build([(0, values, idx)], self.cols)
+
+    def __call__(self, x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+        if x.dtype != self.dtype:
+            raise P2PError(f"x is {x.dtype}, the weights {self.dtype}")
+        return kernels.spmm_tc_gated(x, self.words, self.seg, self.layout_rows, self.cols, self.seg_cap, out=out)
+
+    def nbytes(self) -> int:
+        return self.words.numel() * 4 + self.seg.numel() * 8
 
 
 class Compact:

@@ -10,7 +10,14 @@
 // element below and mask the strays), gather the columns and accumulate TT sums in fp32, then combine the lanes with
 // shuffles. Blocks of the same rows but different token tiles are adjacent in launch order, so a row's weights come
 // from HBM once and from L2 for the other tiles.
-#include "common.cuh"
+//
+// Few tokens (a draft pass of 16 + 1): one block per SM stages ALL of x at once, row-major, with one bulk copy
+// (cp.async.bulk, the TMA engine's untiled form) per token row completing on an mbarrier, while its warps prefetch
+// their first rows' weights into L2; then every warp of the grid takes whole rows in turn. x is read from L2 once per
+// SM instead of once per (token tile, row group) block, and each block does a share of the rows large enough to hide
+// the staging. The wait for the copies is bounded (2 s): past it the block records the failure
+// (p2p_spmm_rows_status) and returns without computing.
+#include "sm100.cuh"
 
 namespace p2p {
 namespace {
@@ -179,6 +186,136 @@ __global__ void __launch_bounds__(kRowsBlock) spmm_rows_kernel(const T* __restri
     }
 }
 
+constexpr int kStagedBlock = 512;
+constexpr int kStagedWarps = kStagedBlock / 32;
+constexpr int kStagedMaxTokens = 32;
+constexpr int kStagedSmem = 200 * 1024;
+constexpr uint64_t kStagedWaitNs = 2000000000ull;
+
+__device__ int g_rows_error;   // 1 once a staged block's wait for its copies of x gave up (since the last reset)
+
+// y rows of the grid's warps, x [tokens <= TT, cols] staged row-major in shared memory (xs[t * cols + c]).
+template <typename T, typename I, int TT>
+__global__ void __launch_bounds__(kStagedBlock, 1) spmm_rows_staged_kernel(const T* __restrict__ x, int tokens,
+                                                                           int cols, int64_t ldx, BlockTable bt,
+                                                                           int64_t total_rows, T* __restrict__ y,
+                                                                           int64_t ldy) {
+    constexpr int VEC = 16 / sizeof(T);
+    extern __shared__ __align__(128) unsigned char smem_raw[];
+    __shared__ __align__(8) uint64_t bar;
+    __shared__ int go;
+    const T* xs = reinterpret_cast<const T*>(smem_raw);
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const uint32_t b = sm100::smem_u32(&bar);
+    if (tid == 0) {
+        sm100::mbar_init(b, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        const uint32_t row_bytes = (uint32_t)cols * sizeof(T);
+        sm100::mbar_expect_tx(b, row_bytes * (uint32_t)tokens);
+        const uint32_t dst = sm100::smem_u32(smem_raw);
+        for (int t = 0; t < tokens; ++t) sm100::bulk_load(dst + t * row_bytes, x + t * ldx, row_bytes, b);
+    }
+    // while x lands: the first row of this warp, into L2 (a 128-byte line a lane)
+    const int64_t gw = (int64_t)blockIdx.x * kStagedWarps + warp;
+    const int64_t stride = (int64_t)gridDim.x * kStagedWarps;
+    if (gw < total_rows) {
+        int bi = 0;
+        while (bi + 1 < bt.n && gw >= bt.start[bi + 1]) ++bi;
+        const p2p_row_block& blk = bt.b[bi];
+        const int64_t base = (gw - bt.start[bi]) * blk.ld;
+        const char* v = reinterpret_cast<const char*>(blk.vals) + base * sizeof(T);
+        for (int64_t off = (int64_t)lane * 128; off < blk.k * (int64_t)sizeof(T); off += 32 * 128)
+            asm volatile("prefetch.global.L2 [%0];" ::"l"(v + off));
+        if (blk.idx) {
+            const char* ix = reinterpret_cast<const char*>(blk.idx) + base * sizeof(I);
+            for (int64_t off = (int64_t)lane * 128; off < blk.k * (int64_t)sizeof(I); off += 32 * 128)
+                asm volatile("prefetch.global.L2 [%0];" ::"l"(ix + off));
+        }
+    }
+    if (tid == 0) {
+        bool ok = sm100::mbar_try(b, 0);
+        const uint64_t t0 = sm100::now_ns();
+        while (!ok && sm100::now_ns() - t0 < kStagedWaitNs) ok = sm100::mbar_try(b, 0);
+        if (!ok) atomicExch(&g_rows_error, 1);
+        go = ok;
+    }
+    __syncthreads();
+    if (!go) return;
+
+    const unsigned cmax = (unsigned)(cols - 1);
+    for (int64_t r = gw; r < total_rows; r += stride) {
+        int bi = 0;
+        while (bi + 1 < bt.n && r >= bt.start[bi + 1]) ++bi;
+        const p2p_row_block& blk = bt.b[bi];
+        const int64_t lr = r - bt.start[bi];
+        const T* v = reinterpret_cast<const T*>(blk.vals);
+        const I* ix = reinterpret_cast<const I*>(blk.idx);
+        const int64_t base = lr * blk.ld, end = base + blk.k;
+        float acc[TT];
+#pragma unroll
+        for (int t = 0; t < TT; ++t) acc[t] = 0.f;
+        for (int64_t e = (base & ~(int64_t)(VEC - 1)) + lane * VEC; e < end; e += 32 * VEC) {
+            float fv[VEC];
+            int ci[VEC];
+            load_step<T, I, VEC>(v, ix, e, fv, ci);
+            if (ix == nullptr) {
+#pragma unroll
+                for (int i = 0; i < VEC; ++i) ci[i] += (int)(e - base);
+            }
+            const bool whole = e >= base && e + VEC <= end;
+#pragma unroll
+            for (int i = 0; i < VEC; ++i) {
+                if (!whole && (e + i < base || e + i >= end)) continue;
+                const T* col = xs + min((unsigned)ci[i], cmax);
+#pragma unroll
+                for (int t = 0; t < TT; ++t)
+                    if (t < tokens) acc[t] = fmaf(fv[i], to_f32(col[(size_t)t * cols]), acc[t]);
+            }
+        }
+#pragma unroll
+        for (int t = 0; t < TT; ++t) {
+#pragma unroll
+            for (int d = 16; d > 0; d >>= 1) acc[t] += __shfl_xor_sync(0xffffffffu, acc[t], d);
+        }
+        float mine = 0.f;
+#pragma unroll
+        for (int t = 0; t < TT; ++t)
+            if (lane == t) mine = acc[t];
+        if (lane < tokens) y[(int64_t)lane * ldy + blk.row0 + lr] = from_f32<T>(mine);
+    }
+}
+
+// The staged kernel takes the launch when all tokens fit one block's shared memory and x's rows are 16-byte aligned.
+template <typename T>
+bool staged_fits(const void* x, int64_t tokens, int64_t cols, int64_t ldx) {
+    return tokens >= 1 && tokens <= kStagedMaxTokens && tokens * cols * (int64_t)sizeof(T) <= kStagedSmem &&
+           (cols * (int64_t)sizeof(T)) % 16 == 0 && (ldx * (int64_t)sizeof(T)) % 16 == 0 && aligned16(x);
+}
+
+template <typename T, typename I, int TT>
+int launch_staged(const void* x, int64_t tokens, int64_t cols, int64_t ldx, const BlockTable& bt, int64_t total_rows,
+                  void* y, int64_t ldy, cudaStream_t s) {
+    auto kern = spmm_rows_staged_kernel<T, I, TT>;
+    const int smem = (int)(tokens * cols * sizeof(T));
+    if (int e = allow_smem((const void*)kern, kStagedSmem, "p2p_spmm_rows")) return e;
+    const int64_t want = (total_rows + kStagedWarps - 1) / kStagedWarps;
+    const int grid = (int)(want < sm_count() ? want : sm_count());
+    kern<<<grid, kStagedBlock, smem, s>>>(reinterpret_cast<const T*>(x), (int)tokens, (int)cols, ldx, bt, total_rows,
+                                          reinterpret_cast<T*>(y), ldy);
+    return launch_status("p2p_spmm_rows");
+}
+
+template <typename T, typename I>
+int dispatch_staged(const void* x, int64_t tokens, int64_t cols, int64_t ldx, const BlockTable& bt, int64_t total_rows,
+                    void* y, int64_t ldy, cudaStream_t s) {
+    if (tokens <= 4) return launch_staged<T, I, 4>(x, tokens, cols, ldx, bt, total_rows, y, ldy, s);
+    if (tokens <= 8) return launch_staged<T, I, 8>(x, tokens, cols, ldx, bt, total_rows, y, ldy, s);
+    if (tokens <= 16) return launch_staged<T, I, 16>(x, tokens, cols, ldx, bt, total_rows, y, ldy, s);
+    if (tokens <= 20) return launch_staged<T, I, 20>(x, tokens, cols, ldx, bt, total_rows, y, ldy, s);
+    return launch_staged<T, I, 32>(x, tokens, cols, ldx, bt, total_rows, y, ldy, s);
+}
+
 template <typename T, typename I, int TT>
 int launch_rows(const void* x, int64_t tokens, int64_t cols, int64_t ldx, const BlockTable& bt, int64_t total_rows,
                 void* y, int64_t ldy, cudaStream_t s) {
@@ -263,8 +400,27 @@ extern "C" int p2p_spmm_rows(const void* x, int dtype, int64_t tokens, int64_t c
                 (long long)ldy);
     cudaStream_t s = as_stream(stream);
     P2P_DISPATCH(dtype, {
+        if (staged_fits<scalar_t>(x, tokens, cols, ldx)) {
+            if (idx_bytes == 2) return dispatch_staged<scalar_t, int16_t>(x, tokens, cols, ldx, bt, total, y, ldy, s);
+            return dispatch_staged<scalar_t, int32_t>(x, tokens, cols, ldx, bt, total, y, ldy, s);
+        }
         if (idx_bytes == 2) return dispatch_tt<scalar_t, int16_t>(x, tokens, cols, ldx, bt, total, y, ldy, s);
         return dispatch_tt<scalar_t, int32_t>(x, tokens, cols, ldx, bt, total, y, ldy, s);
     });
+    return P2P_OK;
+}
+
+extern "C" int p2p_spmm_rows_status(int reset, void* stream) {
+    cudaStream_t st = as_stream(stream);
+    int v = 0;
+    if (cudaMemcpyFromSymbolAsync(&v, g_rows_error, sizeof(int), 0, cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+        cudaStreamSynchronize(st) != cudaSuccess)
+        return fail(P2P_ECUDA, "p2p_spmm_rows_status: %s", cudaGetErrorString(cudaGetLastError()));
+    if (reset && v) {
+        const int zero = 0;
+        cudaMemcpyToSymbolAsync(g_rows_error, &zero, sizeof(int), 0, cudaMemcpyHostToDevice, st);
+        cudaStreamSynchronize(st);
+    }
+    if (v) return fail(P2P_ECUDA, "p2p_spmm_rows: a block's wait for its staged x gave up");
     return P2P_OK;
 }

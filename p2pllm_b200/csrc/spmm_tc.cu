@@ -94,7 +94,25 @@ struct TcParams {
     uint64_t wait_ns;                 // how long a pipeline wait may take before the launch gives up
     unsigned seq;                     // this launch's sequence number (nonzero), naming it in g_tc_failed_seq
     int hold_tile;                    // a test's withheld x tile (each CTA's tile of that index is never loaded), or -1
+    // Gated (SiLU-and-multiply) output: the module's rows are interleaved gate / up, 64 of each a row tile (tile k:
+    // gate rows 64k..64k+63, then the up rows of the same units), and y [tokens, rows / 2] takes
+    // dtype(silu(gate) * up) of the two rounded outputs, column 64k + j. The accumulators meet in shared memory (or
+    // the cluster's, or the partials) before the product; y never leaves through TMA.
+    int gated;
 };
+
+// y[t, c] of a gated launch from one unit of 4 gate sums g and the 4 up sums u of the same units (fp32): each output
+// rounded as the unfused path rounds it -- the projection's outputs to the model dtype, then SiLU(gate) * up in fp32.
+template <typename T>
+__device__ __forceinline__ void store_gated(T* yt, int64_t c0, int64_t limit, float4 g, float4 u) {
+    const float gv[4] = {g.x, g.y, g.z, g.w}, uv[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+        if (c0 + c >= limit) break;
+        const float gr = to_f32(from_f32<T>(gv[c])), ur = to_f32(from_f32<T>(uv[c]));
+        yt[c0 + c] = from_f32<T>(gr / (1.0f + expf(-gr)) * ur);
+    }
+}
 
 // A warp's share of one segment's words: the entries of its 16 rows (8-row groups 2 wg and 2 wg + 1), [lo, hi) in
 // words from the CTA's first segment, from the segment's header (cumulative counts of its 8-row groups).
@@ -406,7 +424,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             for (int j = 0; j < 16; ++j) {
                 const int t = c * 16 + j;
                 if (t < tokens) {
-                    if (p.y_tma) {
+                    if (p.gated && p.n_split == 1) {
+                        reinterpret_cast<float*>(gbase)[t * tc::kTileRows + row_local] = v[j];   // rings are free
+                    } else if (p.y_tma) {
                         reinterpret_cast<T*>(gbase)[t * tc::kTileRows + row_local] = from_f32<T>(v[j]);  // rings free
                     } else if (p.n_split == 1) {
                         if (row_ok) reinterpret_cast<T*>(p.y)[(xrow0 + t) * p.ldy + row] = from_f32<T>(v[j]);
@@ -426,6 +446,20 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     if (warp == kProducerWarp) {
         tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(p.tmem_cols) : "memory");
+    }
+    if (p.gated && p.n_split == 1) {
+        // The tile's accumulators are in shared memory ([token][128 rows], fp32): gate unit r and up unit r sit 64
+        // rows apart; every thread takes (token, 4 units) pieces.
+        const float* acc = reinterpret_cast<const float*>(gbase);
+        T* y = reinterpret_cast<T*>(p.y);
+        const int64_t c_base = (col0 >> 1), limit = p.rows >> 1;
+        for (int u = threadIdx.x; u < tokens * 16; u += kTcThreads) {
+            const int t = u >> 4, r4 = (u & 15) * 4;
+            const float4 g = *reinterpret_cast<const float4*>(acc + t * tc::kTileRows + r4);
+            const float4 up = *reinterpret_cast<const float4*>(acc + t * tc::kTileRows + 64 + r4);
+            store_gated<T>(y + (xrow0 + t) * p.ldy, c_base + r4, limit, g, up);
+        }
+        return;
     }
     if (p.y_tma) {
         // The tile of y staged as [token][128 rows] in shared memory goes out in one TMA store a box (rows past the
@@ -447,9 +481,28 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         // alive until every CTA of the cluster has read it.
         cluster_sync_all();
         const int ns = p.n_split;
+        const uint32_t part = smem_u32(gbase);
+        if (p.gated) {
+            // units of 4 gate rows, each with the 4 up rows 64 below
+            const int64_t n4 = (int64_t)tokens * 16;
+            const int64_t u_begin = n4 * split / ns, u_end = n4 * (split + 1) / ns;
+            for (int64_t u = u_begin + threadIdx.x; u < u_end; u += kTcThreads) {
+                const int t = (int)(u / 16), r4 = (int)(u % 16) * 4;
+                const uint32_t off = part + (uint32_t)(t * tc::kTileRows + r4) * 4u;
+                float4 g = make_float4(0.f, 0.f, 0.f, 0.f), up = g;
+                for (int sp = 0; sp < ns; ++sp) {
+                    const float4 a = ld_cluster_f4(cluster_addr(off, sp));
+                    const float4 b = ld_cluster_f4(cluster_addr(off + 256u, sp));
+                    g.x += a.x; g.y += a.y; g.z += a.z; g.w += a.w;
+                    up.x += b.x; up.y += b.y; up.z += b.z; up.w += b.w;
+                }
+                store_gated<T>(reinterpret_cast<T*>(p.y) + (xrow0 + t) * p.ldy, (col0 >> 1) + r4, p.rows >> 1, g, up);
+            }
+            cluster_sync_all();
+            return;
+        }
         const int64_t n4 = (int64_t)tokens * (tc::kTileRows / 4);
         const int64_t u_begin = n4 * split / ns, u_end = n4 * (split + 1) / ns;
-        const uint32_t part = smem_u32(gbase);
         for (int64_t u = u_begin + threadIdx.x; u < u_end; u += kTcThreads) {
             const int t = (int)(u / 32), r4 = (int)(u % 32) * 4;
             const uint32_t off = part + (uint32_t)(t * tc::kTileRows + r4) * 4u;
@@ -481,6 +534,25 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     __syncthreads();
     if (!s_last) return;
     __threadfence();
+    if (p.gated) {
+        // units of 4 gate rows with their 4 up rows, the splits added in order
+        const int64_t n4 = (int64_t)p.tokens * 16;
+        const int64_t col = (int64_t)rt * tc::kTileRows;
+        const int64_t split_stride = (int64_t)p.tokens * p.rows_pad;
+        for (int64_t u = threadIdx.x; u < n4; u += kTcThreads) {
+            const int64_t t = u / 16, off = t * p.rows_pad + col + (u % 16) * 4;
+            float4 g = make_float4(0.f, 0.f, 0.f, 0.f), up = g;
+            for (int sp = 0; sp < p.n_split; ++sp) {
+                const float4 a = __ldcg(reinterpret_cast<const float4*>(p.partial + sp * split_stride + off));
+                const float4 b = __ldcg(reinterpret_cast<const float4*>(p.partial + sp * split_stride + off + 64));
+                g.x += a.x; g.y += a.y; g.z += a.z; g.w += a.w;
+                up.x += b.x; up.y += b.y; up.z += b.z; up.w += b.w;
+            }
+            store_gated<T>(reinterpret_cast<T*>(p.y) + t * p.ldy, (col >> 1) + (u % 16) * 4, p.rows >> 1, g, up);
+        }
+        if (threadIdx.x == 0) p.tickets[rt] = 0u;
+        return;
+    }
     // Four rows a unit (16-byte loads), kUnits units a thread at a time, every split's loads of a pair of splits in
     // flight together; the sums still run split by split, so the result does not depend on who added them.
     constexpr int kUnits = 8;
@@ -710,8 +782,10 @@ namespace {
 // p2p_spmm_tc, with the wait limit and withheld tile of p2p_spmm_tc_withhold (hold_tile < 0: none).
 int spmm_tc_impl(const void* x, int dtype, int64_t tokens, int64_t cols, int64_t ldx, const uint32_t* words,
                  const int64_t* seg, int64_t rows, int64_t seg_cap_words, void* y, int64_t ldy, void* workspace,
-                 size_t workspace_bytes, void* stream, int hold_tile, uint64_t wait_ns) {
+                 size_t workspace_bytes, void* stream, int hold_tile, uint64_t wait_ns, int gated) {
     P2P_REQUIRE(tokens >= 0 && rows >= 0 && cols >= 1, "p2p_spmm_tc: bad shape");
+    P2P_REQUIRE(!gated || rows % tc::kTileRows == 0, "p2p_spmm_tc_gated: %lld interleaved rows, not whole row tiles",
+                (long long)rows);
     if (tokens == 0 || rows == 0) return P2P_OK;
     if (dtype != P2P_BF16 && dtype != P2P_F16)
         return fail(P2P_EUNSUPPORTED, "p2p_spmm_tc: bf16 or f16 (fp32 weights take p2p_spmm_rows)");
@@ -719,7 +793,7 @@ int spmm_tc_impl(const void* x, int dtype, int64_t tokens, int64_t cols, int64_t
     P2P_REQUIRE(aligned16(words), "p2p_spmm_tc: words must start on a 16-byte boundary");
     P2P_REQUIRE(cols % 8 == 0 && ldx % 8 == 0 && ldx >= cols && aligned16(x),
                 "p2p_spmm_tc: x needs 16-byte aligned rows (cols and ldx multiples of 8)");
-    P2P_REQUIRE(ldy >= rows, "p2p_spmm_tc: ldy %lld below rows %lld", (long long)ldy, (long long)rows);
+    P2P_REQUIRE(ldy >= (gated ? rows / 2 : rows), "p2p_spmm_tc: ldy %lld below y's width", (long long)ldy);
     P2P_REQUIRE(seg_cap_words >= 0 && seg_cap_words % 4 == 0 &&
                     seg_cap_words <= tc::kHeaderWords + tc::kTileRows * tc::kTileCols + 4,
                 "p2p_spmm_tc: segment capacity %lld words", (long long)seg_cap_words);
@@ -773,12 +847,16 @@ int spmm_tc_impl(const void* x, int dtype, int64_t tokens, int64_t cols, int64_t
         prm.wait_ns = wait_ns;
         prm.seq = next_seq();
         prm.hold_tile = hold_tile;
+        prm.gated = gated;
+        if (gated && pl.n_split == 1 &&
+            (int64_t)pl.n_total * tc::kTileRows * 4 > (int64_t)pl.a_slots * kASlotBytes + (int64_t)pl.x_slots * pl.b_bytes)
+            return fail(P2P_EUNSUPPORTED, "p2p_spmm_tc_gated: %d tokens do not fit the staged tile", tn);
         CUtensorMap map, ymap;
         const void* xt = reinterpret_cast<const char*>(x) + t0 * ldx * elem;
         if (int e = encode_x_map(&map, xt, dtype, tn, cols, ldx, pl.box_rows)) return e;
         // y through TMA stores when unsplit and aligned (rows of y start on 16 bytes); the staged tile is
         // n_total x 128 x 2 bytes of the rings
-        prm.y_tma = pl.n_split == 1 && ldy % 8 == 0 && aligned16(prm.y) &&
+        prm.y_tma = !gated && pl.n_split == 1 && ldy % 8 == 0 && aligned16(prm.y) &&
                     (int64_t)pl.n_total * tc::kTileRows * 2 <= (int64_t)pl.a_slots * kASlotBytes;
         ymap = map;
         if (prm.y_tma && encode_y_map(&ymap, prm.y, dtype, tn, rows, ldy, pl.box_rows) != P2P_OK) prm.y_tma = 0;
@@ -795,7 +873,14 @@ extern "C" int p2p_spmm_tc(const void* x, int dtype, int64_t tokens, int64_t col
                            const int64_t* seg, int64_t rows, int64_t seg_cap_words, void* y, int64_t ldy,
                            void* workspace, size_t workspace_bytes, void* stream) {
     return spmm_tc_impl(x, dtype, tokens, cols, ldx, words, seg, rows, seg_cap_words, y, ldy, workspace,
-                        workspace_bytes, stream, -1, kWaitNs);
+                        workspace_bytes, stream, -1, kWaitNs, 0);
+}
+
+extern "C" int p2p_spmm_tc_gated(const void* x, int dtype, int64_t tokens, int64_t cols, int64_t ldx,
+                                 const uint32_t* words, const int64_t* seg, int64_t rows, int64_t seg_cap_words,
+                                 void* y, int64_t ldy, void* workspace, size_t workspace_bytes, void* stream) {
+    return spmm_tc_impl(x, dtype, tokens, cols, ldx, words, seg, rows, seg_cap_words, y, ldy, workspace,
+                        workspace_bytes, stream, -1, kWaitNs, 1);
 }
 
 extern "C" int p2p_spmm_tc_withhold(const void* x, int dtype, int64_t tokens, int64_t cols, int64_t ldx,
@@ -807,13 +892,14 @@ extern "C" int p2p_spmm_tc_withhold(const void* x, int dtype, int64_t tokens, in
                 (long long)wait_us);
     P2P_REQUIRE(tokens <= 512, "p2p_spmm_tc_withhold: one launch (at most 512 tokens)");
     return spmm_tc_impl(x, dtype, tokens, cols, ldx, words, seg, rows, seg_cap_words, y, ldy, workspace,
-                        workspace_bytes, stream, (int)hold_tile, (uint64_t)wait_us * 1000ull);
+                        workspace_bytes, stream, (int)hold_tile, (uint64_t)wait_us * 1000ull, 0);
 }
 
-extern "C" int p2p_spmm_tc_grouped(const void* x, int dtype, int64_t x_rows, int64_t cols, int64_t ldx,
-                                   const uint32_t* words, const int64_t* seg, int64_t layout_row_tiles,
-                                   int64_t rows, int64_t item_row_tiles, int64_t seg_cap_words, const int32_t* items,
-                                   int64_t n_items, int64_t max_tokens, void* y, int64_t ldy, void* stream) {
+namespace {
+int grouped_impl(const void* x, int dtype, int64_t x_rows, int64_t cols, int64_t ldx, const uint32_t* words,
+                 const int64_t* seg, int64_t layout_row_tiles, int64_t rows, int64_t item_row_tiles,
+                 int64_t seg_cap_words, const int32_t* items, int64_t n_items, int64_t max_tokens, void* y,
+                 int64_t ldy, void* stream, int gated) {
     P2P_REQUIRE(x_rows >= 0 && rows >= 1 && cols >= 1 && n_items >= 0, "p2p_spmm_tc_grouped: bad shape");
     if (n_items == 0 || x_rows == 0) return P2P_OK;
     if (dtype != P2P_BF16 && dtype != P2P_F16) return fail(P2P_EUNSUPPORTED, "p2p_spmm_tc_grouped: bf16 or f16");
@@ -821,7 +907,9 @@ extern "C" int p2p_spmm_tc_grouped(const void* x, int dtype, int64_t x_rows, int
     P2P_REQUIRE(aligned16(words) && aligned16(items), "p2p_spmm_tc_grouped: words and items need 16-byte alignment");
     P2P_REQUIRE(cols % 8 == 0 && ldx % 8 == 0 && ldx >= cols && aligned16(x),
                 "p2p_spmm_tc_grouped: x needs 16-byte aligned rows (cols and ldx multiples of 8)");
-    P2P_REQUIRE(ldy >= rows, "p2p_spmm_tc_grouped: ldy %lld below rows %lld", (long long)ldy, (long long)rows);
+    P2P_REQUIRE(ldy >= (gated ? rows / 2 : rows), "p2p_spmm_tc_grouped: ldy %lld below y's width", (long long)ldy);
+    P2P_REQUIRE(!gated || rows % tc::kTileRows == 0,
+                "p2p_spmm_tc_grouped_gated: %lld interleaved rows an expert, not whole row tiles", (long long)rows);
     P2P_REQUIRE(item_row_tiles == (rows + tc::kTileRows - 1) / tc::kTileRows,
                 "p2p_spmm_tc_grouped: %lld row tiles an item for %lld rows", (long long)item_row_tiles, (long long)rows);
     P2P_REQUIRE(max_tokens >= 1 && max_tokens <= 256, "p2p_spmm_tc_grouped: items of 1 to 256 tokens (%lld)",
@@ -867,11 +955,34 @@ extern "C" int p2p_spmm_tc_grouped(const void* x, int dtype, int64_t x_rows, int
     prm.wait_ns = kWaitNs;
     prm.seq = next_seq();
     prm.hold_tile = -1;
+    prm.gated = gated;
+    if (gated &&
+        (int64_t)pl.n_total * tc::kTileRows * 4 > (int64_t)pl.a_slots * kASlotBytes + (int64_t)pl.x_slots * pl.b_bytes)
+        return fail(P2P_EUNSUPPORTED, "p2p_spmm_tc_grouped_gated: %lld tokens an item do not fit the staged tile",
+                    (long long)max_tokens);
     CUtensorMap map;
     if (int e = encode_x_map(&map, x, dtype, x_rows, cols, ldx, pl.box_rows)) return e;
     const dim3 grid((unsigned)item_row_tiles, (unsigned)n_items);
     return dtype == P2P_BF16 ? launch_tc<__nv_bfloat16>(map, map, prm, grid, pl.smem, st)
                              : launch_tc<__half>(map, map, prm, grid, pl.smem, st);
+}
+}  // namespace
+
+extern "C" int p2p_spmm_tc_grouped(const void* x, int dtype, int64_t x_rows, int64_t cols, int64_t ldx,
+                                   const uint32_t* words, const int64_t* seg, int64_t layout_row_tiles,
+                                   int64_t rows, int64_t item_row_tiles, int64_t seg_cap_words, const int32_t* items,
+                                   int64_t n_items, int64_t max_tokens, void* y, int64_t ldy, void* stream) {
+    return grouped_impl(x, dtype, x_rows, cols, ldx, words, seg, layout_row_tiles, rows, item_row_tiles,
+                        seg_cap_words, items, n_items, max_tokens, y, ldy, stream, 0);
+}
+
+extern "C" int p2p_spmm_tc_grouped_gated(const void* x, int dtype, int64_t x_rows, int64_t cols, int64_t ldx,
+                                         const uint32_t* words, const int64_t* seg, int64_t layout_row_tiles,
+                                         int64_t rows, int64_t item_row_tiles, int64_t seg_cap_words,
+                                         const int32_t* items, int64_t n_items, int64_t max_tokens, void* y,
+                                         int64_t ldy, void* stream) {
+    return grouped_impl(x, dtype, x_rows, cols, ldx, words, seg, layout_row_tiles, rows, item_row_tiles,
+                        seg_cap_words, items, n_items, max_tokens, y, ldy, stream, 1);
 }
 
 extern "C" int p2p_spmm_tc_status(int reset, void* stream) {

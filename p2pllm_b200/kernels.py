@@ -316,6 +316,26 @@ def spmm_tc(x: torch.Tensor, words: torch.Tensor, seg: torch.Tensor, rows: int, 
     return out
 
 
+def spmm_tc_gated(x: torch.Tensor, words: torch.Tensor, seg: torch.Tensor, layout_rows: int, cols: int, seg_cap: int,
+                  out: torch.Tensor | None = None) -> torch.Tensor:
+    """h [tokens, layout_rows / 2] = dtype(silu(g) * u) of a gate + up module in the interleaved tensor-core layout
+    (compact.gate_up_rows), the gate applied in the GEMM's epilogue (p2p_spmm_tc_gated)."""
+    require_cuda(x)
+    if x.dim() != 2 or x.shape[1] != cols:
+        raise P2PError(f"x of {tuple(x.shape)} does not have {cols} columns")
+    if x.stride(1) != 1 or x.stride(0) % 8 or x.data_ptr() % 16:
+        x = x.contiguous()
+    out = _out(out, (x.shape[0], layout_rows // 2), x)
+    lib = _lib.load()
+    need = lib.p2p_spmm_tc_workspace(layout_rows, cols, x.shape[0])
+    ws = _workspace(x.device, need, "spmm_tc") if need else None
+    call("p2p_spmm_tc_gated", ptr(x), dtype_code(x), x.shape[0], cols, x.stride(0), ptr(words), ptr(seg), layout_rows,
+         seg_cap, ptr(out), out.stride(0), ptr(ws), 0 if ws is None else ws.numel(), stream_of(x))
+    if CHECK_WAITS:
+        spmm_tc_status(x.device)
+    return out
+
+
 def spmm_tc_withhold(x: torch.Tensor, words: torch.Tensor, seg: torch.Tensor, rows: int, cols: int, seg_cap: int,
                      hold_tile: int, wait_us: int) -> torch.Tensor:
     """A launch of the tensor-core GEMM in which every CTA withholds its x tile number hold_tile, so the pipeline's

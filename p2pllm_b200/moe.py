@@ -6,9 +6,10 @@ instead of expanding every used expert to dense on every pass (p2p/compact.py:22
     GroupedMoE    quant_method.apply(layer, dispatch_output): gated-SiLU experts (w13 = gate then up, w2 = down)
 
 A pass: one kernel (p2p_moe_route) sorts the routed (token, slot) pairs by expert (stable) and writes the grouped
-GEMM's items; x's rows are gathered in that order; one grouped launch of the compact GEMM (p2p_spmm_tc_grouped: a CTA
-takes one row tile of one expert's run of up to 256 tokens) gives gate and up for every pair; SiLU(gate) * up in fp32,
-rounded to x's dtype; a second grouped launch gives down; p2p_moe_combine weights each token's outputs by its routing
+GEMM's items; x's rows are gathered in that order; one grouped launch of the compact GEMM (p2p_spmm_tc_grouped_gated:
+a CTA takes one row tile of one expert's run of up to 256 tokens, the expert's gate and up rows interleaved 64 and 64
+so that its epilogue writes SiLU(gate) * up, in fp32 from the rounded outputs, rounded to x's dtype); a second grouped
+launch gives down; p2p_moe_combine weights each token's outputs by its routing
 weights and adds them in slot order in fp32 (deterministic). Three numbers (pairs, items, the largest item) are read
 back once a pass to size the launches (the reference's CompactMoE also syncs, on torch.unique).
 """
@@ -18,7 +19,7 @@ import torch
 
 from . import kernels
 from ._lib import P2PError, call, dtype_code, ptr, require_cuda, stream_of
-from .compact import _cols, to_compact
+from .compact import _cols, gate_up_rows, to_compact
 
 ITEM_TOKENS = 256                       # tokens one grouped CTA takes (an accumulator of at most 256 columns)
 
@@ -28,7 +29,11 @@ class ExpertTiles:
     "compact", values [E, r, k], words | idx [E, r, ...], C), in row order), laid out for the grouped GEMM: expert
     e's rows start at row tile e * item_row_tiles. Built once at load (one layout build an expert)."""
 
-    def __init__(self, blocks: list):
+    def __init__(self, blocks: list, gated: bool = False):
+        self.gated = gated
+        if gated:                               # gate rows then up rows, interleaved: one compact (or dense) block
+            values, idx = gate_up_rows(blocks)
+            blocks = [("compact", values, idx, _cols(blocks[0])) if idx is not None else ("dense", values)]
         blocks = [to_compact(b) for b in blocks]
         self.cols = _cols(blocks[0])
         self.experts = blocks[0][1].shape[0]
@@ -56,8 +61,9 @@ class ExpertTiles:
         self.layout_row_tiles = self.experts * self.item_row_tiles
 
     def __call__(self, x: torch.Tensor, items: torch.Tensor, max_tokens: int, out: torch.Tensor) -> torch.Tensor:
-        """out [P, rows] rows s.. of an item = x rows s.. times the item's expert (items: int32 [n, 4] on the GPU)."""
-        call("p2p_spmm_tc_grouped", ptr(x), dtype_code(x), x.shape[0], self.cols, x.stride(0), ptr(self.words),
+        """out [P, rows] rows s.. of an item = x rows s.. times the item's expert (items: int32 [n, 4] on the GPU);
+        gated: out [P, rows / 2] = dtype(silu(gate) * up) of them, applied in the GEMM's epilogue."""
+        call("p2p_spmm_tc_grouped_gated" if self.gated else "p2p_spmm_tc_grouped", ptr(x), dtype_code(x), x.shape[0], self.cols, x.stride(0), ptr(self.words),
              ptr(self.seg), self.layout_row_tiles, self.rows, self.item_row_tiles, self.seg_cap, ptr(items),
              items.shape[0], max_tokens, ptr(out), out.stride(0), stream_of(x))
         if kernels.CHECK_WAITS:
@@ -96,7 +102,12 @@ class GroupedMoE(torch.nn.Module):
     def __init__(self, method, weights: dict):
         super().__init__()
         self.method = method
-        self.w13 = ExpertTiles(weights["w13_weight"])
+        two_r = sum(b[1].shape[-2] for b in weights["w13_weight"])
+        # SiLU(gate) * up inside the gate/up launch when the rows allow it (R a multiple of 64, one k)
+        try:
+            self.w13 = ExpertTiles(weights["w13_weight"], gated=two_r % 128 == 0)
+        except P2PError:
+            self.w13 = ExpertTiles(weights["w13_weight"])
         self.w2 = ExpertTiles(weights["w2_weight"])
         if self.w13.rows % 2 or self.w2.cols != self.w13.rows // 2 or self.w2.rows != self.w13.cols:
             raise P2PError("w13 [E, 2R, H] and w2 [E, H, R] do not match")
@@ -121,9 +132,12 @@ class GroupedMoE(torch.nn.Module):
         if P == 0:
             return out.zero_().reshape(*x.shape[:-1], self.w2.rows)
         xs = x2.index_select(0, r["order"] // K).contiguous()
-        gu = self.w13(xs, r["items"], r["most"], torch.empty(P, self.w13.rows, dtype=x2.dtype, device=x.device))
         R = self.w13.rows // 2
-        h = (torch.nn.functional.silu(gu[:, :R].float()) * gu[:, R:].float()).to(x2.dtype).contiguous()
+        if self.w13.gated:
+            h = self.w13(xs, r["items"], r["most"], torch.empty(P, R, dtype=x2.dtype, device=x.device))
+        else:
+            gu = self.w13(xs, r["items"], r["most"], torch.empty(P, self.w13.rows, dtype=x2.dtype, device=x.device))
+            h = (torch.nn.functional.silu(gu[:, :R].float()) * gu[:, R:].float()).to(x2.dtype).contiguous()
         down = self.w2(h, r["items"], r["most"], torch.empty(P, self.w2.rows, dtype=x2.dtype, device=x.device))
         w = weights.reshape(-1).float().contiguous()
         call("p2p_moe_combine", ptr(down), dtype_code(down), down.stride(0), ptr(r["where"]), ptr(w), T, K,

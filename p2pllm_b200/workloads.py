@@ -142,7 +142,8 @@ class DecoderBlock:
     attention of the pass's own tokens (GQA: 40 query heads over 8 KV heads of 128; no KV cache of earlier tokens and no
     rotary embedding -- this package has neither), o, residual; RMSNorm, SiLU(gate) * up, down, residual. Each of the
     four linear modules (qkv, o, gate_up, down) is a callable x -> y: a dense bf16 weight (torch linear) for an exact
-    layer, a compact.Compact for a replica."""
+    layer, a compact.Compact for a replica. A module "gated" in place of "gate_up" returns SiLU(gate) * up itself
+    (compact.GatedTiles: the activation in the GEMM's epilogue)."""
 
     def __init__(self, modules: dict, heads: int = 40, kv_heads: int = 8, head_dim: int = 128):
         self.m = modules
@@ -158,6 +159,8 @@ class DecoderBlock:
         v = v.reshape(T, self.kv_heads, self.d).transpose(0, 1).unsqueeze(0)
         a = F.scaled_dot_product_attention(q, k, v, is_causal=True, enable_gqa=True)
         h = h + self.m["o"](a.squeeze(0).transpose(0, 1).reshape(T, self.heads * self.d))
+        if "gated" in self.m:
+            return h + self.m["down"](self.m["gated"](rms_norm(h)))
         gu = self.m["gate_up"](rms_norm(h))
         gate, up = gu.chunk(2, dim=-1)
         return h + self.m["down"]((F.silu(gate.float()) * up.float()).to(h.dtype))
@@ -193,7 +196,8 @@ def cfg5_exact(layer: int, device, seed: int = 5) -> DecoderBlock:
 
 def cfg5_replica(layer: int, device, seed: int = 5, layout: str | None = None) -> tuple:
     """(the keep-40 replica of layer `layer` as a DecoderBlock over compact.Compact modules, its weight bytes): every
-    projection pruned by the Wanda selection on the GPU, the dense weights dropped."""
+    projection pruned by the Wanda selection on the GPU, the dense weights dropped. In the tensor-core layout the gate
+    and up projections form one compact.GatedTiles (SiLU * up in the GEMM's epilogue)."""
     from . import compact, wanda
     norms = cfg5_norms(layer, device, seed)
     keep = {p.name: p.keep for p in QWEN25_32B}
@@ -204,6 +208,11 @@ def cfg5_replica(layer: int, device, seed: int = 5, layout: str | None = None) -
         for n in names:
             values, idx = wanda.select(w.pop(n), keep[n], norms[m])
             blocks.append(("compact", values, idx, QWEN25_32B_COLS[n]))
+        if m == "gate_up" and (layout or compact.DEFAULT_LAYOUT) == "tc":
+            gt = compact.GatedTiles(blocks)
+            nbytes += gt.nbytes()
+            mods["gated"] = gt
+            continue
         c = compact.Compact.__new__(compact.Compact)
         c.tiles = compact.Tiles(blocks, layout=layout)
         nbytes += c.nbytes()

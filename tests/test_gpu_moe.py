@@ -124,3 +124,23 @@ def test_route_is_a_stable_sort_by_expert(T, K, E):
             k += 1
         start += c
     assert k == len(items) and r["most"] == max((it[2] for it in items), default=0)
+
+
+def test_grouped_gate_in_the_epilogue_matches_silu_between_launches():
+    """Config-4 shapes (R = 768): the gate/up launch with SiLU(gate) * up in its epilogue against the same pass with
+    the activation between the two launches (rel-L2 1e-3: only the epilogue's exp may differ in the last fp32 bit)."""
+    E, R, H, T, K = 128, 768, 2048, 272, 8
+    blocks, w13, w2, g = _layer(E, R, H, 30, torch.bfloat16, 5)
+    fused = moe.GroupedMoE(None, blocks)
+    assert fused.w13.gated
+    unfused = moe.GroupedMoE(None, blocks)
+    unfused.w13 = moe.ExpertTiles(blocks["w13_weight"])
+    assert not unfused.w13.gated
+    logits = torch.randn(T, E, generator=g, device="cuda")
+    w, ids = logits.softmax(-1).topk(K, dim=-1)
+    x = torch.randn(T, H, generator=g, device="cuda").bfloat16()
+    got = fused.apply(None, Dispatch(x, TopK(w, ids)))
+    want = unfused.apply(None, Dispatch(x, TopK(w, ids)))
+    rel = float((got.double() - want.double()).norm() / want.double().norm())
+    assert rel <= 1e-3, rel
+    _check(got, _reference_moe(x, ids, w, w13, w2))
