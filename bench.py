@@ -600,7 +600,7 @@ def run_sharded(args, layer, rank, world, device, peaks):
     names = list(MODULES)
     blocks = {m: [("compact", *layer.selected[n], layer.proj[n].cols) for n in MODULES[m][1]] for m in names}
     peers = shard.PeerGroup(None, device)
-    sharded = {m: shard.ShardedCompact(blocks[m], fused=True, peers=peers) for m in names}
+    sharded = {m: shard.ShardedCompact(blocks[m], fused=True, peers=peers, layout=args.layout) for m in names}
     for m in names:
         sharded[m].prepare(args.tokens, torch.bfloat16, device)
     xs = {m: layer.inputs[MODULES[m][0]] for m in names}
@@ -700,15 +700,24 @@ def run_sharded(args, layer, rank, world, device, peaks):
     dist.barrier()
     rep_ms = max_over_ranks(_region_ms(layer.step, args.steps, stream), world, device)
 
-    # e2e: rank 0 copies the step's inputs in from pinned memory (input stream, double-buffered) and broadcasts them;
-    # every rank runs its shards, storing into every rank's y; rank 0 copies y back on an output stream while the next
-    # step computes. y of step k sits in the symmetric buffer k % 2 that step k + 2 overwrites on every rank, so rank 0
-    # enters step k + 1's peer barrier only once step k's copy-out has finished.
-    host_x = {m: xs[m].cpu().pin_memory() for m in names} if rank == 0 else None
-    host_y = {m: torch.empty(args.tokens, sharded[m].rows, dtype=torch.bfloat16).pin_memory() for m in names} \
-        if rank == 0 else None
+    # e2e: the step's inputs sit in pinned host memory; each rank copies in its T/N rows of every input (input stream,
+    # double-buffered) and one NCCL all-gather a module assembles x on every rank; every rank runs its shards, storing
+    # into every rank's y; each rank copies its own columns of y back on an output stream while the next step
+    # computes, so the host links of all ranks carry the copies. y of step k sits in the symmetric buffer k % 2 that
+    # step k + 2 overwrites on every rank, so each rank enters step k + 1's peer barrier only once its copy-out of step
+    # k has finished.
+    chunk = -(-args.tokens // world)
+    host_x = {}
+    for m in names:
+        padded = torch.zeros(chunk * world, xs[m].shape[1], dtype=torch.bfloat16)
+        padded[:args.tokens] = xs[m].cpu()
+        host_x[m] = padded[rank * chunk:(rank + 1) * chunk].contiguous().pin_memory()
+    host_y = {m: torch.empty(args.tokens, sharded[m].mine, dtype=torch.bfloat16).pin_memory() for m in names}
     s_in, s_out = torch.cuda.Stream(device), torch.cuda.Stream(device)
-    dev_x = [{m: torch.empty_like(xs[m]) for m in names} for _ in range(2)]
+    stage = [{m: torch.empty(chunk, xs[m].shape[1], dtype=torch.bfloat16, device=device) for m in names}
+             for _ in range(2)]
+    full = [{m: torch.empty(chunk * world, xs[m].shape[1], dtype=torch.bfloat16, device=device) for m in names}
+            for _ in range(2)]
     landed, consumed, copied = ([torch.cuda.Event() for _ in range(2)] for _ in range(3))
     for ev in consumed + copied:
         ev.record(stream)
@@ -716,32 +725,30 @@ def run_sharded(args, layer, rank, world, device, peaks):
     def e2e_run(n):
         for k in range(n):
             buf = k % 2
-            if rank == 0:
-                with torch.cuda.stream(s_in):
-                    s_in.wait_event(consumed[buf])
-                    for m in names:
-                        dev_x[buf][m].copy_(host_x[m], non_blocking=True)
-                    landed[buf].record(s_in)
-                stream.wait_event(landed[buf])
+            with torch.cuda.stream(s_in):
+                s_in.wait_event(consumed[buf])
+                for m in names:
+                    stage[buf][m].copy_(host_x[m], non_blocking=True)
+                landed[buf].record(s_in)
+            stream.wait_event(landed[buf])
             for m in names:
-                dist.broadcast(dev_x[buf][m], 0)
+                dist.all_gather_into_tensor(full[buf][m], stage[buf][m])
             mods = rotation[k % copies]
             ys = {}
             for m in names:
                 mods[m]._turn = buf                    # y buffer by step parity, whichever weight copy runs
-                ys[m] = mods[m].apply_fused(dev_x[buf][m], sync=False)
+                ys[m] = mods[m].apply_fused(full[buf][m][:args.tokens], sync=False)
             consumed[buf].record(stream)
-            if rank == 0:
-                stream.wait_event(copied[buf ^ 1])     # step k - 1's y has reached the host
+            stream.wait_event(copied[buf ^ 1])         # this rank's copy-out of step k - 1 has finished
             peers.barrier()
-            if rank == 0:
-                done = torch.cuda.Event()
-                done.record(stream)
-                with torch.cuda.stream(s_out):
-                    s_out.wait_event(done)
-                    for m in names:
-                        host_y[m].copy_(ys[m], non_blocking=True)
-                    copied[buf].record(s_out)
+            done = torch.cuda.Event()
+            done.record(stream)
+            with torch.cuda.stream(s_out):
+                s_out.wait_event(done)
+                for m in names:
+                    a_, b_ = sharded[m].ranges[rank]
+                    host_y[m].copy_(ys[m][:, a_:b_], non_blocking=True)
+                copied[buf].record(s_out)
 
     e2e_run(max(3, copies))
     torch.cuda.synchronize(device)
@@ -755,7 +762,7 @@ def run_sharded(args, layer, rank, world, device, peaks):
     torch.cuda.synchronize(device)
     e2e_ms = max_over_ranks(a.elapsed_time(b), world, device)
     peers.status()
-    h2d = sum(t.numel() * 2 for t in xs.values())
+    h2d = sum(chunk * world * t.shape[1] * 2 for t in xs.values())
     d2h = sum(args.tokens * sharded[m].rows * 2 for m in names)
 
     local_bytes = sum(sharded[m].local.nbytes() for m in names if sharded[m].local is not None) + \
@@ -768,7 +775,8 @@ def run_sharded(args, layer, rank, world, device, peaks):
             "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (seeded N(0,0.02) weights, lognormal-scaled N(0,1) activations; no checkpoint or dataset)",
             "config": {"workload": "cfg2 Llama-3-8B replica layer (q,k,v,o keep 33; gate,up,down keep 36), "
-                                   f"T={args.tokens}", "tokens": args.tokens, "layout": "mask",
+                                   f"T={args.tokens}", "tokens": args.tokens,
+                       "layout": sharded[names[0]].local.tiles.layout,
                        "parallelism": f"row-sharded over {world} GPUs (whole 128-row tiles of every module a rank, "
                                       "full x); y gathered in the GEMM's epilogue by peer stores over NVLink, one "
                                       "bounded peer barrier a step",
@@ -790,8 +798,9 @@ def run_sharded(args, layer, rank, world, device, peaks):
                          "how": "each rank the whole layer on its own tokens, no data-path collective"},
             "e2e": {"value": args.tokens * args.steps / (e2e_ms / 1e3), "unit": UNIT, "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h,
-                    "how": "rank 0: pinned-host inputs in (input stream), NCCL broadcast, every rank its fused shards "
-                           "+ a peer barrier, rank 0: y back to pinned host memory on an output stream overlapping "
+                    "how": "each rank copies its T/N rows of the pinned-host inputs in (input stream), an NCCL "
+                           "all-gather a module assembles x, every rank its fused shards + a peer barrier, each rank "
+                           "copies its own columns of y back to pinned host memory on an output stream overlapping "
                            "the next step",
                     "d2h_mb_per_step": d2h / 1e6},
             "gpu_launches": args.steps * (len(names) + 1),
@@ -832,7 +841,7 @@ def _cfg5_down_sharded(args, rank, world, device, stream) -> dict:
         us = _region_ms(lambda: whole.apply(None, x), args.steps, stream) / args.steps * 1e3
         return {"us_per_call": us, "ranks": 1, "layout": whole.tiles.layout, "weights_mb": whole.nbytes() / 1e6}
     peers = shard.PeerGroup(None, device)
-    sc = shard.ShardedCompact(blocks, fused=True, peers=peers)
+    sc = shard.ShardedCompact(blocks, fused=True, peers=peers, layout=args.layout)
     sc.prepare(T, torch.bfloat16, device)
     y = sc.apply(None, x).clone()
     digest = int.from_bytes(hashlib.sha256(y.cpu().view(torch.int16).numpy().tobytes()).digest()[:7], "little")
@@ -858,7 +867,7 @@ def _cfg5_down_sharded(args, rank, world, device, stream) -> dict:
     dist.barrier()
     ms = max_over_ranks(_region_ms(call, args.steps, stream), world, device)
     peers.status()
-    return {"us_per_call": ms / args.steps * 1e3, "ranks": world, "layout": "mask", "rows_per_rank": sc.mine,
+    return {"us_per_call": ms / args.steps * 1e3, "ranks": world, "layout": sc.local.tiles.layout, "rows_per_rank": sc.mine,
             "shard_mb": sc.local.nbytes() / 1e6, "rel_l2_vs_one_gpu": _bcast_from(rel, 0, world, device),
             "same_bits_on_every_rank": same, "l2": f"{copies} copies of each rank's shard in turn",
             "how": "each rank its 128-row tiles of the module, y stored into every rank's y by the GEMM's epilogue, "

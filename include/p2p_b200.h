@@ -239,6 +239,16 @@ int p2p_spmm_tc_grouped(const void* x, int dtype, int64_t x_rows, int64_t cols, 
                         int64_t seg_cap_words, const int32_t* items, int64_t n_items, int64_t max_tokens, void* y,
                         int64_t ldy, void* stream);
 
+/* p2p_spmm_tc with the all-gather of a row-sharded module fused into its epilogue: this rank's `rows` rows of y go
+ * to columns y_col0 .. y_col0 + rows - 1 of each of the n_ys (1..8) buffers ys[k] [tokens, ldy] -- the y of every
+ * rank of the node, peers' buffers addressed through CUDA IPC / symmetric memory -- by plain stores over NVLink (8-byte
+ * stores when ldy, y_col0 and the buffers allow). The other ranks read their y only after a p2p_peer_barrier that
+ * follows this launch on every rank. The counterpart of p2p_spmm_mask_peers for the tensor-core layout; no
+ * counterpart in the reference (it all-gathers through NCCL, p2p/wanda.py:81 on the scores). */
+int p2p_spmm_tc_peers(const void* x, int dtype, int64_t tokens, int64_t cols, int64_t ldx, const uint32_t* words,
+                      const int64_t* seg, int64_t rows, int64_t seg_cap_words, void* const* ys, int n_ys,
+                      int64_t y_col0, int64_t ldy, void* workspace, size_t workspace_bytes, void* stream);
+
 /* The gated forms: a gate + up module whose rows are interleaved 64 and 64 (row tile k: gate rows 64k..64k+63, then
  * up rows 64k..64k+63; rows = 2R, R a multiple of 64), and y [tokens, ldy >= R] = dtype(silu(g) * u), g and u the two
  * projections' outputs rounded to dtype, computed in the GEMM's epilogue (the accumulators of a row tile meet in
@@ -252,6 +262,16 @@ int p2p_spmm_tc_grouped_gated(const void* x, int dtype, int64_t x_rows, int64_t 
                               const uint32_t* words, const int64_t* seg, int64_t layout_row_tiles, int64_t rows,
                               int64_t item_row_tiles, int64_t seg_cap_words, const int32_t* items, int64_t n_items,
                               int64_t max_tokens, void* y, int64_t ldy, void* stream);
+
+/* The gated half of expert calibration on the grouped launch: for routed experts whose gate + up rows are interleaved
+ * as above (dense rows work too: a keep-100 layout), sums [n_items, ld_sums >= rows / 2] fp32 receives, per item and
+ * unit j, the sum over the item's tokens of (silu(g) * u)^2 with g and u the unrounded fp32 products (bf16 / f16
+ * inputs multiply exactly in fp32). Nothing else is written. Replaces p2p/wanda.py:16-19's loop (an fp32 GEMM, SiLU
+ * and a sum of squares per expert). */
+int p2p_spmm_tc_grouped_gated_sums(const void* x, int dtype, int64_t x_rows, int64_t cols, int64_t ldx,
+                                   const uint32_t* words, const int64_t* seg, int64_t layout_row_tiles, int64_t rows,
+                                   int64_t item_row_tiles, int64_t seg_cap_words, const int32_t* items,
+                                   int64_t n_items, int64_t max_tokens, float* sums, int64_t ld_sums, void* stream);
 
 /* The routing of a routed-experts pass, on the GPU: ids [n_pairs] int64 (a token's slots consecutive; < 0: no expert).
  * order [n_pairs]: the routed pairs sorted by expert, and within an expert by pair index (stable); where [n_pairs]:

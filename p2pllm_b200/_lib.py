@@ -67,9 +67,13 @@ SIGNATURES = {
     "p2p_spmm_tc_grouped": ([_vp, _int, _i64, _i64, _i64, _vp, _vp, _i64, _i64, _i64, _i64, _vp, _i64, _i64, _vp, _i64,
                              _vp], _int),
     "p2p_spmm_tc_status": ([_int, _vp], _int),
+    "p2p_spmm_tc_peers": ([_vp, _int, _i64, _i64, _i64, _vp, _vp, _i64, _i64, ctypes.POINTER(_vp), _int, _i64, _i64, _vp,
+                           _sz, _vp], _int),
     "p2p_spmm_tc_gated": ([_vp, _int, _i64, _i64, _i64, _vp, _vp, _i64, _i64, _vp, _i64, _vp, _sz, _vp], _int),
     "p2p_spmm_tc_grouped_gated": ([_vp, _int, _i64, _i64, _i64, _vp, _vp, _i64, _i64, _i64, _i64, _vp, _i64, _i64,
                                    _vp, _i64, _vp], _int),
+    "p2p_spmm_tc_grouped_gated_sums": ([_vp, _int, _i64, _i64, _i64, _vp, _vp, _i64, _i64, _i64, _i64, _vp, _i64,
+                                        _i64, _vp, _i64, _vp], _int),
     "p2p_spmm_tc_withhold": ([_vp, _int, _i64, _i64, _i64, _vp, _vp, _i64, _i64, _vp, _i64, _vp, _sz, _i64, _i64,
                               _vp], _int),
     "p2p_moe_route": ([_vp, _i64, _int, _vp, _vp, _vp, _vp, _i64, _vp, _vp], _int),

@@ -11,8 +11,8 @@
 // p2p_hop_send (one launch on the sender): each CTA first waits until every destination has consumed pass
 // p - ring of this sender (so the slot is free), then computes its share of the part -- a copy or fp32 sum of parts,
 // a member's difference dtype(y - x), or the whole group combine of p2p/replica.py:81-85 -- and stores it straight
-// into every destination's slot over NVLink; then one thread fences at system scope and adds 1 to every destination's
-// arrived[me] with a release. p2p_hop_recv (one launch on the receiver): each CTA waits until arrived[s] shows all
+// into every destination's slot over NVLink; then, after a CTA barrier, one thread fences (acquire-release, system
+// scope) and adds 1 to every destination's arrived[me] with a release. p2p_hop_recv (one launch on the receiver): each CTA waits until arrived[s] shows all
 // of pass p from every source s, adds the parts in fp32 in member order into `out` (rounded once, to the model dtype),
 // and adds 1 to every source's freed[me]. Both kernels run hop_grid(n) CTAs, so a pass is complete at
 // (p + 1) * grid arrivals; counters only grow (compared modulo 2^32).
@@ -56,7 +56,7 @@ __device__ bool wait_count(const uint32_t* p, uint32_t target, uint64_t limit_ns
         asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
         if ((int32_t)(v - target) >= 0) return true;
         if (hop_now() - t0 > limit_ns) return false;
-        __nanosleep(100);
+        __nanosleep(32);
     }
 }
 
@@ -103,9 +103,9 @@ __global__ void __launch_bounds__(kHopBlock) hop_send_kernel(const __grid_consta
         const uint4 raw = pack_vec<T, VEC>(total);
         for (int d = 0; d < dst.n; ++d) *reinterpret_cast<uint4*>(dst.inbox[d] + slot + v * 16) = raw;
     }
-    __syncthreads();
+    __syncthreads();                            // every thread's stores of the part happen before the signal
     if (threadIdx.x == 0) {
-        __threadfence_system();
+        asm volatile("fence.acq_rel.sys;" ::: "memory");
         for (int d = 0; d < dst.n; ++d) signal(reinterpret_cast<uint32_t*>(dst.inbox[d] + kArrivedAt) + me);
     }
 }
@@ -147,9 +147,9 @@ __global__ void __launch_bounds__(kHopBlock) hop_recv_kernel(const __grid_consta
         }
         store_vec<T, VEC>(out, v * VEC, total);
     }
-    __syncthreads();
+    __syncthreads();                            // every read of the slots is done before the slots are freed
     if (threadIdx.x == 0) {
-        __threadfence_system();
+        asm volatile("fence.acq_rel.sys;" ::: "memory");
         for (int s = 0; s < src.n; ++s) signal(reinterpret_cast<uint32_t*>(src.inbox[s] + kFreedAt) + me);
     }
 }

@@ -98,8 +98,45 @@ struct TcParams {
     // gate rows 64k..64k+63, then the up rows of the same units), and y [tokens, rows / 2] takes
     // dtype(silu(gate) * up) of the two rounded outputs, column 64k + j. The accumulators meet in shared memory (or
     // the cluster's, or the partials) before the product; y never leaves through TMA.
+    // gated == 2 (grouped launches only): no y; per item and unit j, sums[item, 64k + j] = the fp32 sum over the
+    // item's tokens of (silu(g) * u)^2, g and u the unrounded fp32 accumulators (the gated half of expert calibration).
     int gated;
+    float* sums;
+    int64_t ld_sums;
+    // Row sharding with the all-gather fused in: n_ys > 0 sends every value of y to each ys[k] (every rank's y, peers'
+    // through peer memory) at column y_col0 + row, instead of y. Plain stores only (no TMA); vec4: 8-byte stores of 4
+    // values are aligned.
+    void* ys[8];
+    int n_ys, vec4;
+    int64_t y_col0;
 };
+
+// Four values of y row `yrow` from module row c0 on (rows past the module are not written): to y, or to every ys[k].
+template <typename T, bool kPeers>
+__device__ __forceinline__ void put4(const TcParams& p, int64_t yrow, int64_t c0, const float (&v)[4]) {
+    if constexpr (!kPeers) {
+        T* yt = reinterpret_cast<T*>(p.y) + yrow * p.ldy;
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+            if (c0 + c < p.rows) yt[c0 + c] = from_f32<T>(v[c]);
+        return;
+    }
+    const int64_t at = yrow * p.ldy + p.y_col0 + c0;
+    if (p.vec4 && c0 + 3 < p.rows) {
+        uint2 raw;
+        T* e = reinterpret_cast<T*>(&raw);
+#pragma unroll
+        for (int c = 0; c < 4; ++c) e[c] = from_f32<T>(v[c]);
+        for (int k = 0; k < p.n_ys; ++k) *reinterpret_cast<uint2*>(reinterpret_cast<T*>(p.ys[k]) + at) = raw;
+        return;
+    }
+    for (int k = 0; k < p.n_ys; ++k) {
+        T* yt = reinterpret_cast<T*>(p.ys[k]) + at;
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+            if (c0 + c < p.rows) yt[c] = from_f32<T>(v[c]);
+    }
+}
 
 // y[t, c] of a gated launch from one unit of 4 gate sums g and the 4 up sums u of the same units (fp32): each output
 // rounded as the unfused path rounds it -- the projection's outputs to the model dtype, then SiLU(gate) * up in fp32.
@@ -156,7 +193,8 @@ __device__ __forceinline__ void l2_prefetch(const void* src, uint32_t bytes) {
 
 
 // kL2: the launch prefetches segments into L2 ahead of the register loads (few tokens; see the expanders).
-template <typename T, bool kL2>
+// kPeers: y goes to every ys[k] (row sharding with the all-gather fused in) instead of y.
+template <typename T, bool kL2, bool kPeers>
 __global__ void __launch_bounds__(kTcThreads, 1)
     spmm_tc_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_y, TcParams p) {
     extern __shared__ uint8_t smem_raw[];
@@ -429,7 +467,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     } else if (p.y_tma) {
                         reinterpret_cast<T*>(gbase)[t * tc::kTileRows + row_local] = from_f32<T>(v[j]);  // rings free
                     } else if (p.n_split == 1) {
-                        if (row_ok) reinterpret_cast<T*>(p.y)[(xrow0 + t) * p.ldy + row] = from_f32<T>(v[j]);
+                        if (row_ok) {
+                            if constexpr (!kPeers) {
+                                reinterpret_cast<T*>(p.y)[(xrow0 + t) * p.ldy + row] = from_f32<T>(v[j]);
+                            } else {
+                                const int64_t at = (xrow0 + t) * p.ldy + p.y_col0 + row;
+                                for (int k = 0; k < p.n_ys; ++k) reinterpret_cast<T*>(p.ys[k])[at] = from_f32<T>(v[j]);
+                            }
+                        }
                     } else if (p.cluster) {
                         reinterpret_cast<float*>(gbase)[t * tc::kTileRows + row_local] = v[j];   // rings are free
                     } else if (row_ok) {
@@ -446,6 +491,30 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     if (warp == kProducerWarp) {
         tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(p.tmem_cols) : "memory");
+    }
+    if (p.gated == 2) {
+        // Column sums of squares of the gated activations: thread (unit j, token group tg) adds tokens tg, tg + 8,
+        // ... in fp32; then the 8 groups are added in order (the result does not depend on scheduling).
+        const float* acc = reinterpret_cast<const float*>(gbase);
+        float* red = reinterpret_cast<float*>(gbase) + (size_t)p.n_total * tc::kTileRows;
+        for (int q = threadIdx.x; q < 64 * 8; q += kTcThreads) {
+            const int j = q & 63, tg = q >> 6;
+            float sum = 0.f;
+            for (int t = tg; t < tokens; t += 8) {
+                const float g = acc[t * tc::kTileRows + j], u = acc[t * tc::kTileRows + 64 + j];
+                const float a = g / (1.0f + expf(-g)) * u;
+                sum = fmaf(a, a, sum);
+            }
+            red[tg * 64 + j] = sum;
+        }
+        __syncthreads();
+        if (threadIdx.x < 64) {
+            float sum = 0.f;
+#pragma unroll
+            for (int tg = 0; tg < 8; ++tg) sum += red[tg * 64 + threadIdx.x];
+            p.sums[(int64_t)blockIdx.y * p.ld_sums + (col0 >> 1) + threadIdx.x] = sum;
+        }
+        return;
     }
     if (p.gated && p.n_split == 1) {
         // The tile's accumulators are in shared memory ([token][128 rows], fp32): gate unit r and up unit r sit 64
@@ -516,12 +585,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 if (sp < ns) {
                     acc.x += parts[sp].x; acc.y += parts[sp].y; acc.z += parts[sp].z; acc.w += parts[sp].w;
                 }
-            const int64_t row = col0 + r4;
-            T* yt = reinterpret_cast<T*>(p.y) + (xrow0 + t) * p.ldy;
             const float v[4] = {acc.x, acc.y, acc.z, acc.w};
-#pragma unroll
-            for (int c = 0; c < 4; ++c)
-                if (row + c < p.rows) yt[row + c] = from_f32<T>(v[c]);
+            put4<T, kPeers>(p, xrow0 + t, col0 + r4, v);
         }
         cluster_sync_all();
         return;
@@ -595,11 +660,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             const int64_t u = u0 + (int64_t)q * kTcThreads;
             if (u >= n4) break;
             const int64_t t = u / 32, row = col + (u % 32) * 4;
-            T* yt = reinterpret_cast<T*>(p.y) + t * p.ldy;
             const float v[4] = {acc[q].x, acc[q].y, acc[q].z, acc[q].w};
-#pragma unroll
-            for (int c = 0; c < 4; ++c)
-                if (row + c < p.rows) yt[row + c] = from_f32<T>(v[c]);
+            put4<T, kPeers>(p, t, row, v);
         }
     }
     if (threadIdx.x == 0) p.tickets[rt] = 0u;            // the workspace is zeroed again for the next call
@@ -642,7 +704,9 @@ int launch_tc(const CUtensorMap& map, const CUtensorMap& ymap, const TcParams& p
               cudaStream_t st) {
     // Few tokens: the variant that prefetches the segments into L2.
     const bool l2 = prm.n_total <= 64;
-    auto kernel = l2 ? spmm_tc_kernel<T, true> : spmm_tc_kernel<T, false>;
+    auto kernel = spmm_tc_kernel<T, false, false>;
+    if (prm.n_ys) kernel = l2 ? spmm_tc_kernel<T, true, true> : spmm_tc_kernel<T, false, true>;
+    else if (l2) kernel = spmm_tc_kernel<T, true, false>;
     if (int e = allow_smem((const void*)kernel, smem, "p2p_spmm_tc")) return e;
     // A programmatic dependent of the stream's previous kernel (the kernel waits for it before loading x), and with
     // split columns reduced in clusters, the n_split CTAs of a row tile as one cluster (grid.y == n_split).
@@ -693,10 +757,14 @@ int max_clusters(const TcPlan& pl, int n_split) {
     auto it = known.find(key);
     if (it != known.end()) return it->second;
     int clusters = 0;
-    if (allow_smem((const void*)spmm_tc_kernel<__nv_bfloat16, false>, pl.smem, "p2p_spmm_tc") == P2P_OK &&
-        allow_smem((const void*)spmm_tc_kernel<__nv_bfloat16, true>, pl.smem, "p2p_spmm_tc") == P2P_OK &&
-        allow_smem((const void*)spmm_tc_kernel<__half, false>, pl.smem, "p2p_spmm_tc") == P2P_OK &&
-        allow_smem((const void*)spmm_tc_kernel<__half, true>, pl.smem, "p2p_spmm_tc") == P2P_OK) {
+    const void* variants[8] = {
+        (const void*)spmm_tc_kernel<__nv_bfloat16, false, false>, (const void*)spmm_tc_kernel<__nv_bfloat16, true, false>,
+        (const void*)spmm_tc_kernel<__half, false, false>,        (const void*)spmm_tc_kernel<__half, true, false>,
+        (const void*)spmm_tc_kernel<__nv_bfloat16, false, true>,  (const void*)spmm_tc_kernel<__nv_bfloat16, true, true>,
+        (const void*)spmm_tc_kernel<__half, false, true>,         (const void*)spmm_tc_kernel<__half, true, true>};
+    bool allowed = true;
+    for (const void* k : variants) allowed = allowed && allow_smem(k, pl.smem, "p2p_spmm_tc") == P2P_OK;
+    if (allowed) {
         cudaLaunchConfig_t cfg = {};
         cudaLaunchAttribute attr[1];
         attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -708,7 +776,7 @@ int max_clusters(const TcPlan& pl, int n_split) {
         cfg.dynamicSmemBytes = pl.smem;
         cfg.attrs = attr;
         cfg.numAttrs = 1;
-        if (cudaOccupancyMaxActiveClusters(&clusters, spmm_tc_kernel<__nv_bfloat16, false>, &cfg) != cudaSuccess)
+        if (cudaOccupancyMaxActiveClusters(&clusters, spmm_tc_kernel<__nv_bfloat16, false, false>, &cfg) != cudaSuccess)
             clusters = 0;
         cudaGetLastError();                                  // a refusal here only means: use the workspace path
     }
@@ -782,14 +850,20 @@ namespace {
 // p2p_spmm_tc, with the wait limit and withheld tile of p2p_spmm_tc_withhold (hold_tile < 0: none).
 int spmm_tc_impl(const void* x, int dtype, int64_t tokens, int64_t cols, int64_t ldx, const uint32_t* words,
                  const int64_t* seg, int64_t rows, int64_t seg_cap_words, void* y, int64_t ldy, void* workspace,
-                 size_t workspace_bytes, void* stream, int hold_tile, uint64_t wait_ns, int gated) {
+                 size_t workspace_bytes, void* stream, int hold_tile, uint64_t wait_ns, int gated,
+                 void* const* ys = nullptr, int n_ys = 0, int64_t y_col0 = 0) {
     P2P_REQUIRE(tokens >= 0 && rows >= 0 && cols >= 1, "p2p_spmm_tc: bad shape");
     P2P_REQUIRE(!gated || rows % tc::kTileRows == 0, "p2p_spmm_tc_gated: %lld interleaved rows, not whole row tiles",
                 (long long)rows);
     if (tokens == 0 || rows == 0) return P2P_OK;
     if (dtype != P2P_BF16 && dtype != P2P_F16)
         return fail(P2P_EUNSUPPORTED, "p2p_spmm_tc: bf16 or f16 (fp32 weights take p2p_spmm_rows)");
-    P2P_REQUIRE(x && words && seg && y, "p2p_spmm_tc: null pointer");
+    P2P_REQUIRE(x && words && seg && (y || n_ys > 0), "p2p_spmm_tc: null pointer");
+    P2P_REQUIRE(n_ys >= 0 && n_ys <= 8 && !(n_ys && gated), "p2p_spmm_tc_peers: 1 to 8 y buffers, not gated");
+    for (int k = 0; k < n_ys; ++k) P2P_REQUIRE(ys[k], "p2p_spmm_tc_peers: y buffer %d is null", k);
+    P2P_REQUIRE(n_ys == 0 || (y_col0 >= 0 && y_col0 + rows <= ldy),
+                "p2p_spmm_tc_peers: columns %lld.. of %lld rows do not fit ldy %lld", (long long)y_col0,
+                (long long)rows, (long long)ldy);
     P2P_REQUIRE(aligned16(words), "p2p_spmm_tc: words must start on a 16-byte boundary");
     P2P_REQUIRE(cols % 8 == 0 && ldx % 8 == 0 && ldx >= cols && aligned16(x),
                 "p2p_spmm_tc: x needs 16-byte aligned rows (cols and ldx multiples of 8)");
@@ -826,7 +900,7 @@ int spmm_tc_impl(const void* x, int dtype, int64_t tokens, int64_t cols, int64_t
         prm.b_bytes = pl.b_bytes;
         prm.kt_per_split = pl.kt_per_split;
         prm.n_split = pl.n_split;
-        prm.y = reinterpret_cast<char*>(y) + t0 * ldy * elem;
+        prm.y = y ? reinterpret_cast<char*>(y) + t0 * ldy * elem : nullptr;
         prm.ldy = ldy;
         prm.rows_pad = row_tiles * tc::kTileRows;
         prm.partial = nullptr;
@@ -848,6 +922,15 @@ int spmm_tc_impl(const void* x, int dtype, int64_t tokens, int64_t cols, int64_t
         prm.seq = next_seq();
         prm.hold_tile = hold_tile;
         prm.gated = gated;
+        prm.sums = nullptr;
+        prm.ld_sums = 0;
+        prm.n_ys = n_ys;
+        prm.y_col0 = y_col0;
+        prm.vec4 = ldy % 4 == 0 && y_col0 % 4 == 0;
+        for (int k = 0; k < 8; ++k) {
+            prm.ys[k] = k < n_ys ? reinterpret_cast<char*>(ys[k]) + t0 * ldy * elem : nullptr;
+            if (k < n_ys && (reinterpret_cast<uintptr_t>(ys[k]) & 7)) prm.vec4 = 0;
+        }
         if (gated && pl.n_split == 1 &&
             (int64_t)pl.n_total * tc::kTileRows * 4 > (int64_t)pl.a_slots * kASlotBytes + (int64_t)pl.x_slots * pl.b_bytes)
             return fail(P2P_EUNSUPPORTED, "p2p_spmm_tc_gated: %d tokens do not fit the staged tile", tn);
@@ -856,7 +939,7 @@ int spmm_tc_impl(const void* x, int dtype, int64_t tokens, int64_t cols, int64_t
         if (int e = encode_x_map(&map, xt, dtype, tn, cols, ldx, pl.box_rows)) return e;
         // y through TMA stores when unsplit and aligned (rows of y start on 16 bytes); the staged tile is
         // n_total x 128 x 2 bytes of the rings
-        prm.y_tma = !gated && pl.n_split == 1 && ldy % 8 == 0 && aligned16(prm.y) &&
+        prm.y_tma = !gated && n_ys == 0 && pl.n_split == 1 && ldy % 8 == 0 && aligned16(prm.y) &&
                     (int64_t)pl.n_total * tc::kTileRows * 2 <= (int64_t)pl.a_slots * kASlotBytes;
         ymap = map;
         if (prm.y_tma && encode_y_map(&ymap, prm.y, dtype, tn, rows, ldy, pl.box_rows) != P2P_OK) prm.y_tma = 0;
@@ -874,6 +957,15 @@ extern "C" int p2p_spmm_tc(const void* x, int dtype, int64_t tokens, int64_t col
                            void* workspace, size_t workspace_bytes, void* stream) {
     return spmm_tc_impl(x, dtype, tokens, cols, ldx, words, seg, rows, seg_cap_words, y, ldy, workspace,
                         workspace_bytes, stream, -1, kWaitNs, 0);
+}
+
+extern "C" int p2p_spmm_tc_peers(const void* x, int dtype, int64_t tokens, int64_t cols, int64_t ldx,
+                                 const uint32_t* words, const int64_t* seg, int64_t rows, int64_t seg_cap_words,
+                                 void* const* ys, int n_ys, int64_t y_col0, int64_t ldy, void* workspace,
+                                 size_t workspace_bytes, void* stream) {
+    P2P_REQUIRE(ys && n_ys >= 1, "p2p_spmm_tc_peers: no y buffers");
+    return spmm_tc_impl(x, dtype, tokens, cols, ldx, words, seg, rows, seg_cap_words, nullptr, ldy, workspace,
+                        workspace_bytes, stream, -1, kWaitNs, 0, ys, n_ys, y_col0);
 }
 
 extern "C" int p2p_spmm_tc_gated(const void* x, int dtype, int64_t tokens, int64_t cols, int64_t ldx,
@@ -899,11 +991,12 @@ namespace {
 int grouped_impl(const void* x, int dtype, int64_t x_rows, int64_t cols, int64_t ldx, const uint32_t* words,
                  const int64_t* seg, int64_t layout_row_tiles, int64_t rows, int64_t item_row_tiles,
                  int64_t seg_cap_words, const int32_t* items, int64_t n_items, int64_t max_tokens, void* y,
-                 int64_t ldy, void* stream, int gated) {
+                 int64_t ldy, void* stream, int gated, float* sums = nullptr, int64_t ld_sums = 0) {
     P2P_REQUIRE(x_rows >= 0 && rows >= 1 && cols >= 1 && n_items >= 0, "p2p_spmm_tc_grouped: bad shape");
     if (n_items == 0 || x_rows == 0) return P2P_OK;
     if (dtype != P2P_BF16 && dtype != P2P_F16) return fail(P2P_EUNSUPPORTED, "p2p_spmm_tc_grouped: bf16 or f16");
-    P2P_REQUIRE(x && words && seg && items && y, "p2p_spmm_tc_grouped: null pointer");
+    P2P_REQUIRE(x && words && seg && items && (y || gated == 2) && (sums || gated != 2),
+                "p2p_spmm_tc_grouped: null pointer");
     P2P_REQUIRE(aligned16(words) && aligned16(items), "p2p_spmm_tc_grouped: words and items need 16-byte alignment");
     P2P_REQUIRE(cols % 8 == 0 && ldx % 8 == 0 && ldx >= cols && aligned16(x),
                 "p2p_spmm_tc_grouped: x needs 16-byte aligned rows (cols and ldx multiples of 8)");
@@ -956,8 +1049,14 @@ int grouped_impl(const void* x, int dtype, int64_t x_rows, int64_t cols, int64_t
     prm.seq = next_seq();
     prm.hold_tile = -1;
     prm.gated = gated;
-    if (gated &&
-        (int64_t)pl.n_total * tc::kTileRows * 4 > (int64_t)pl.a_slots * kASlotBytes + (int64_t)pl.x_slots * pl.b_bytes)
+    prm.sums = sums;
+    prm.ld_sums = ld_sums;
+    prm.n_ys = 0;
+    prm.vec4 = 0;
+    prm.y_col0 = 0;
+    for (int k = 0; k < 8; ++k) prm.ys[k] = nullptr;
+    if (gated && (int64_t)pl.n_total * tc::kTileRows * 4 + (gated == 2 ? 64 * 8 * 4 : 0) >
+                     (int64_t)pl.a_slots * kASlotBytes + (int64_t)pl.x_slots * pl.b_bytes)
         return fail(P2P_EUNSUPPORTED, "p2p_spmm_tc_grouped_gated: %lld tokens an item do not fit the staged tile",
                     (long long)max_tokens);
     CUtensorMap map;
@@ -983,6 +1082,17 @@ extern "C" int p2p_spmm_tc_grouped_gated(const void* x, int dtype, int64_t x_row
                                          int64_t ldy, void* stream) {
     return grouped_impl(x, dtype, x_rows, cols, ldx, words, seg, layout_row_tiles, rows, item_row_tiles,
                         seg_cap_words, items, n_items, max_tokens, y, ldy, stream, 1);
+}
+
+extern "C" int p2p_spmm_tc_grouped_gated_sums(const void* x, int dtype, int64_t x_rows, int64_t cols, int64_t ldx,
+                                              const uint32_t* words, const int64_t* seg, int64_t layout_row_tiles,
+                                              int64_t rows, int64_t item_row_tiles, int64_t seg_cap_words,
+                                              const int32_t* items, int64_t n_items, int64_t max_tokens, float* sums,
+                                              int64_t ld_sums, void* stream) {
+    P2P_REQUIRE(ld_sums >= rows / 2, "p2p_spmm_tc_grouped_gated_sums: ld_sums %lld below %lld", (long long)ld_sums,
+                (long long)(rows / 2));
+    return grouped_impl(x, dtype, x_rows, cols, ldx, words, seg, layout_row_tiles, rows, item_row_tiles,
+                        seg_cap_words, items, n_items, max_tokens, nullptr, rows / 2, stream, 2, sums, ld_sums);
 }
 
 extern "C" int p2p_spmm_tc_status(int reset, void* stream) {

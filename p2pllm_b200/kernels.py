@@ -316,6 +316,24 @@ def spmm_tc(x: torch.Tensor, words: torch.Tensor, seg: torch.Tensor, rows: int, 
     return out
 
 
+def spmm_tc_peers(x: torch.Tensor, words: torch.Tensor, seg: torch.Tensor, rows: int, cols: int, seg_cap: int, ys,
+                  n_ys: int, y_col0: int, ldy: int) -> None:
+    """This rank's rows of y = x times a module in the tensor-core layout, stored at columns y_col0.. of each of the
+    n_ys y buffers (a ctypes array of device pointers: every rank's y, peers' through peer memory)."""
+    require_cuda(x)
+    if x.dim() != 2 or x.shape[1] != cols:
+        raise P2PError(f"x of {tuple(x.shape)} does not have {cols} columns")
+    if x.stride(1) != 1 or x.stride(0) % 8 or x.data_ptr() % 16:
+        x = x.contiguous()
+    lib = _lib.load()
+    need = lib.p2p_spmm_tc_workspace(rows, cols, x.shape[0])
+    ws = _workspace(x.device, need, "spmm_tc") if need else None
+    call("p2p_spmm_tc_peers", ptr(x), dtype_code(x), x.shape[0], cols, x.stride(0), ptr(words), ptr(seg), rows,
+         seg_cap, ys, n_ys, y_col0, ldy, ptr(ws), 0 if ws is None else ws.numel(), stream_of(x))
+    if CHECK_WAITS:
+        spmm_tc_status(x.device)
+
+
 def spmm_tc_gated(x: torch.Tensor, words: torch.Tensor, seg: torch.Tensor, layout_rows: int, cols: int, seg_cap: int,
                   out: torch.Tensor | None = None) -> torch.Tensor:
     """h [tokens, layout_rows / 2] = dtype(silu(g) * u) of a gate + up module in the interleaved tensor-core layout

@@ -70,6 +70,16 @@ class ExpertTiles:
             kernels.spmm_tc_status(x.device)
         return out
 
+    def gated_sums(self, x: torch.Tensor, items: torch.Tensor, max_tokens: int, out: torch.Tensor) -> torch.Tensor:
+        """out [n_items, rows / 2] fp32: per item, the column sums over its tokens of (silu(g) * u)^2, g and u this
+        gated layout's unrounded products (p2p_spmm_tc_grouped_gated_sums)."""
+        if not self.gated:
+            raise P2PError("gated sums need the interleaved gate / up layout")
+        call("p2p_spmm_tc_grouped_gated_sums", ptr(x), dtype_code(x), x.shape[0], self.cols, x.stride(0),
+             ptr(self.words), ptr(self.seg), self.layout_row_tiles, self.rows, self.item_row_tiles, self.seg_cap,
+             ptr(items), items.shape[0], max_tokens, ptr(out), out.stride(0), stream_of(x))
+        return out
+
     def nbytes(self) -> int:
         return self.words.numel() * 4 + self.seg.numel() * 8
 

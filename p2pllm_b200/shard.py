@@ -6,8 +6,8 @@ computes its rows of y, and y [T, rows] is assembled on every rank. Runs of rows
 earlier ranks taking the extra tile.
 
 Two ways to assemble y:
-  fused (the default on GPUs of one node): the bitmask-layout GEMM stores each of its rows of y straight into every
-      rank's y buffer (symmetric memory, plain stores over NVLink), and a bounded peer barrier (PeerGroup) makes them
+  fused (the default on GPUs of one node): the rank's tensor-core GEMM (either layout) stores each of its rows of y
+      straight into every rank's y buffer (symmetric memory, plain stores over NVLink), and a bounded peer barrier (PeerGroup) makes them
       visible -- the all-gather fused into the GEMM's epilogue, no separate collective, no copies;
   "nccl": the rank's GEMM writes its slot of a gather buffer, one NCCL all_gather_into_tensor collects the slots.
 
@@ -24,6 +24,7 @@ import torch
 import torch.distributed as dist
 
 from . import _lib, compact, kernels
+from ._lib import P2PError
 
 TILE_ROWS = 128
 
@@ -107,12 +108,13 @@ class PeerGroup:
 class ShardedCompact:
     """One rank's share of a compact module: its rows as a Compact, and apply() returning the whole y on every rank.
 
-    fused (the default with more than one rank): the rank's GEMM (bitmask layout) stores its rows of y into every
-    rank's y buffer over NVLink, then a peer barrier; y is a view of one of two symmetric buffers, used in turn, so it
+    fused (the default with more than one rank): the rank's GEMM (the tensor-core layout `layout`, the package's
+    default unless given) stores its rows of y into every rank's y buffer over NVLink, then a peer barrier; y is a view of one of two symmetric buffers, used in turn, so it
     stays valid until this module's next-but-one apply. Otherwise ("nccl"): the GEMM writes its slot of a gather
     buffer, and one all_gather_into_tensor over the process group collects the slots into y."""
 
-    def __init__(self, blocks: list, group=None, fused: bool | None = None, peers: PeerGroup | None = None):
+    def __init__(self, blocks: list, group=None, fused: bool | None = None, peers: PeerGroup | None = None,
+                 layout: str | None = None):
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
@@ -125,7 +127,7 @@ class ShardedCompact:
         self.local = None
         if stop > start:
             self.local = compact.Compact.__new__(compact.Compact)
-            self.local.tiles = compact.Tiles(mine, layout="mask" if self.fused else None)
+            self.local.tiles = compact.Tiles(mine, layout=layout)
         self.width = max(b - a for a, b in self.ranges)
         self.mine = stop - start
         self.peers = peers
@@ -149,8 +151,14 @@ class ShardedCompact:
         self._turn ^= 1
         if self.local is not None:
             t = self.local.tiles
-            kernels.spmm_mask_peers(x2, t.data, t.seg, self.mine, self.cols, ptrs, self.world, self.ranges[self.rank][0],
-                                    self.rows)
+            if t.layout == "tc":
+                kernels.spmm_tc_peers(x2, t.words, t.seg, self.mine, self.cols, t.seg_cap, ptrs, self.world,
+                                      self.ranges[self.rank][0], self.rows)
+            elif t.layout == "mask":
+                kernels.spmm_mask_peers(x2, t.data, t.seg, self.mine, self.cols, ptrs, self.world,
+                                        self.ranges[self.rank][0], self.rows)
+            else:
+                raise P2PError("the fused all-gather needs a tensor-core layout (tc or mask)")
         if sync:
             self.peers.barrier()
         return buf[:T]

@@ -18,15 +18,58 @@ def k_of(keep: float, cols: int) -> int:
     return max(1, round(keep / 100 * cols))
 
 
+def _gated_layout(m):
+    """The module's gate + up experts as one grouped layout whose GEMM squares and sums the gated activations (dense
+    rows: every weight kept), built at the first calibration call and kept on the module while its weights stay; None
+    when the shapes or dtypes do not fit the tensor-core kernel."""
+    from . import moe
+    w = m.w13_weight
+    key = (w.data_ptr(), tuple(w.shape), w.dtype)
+    cached = getattr(m, "_p2p_gated_layout", None)
+    if cached is not None and cached[0] == key:
+        return cached[1]
+    tiles = None
+    if (w.is_cuda and w.dtype in (torch.bfloat16, torch.float16) and w.dim() == 3 and w.shape[1] % 128 == 0
+            and w.shape[2] % 8 == 0 and w.shape[2] <= 256 * 64):
+        r = w.shape[1] // 2
+        tiles = moe.ExpertTiles([("dense", w[:, :r]), ("dense", w[:, r:])], gated=True)
+    m._p2p_gated_layout = (key, tiles)
+    return tiles
+
+
+def _distinct_experts(ids: torch.Tensor, n_exp: int) -> torch.Tensor:
+    """ids [T, K] with each token's repeated experts, and ids outside [0, n_exp), replaced by -1: a token counts once
+    for each expert it reaches."""
+    s = ids.sort(-1).values
+    bad = (s < 0) | (s >= n_exp)
+    bad[:, 1:] |= s[:, 1:] == s[:, :-1]
+    return torch.where(bad, torch.full_like(s, -1), s)
+
+
 def expert_inputs(m, x: torch.Tensor, ids: torch.Tensor) -> tuple:
     """Sums of squares of what a FusedMoE's experts read, per channel and over the tokens routed to each (each token
     once): for gate and up [expert, hidden], for down [expert, rows]. ids: each token's experts; ids outside
-    [0, experts) are skipped. p2p/wanda.py:10-20."""
+    [0, experts) are skipped. p2p/wanda.py:10-20.
+
+    The gated half runs on the grouped tensor-core GEMM when the experts are bf16 / f16 and x has their dtype: the
+    routed tokens sorted by expert (moe.route), one launch over all experts whose epilogue squares silu(g) * u and sums
+    it per item (fp32, the products exact), the items of an expert added in fp64. Otherwise an fp32 GEMM per expert."""
     n_exp, hidden = m.w13_weight.shape[0], m.w13_weight.shape[-1]
     into = torch.zeros(n_exp, hidden, dtype=torch.float64, device=x.device)
     gated = torch.zeros(m.w2_weight.shape[0], m.w2_weight.shape[-1], dtype=torch.float64, device=x.device)
     x2 = x.reshape(-1, hidden)
     kernels.expert_sumsq(x2, ids.reshape(x2.shape[0], -1), into)
+    tiles = _gated_layout(m) if x2.dtype == m.w13_weight.dtype else None
+    if tiles is not None:
+        from . import moe
+        flat = _distinct_experts(ids.reshape(x2.shape[0], -1), n_exp)
+        r = moe.route(flat, n_exp)
+        if r["order"].numel():
+            xs = x2.index_select(0, r["order"] // flat.shape[1]).contiguous()
+            sums = torch.empty(r["items"].shape[0], tiles.rows // 2, dtype=torch.float32, device=x.device)
+            tiles.gated_sums(xs, r["items"], r["most"], sums)
+            gated.index_add_(0, r["items"][:, 0].long(), sums.double())
+        return into, gated
     xf = x2.float()
     flat = ids.reshape(x2.shape[0], -1)
     for e in torch.unique(flat[(flat >= 0) & (flat < n_exp)]).tolist():

@@ -144,3 +144,34 @@ def test_grouped_gate_in_the_epilogue_matches_silu_between_launches():
     rel = float((got.double() - want.double()).norm() / want.double().norm())
     assert rel <= 1e-3, rel
     _check(got, _reference_moe(x, ids, w, w13, w2))
+
+
+def test_gated_expert_calibration_on_the_grouped_kernel():
+    """wanda.expert_inputs' gated half on the grouped GEMM (bf16 experts) against p2p/wanda.py:16-19 restated in torch
+    fp32 (a token routed twice to one expert counts once; experts past 120 never reached; one expert with more than 256
+    tokens, so two items)."""
+    import types
+    from p2pllm_b200 import wanda
+    E, R, H, T, K = 128, 768, 2048, 300, 8
+    g = torch.Generator(device="cuda").manual_seed(11)
+    w13 = (torch.randn(E, 2 * R, H, generator=g, device="cuda") * 0.05).bfloat16()
+    m = types.SimpleNamespace(w13_weight=w13, w2_weight=torch.zeros(E, H, R, device="cuda").bfloat16())
+    logits = torch.randn(T, E, generator=g, device="cuda")
+    logits[:, 120:] = -1e9
+    logits[:, 0] += 10
+    ids = logits.topk(K, dim=-1).indices
+    ids[::7, 1] = ids[::7, 0]                                # a repeated expert in some tokens
+    ids[::11, -1] = -1                                       # and slots routed nowhere
+    x = torch.randn(T, H, generator=g, device="cuda").bfloat16()
+    into, gated = wanda.expert_inputs(m, x, ids)
+    assert wanda._gated_layout(m) is not None
+    want = torch.zeros(E, R, dtype=torch.float64, device="cuda")
+    xf = x.float()
+    for e in range(E):
+        routed = xf[(ids == e).any(-1)]
+        if routed.shape[0] == 0:
+            continue
+        gate, up = (routed @ w13[e].float().T).chunk(2, -1)
+        want[e] = (torch.nn.functional.silu(gate) * up).pow(2).sum(0).double()
+    assert torch.allclose(gated, want, rtol=1e-4, atol=1e-9), float(((gated - want).abs() / want.abs().clamp_min(1e-9)).max())
+    assert (gated[120:] == 0).all()
