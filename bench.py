@@ -56,7 +56,7 @@ def parse():
     p.add_argument("--tokens", type=int, default=272)
     p.add_argument("--calib-tokens", type=int, default=128 * 2048)
     p.add_argument("--no-cpu-baseline", action="store_true")
-    p.add_argument("--workload", default="cfg2", choices=["cfg2", "cfg1", "cfg3", "cfg5", "module"],
+    p.add_argument("--workload", default="cfg2", choices=["cfg2", "cfg1", "cfg3", "cfg4", "cfg5", "module"],
                    help="cfg2 (default): the headline line. cfg1, cfg3, cfg5: one extra line each on one GPU (config "
                         "1's fp32 projection; config 3's replica block + group combine at T = 1, 8, 32, 64; a "
                         "Qwen2.5-32B replica layer at keep 40). module: one module of the cfg2 layer (--module, "
@@ -1136,6 +1136,41 @@ def run_extra(args):
         line.update(metric="config-3 replica member + combine tokens/s (keep 40 MLP block, hidden 4096)",
                     value=per_t[64]["tokens_per_s"], unit="tokens/s", per_tokens=per_t, dtype="bf16",
                     note="synthetic residual-MLP block stands in for a decoder layer (no KV cache here)")
+    elif args.workload == "cfg4":
+        # Routed experts: hidden 2048, 128 experts, top-8 of N(0,1) router logits, intermediate 768, keep 30, 272
+        # tokens; one pass of moe.GroupedMoE (route, gather, gate/up launch with SiLU * up in its epilogue, down
+        # launch, weighted combine), and the same pass with SiLU * up between the launches
+        from types import SimpleNamespace as NS
+        from p2pllm_b200 import moe
+        E, R, H, T, K = 128, 768, 2048, 272, 8
+        g = torch.Generator(device=device).manual_seed(4)
+        blocks = {}
+        for name, rows, cols in (("w13_weight", 2 * R, H), ("w2_weight", H, R)):
+            w = (torch.randn(E, rows, cols, generator=g, device=device) * 0.05).bfloat16()
+            norms = torch.rand(E, cols, generator=g, device=device) + 0.1
+            sel = [wanda.select(w[e], 30, norms[e]) for e in range(E)]
+            values, idx = torch.stack([s_[0] for s_ in sel]), torch.stack([s_[1] for s_ in sel])
+            if name == "w13_weight":
+                blocks[name] = [("compact", values[:, :R], idx[:, :R], cols), ("compact", values[:, R:], idx[:, R:], cols)]
+            else:
+                blocks[name] = [("compact", values, idx, cols)]
+            del w
+        fused = moe.GroupedMoE(None, blocks)
+        unfused = moe.GroupedMoE(None, blocks)
+        unfused.w13 = moe.ExpertTiles(blocks["w13_weight"])
+        wts, ids = torch.topk(torch.softmax(torch.randn(T, E, generator=g, device=device), -1), K)
+        d = NS(hidden_states=torch.randn(T, H, generator=g, device=device).bfloat16(),
+               topk_output=NS(topk_ids=ids, topk_weights=wts))
+        us = _timed_us(lambda: fused.apply(None, d), reps)
+        us_unfused = _timed_us(lambda: unfused.apply(None, d), reps)
+        used = int(torch.unique(ids).numel())
+        alg = sum(b[1].numel() * 4 for bl in blocks.values() for b in bl) * used // E + T * H * 2 * 2
+        line.update(metric="config-4 routed-expert pass tokens/s (128 experts, top-8, keep 30, T=272)",
+                    value=T / us * 1e6, unit="tokens/s", us_per_pass=us, us_per_pass_silu_between_launches=us_unfused,
+                    experts_reached=used, algorithmic_bytes=alg, hbm_gbs=alg / us / 1e3,
+                    frac=alg / us / 1e3 / peak["hbm_gbs"], dtype="bf16",
+                    kernel="moe.GroupedMoE: p2p_moe_route, p2p_spmm_tc_grouped_gated, p2p_spmm_tc_grouped, "
+                           "p2p_moe_combine")
     elif args.workload == "module":
         # one module of the cfg2 layer, --steps launches at --tokens tokens (each behind a spin), for profiling
         from p2pllm_b200 import compact as cp
