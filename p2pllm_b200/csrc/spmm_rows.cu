@@ -255,22 +255,34 @@ __global__ void __launch_bounds__(kStagedBlock, 1) spmm_rows_staged_kernel(const
         float acc[TT];
 #pragma unroll
         for (int t = 0; t < TT; ++t) acc[t] = 0.f;
-        for (int64_t e = (base & ~(int64_t)(VEC - 1)) + lane * VEC; e < end; e += 32 * VEC) {
-            float fv[VEC];
-            int ci[VEC];
-            load_step<T, I, VEC>(v, ix, e, fv, ci);
-            if (ix == nullptr) {
+        // kSteps steps of the row's values and indices in flight at once (one round trip a chunk, not one a step),
+        // then their products
+        constexpr int kSteps = (TT > 20 ? 16 : 32) / VEC;
+        for (int64_t e0 = (base & ~(int64_t)(VEC - 1)) + lane * VEC; e0 < end; e0 += (int64_t)kSteps * 32 * VEC) {
+            float fv[kSteps][VEC];
+            int ci[kSteps][VEC];
 #pragma unroll
-                for (int i = 0; i < VEC; ++i) ci[i] += (int)(e - base);
+            for (int st = 0; st < kSteps; ++st) {
+                const int64_t e = e0 + (int64_t)st * 32 * VEC;
+                if (e < end) load_step<T, I, VEC>(v, ix, e, fv[st], ci[st]);
             }
-            const bool whole = e >= base && e + VEC <= end;
 #pragma unroll
-            for (int i = 0; i < VEC; ++i) {
-                if (!whole && (e + i < base || e + i >= end)) continue;
-                const T* col = xs + min((unsigned)ci[i], cmax);
+            for (int st = 0; st < kSteps; ++st) {
+                const int64_t e = e0 + (int64_t)st * 32 * VEC;
+                if (e >= end) break;
+                if (ix == nullptr) {
 #pragma unroll
-                for (int t = 0; t < TT; ++t)
-                    if (t < tokens) acc[t] = fmaf(fv[i], to_f32(col[(size_t)t * cols]), acc[t]);
+                    for (int i = 0; i < VEC; ++i) ci[st][i] += (int)(e - base);
+                }
+                const bool whole = e >= base && e + VEC <= end;
+#pragma unroll
+                for (int i = 0; i < VEC; ++i) {
+                    if (!whole && (e + i < base || e + i >= end)) continue;
+                    const T* col = xs + min((unsigned)ci[st][i], cmax);
+#pragma unroll
+                    for (int t = 0; t < TT; ++t)
+                        if (t < tokens) acc[t] = fmaf(fv[st][i], to_f32(col[(size_t)t * cols]), acc[t]);
+                }
             }
         }
 #pragma unroll

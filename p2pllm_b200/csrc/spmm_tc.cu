@@ -109,6 +109,7 @@ struct TcParams {
     void* ys[8];
     int n_ys, vec4;
     int64_t y_col0;
+    int stage_peers;                  // unsplit: the tile staged in shared memory, then 16-byte stores to every ys[k]
 };
 
 // Four values of y row `yrow` from module row c0 on (rows past the module are not written): to y, or to every ys[k].
@@ -464,7 +465,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 if (t < tokens) {
                     if (p.gated && p.n_split == 1) {
                         reinterpret_cast<float*>(gbase)[t * tc::kTileRows + row_local] = v[j];   // rings are free
-                    } else if (p.y_tma) {
+                    } else if (p.y_tma || (kPeers && p.stage_peers)) {
                         reinterpret_cast<T*>(gbase)[t * tc::kTileRows + row_local] = from_f32<T>(v[j]);  // rings free
                     } else if (p.n_split == 1) {
                         if (row_ok) {
@@ -529,6 +530,26 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             store_gated<T>(y + (xrow0 + t) * p.ldy, c_base + r4, limit, g, up);
         }
         return;
+    }
+    if constexpr (kPeers) {
+        if (p.stage_peers) {
+            // The tile staged as [token][128 rows]: each token's 256 bytes go to every rank's y in 16-byte stores
+            // (16 threads a token), the last tile's rows past the module one value at a time.
+            const T* tile = reinterpret_cast<const T*>(gbase);
+            for (int q = threadIdx.x; q < tokens * 16; q += kTcThreads) {
+                const int t = q >> 4, c8 = (q & 15) * 8;
+                const int64_t at = (xrow0 + t) * p.ldy + p.y_col0 + col0 + c8;
+                if (col0 + c8 + 8 <= p.rows) {
+                    const uint4 raw = *reinterpret_cast<const uint4*>(tile + t * tc::kTileRows + c8);
+                    for (int k = 0; k < p.n_ys; ++k) *reinterpret_cast<uint4*>(reinterpret_cast<T*>(p.ys[k]) + at) = raw;
+                } else {
+                    for (int e = 0; e < 8 && col0 + c8 + e < p.rows; ++e)
+                        for (int k = 0; k < p.n_ys; ++k)
+                            reinterpret_cast<T*>(p.ys[k])[at + e] = tile[t * tc::kTileRows + c8 + e];
+                }
+            }
+            return;
+        }
     }
     if (p.y_tma) {
         // The tile of y staged as [token][128 rows] in shared memory goes out in one TMA store a box (rows past the
@@ -927,10 +948,14 @@ int spmm_tc_impl(const void* x, int dtype, int64_t tokens, int64_t cols, int64_t
         prm.n_ys = n_ys;
         prm.y_col0 = y_col0;
         prm.vec4 = ldy % 4 == 0 && y_col0 % 4 == 0;
+        bool al16 = ldy % 8 == 0 && y_col0 % 8 == 0;
         for (int k = 0; k < 8; ++k) {
             prm.ys[k] = k < n_ys ? reinterpret_cast<char*>(ys[k]) + t0 * ldy * elem : nullptr;
             if (k < n_ys && (reinterpret_cast<uintptr_t>(ys[k]) & 7)) prm.vec4 = 0;
+            if (k < n_ys && (reinterpret_cast<uintptr_t>(ys[k]) & 15)) al16 = false;
         }
+        prm.stage_peers = n_ys > 0 && pl.n_split == 1 && al16 &&
+                          (int64_t)pl.n_total * tc::kTileRows * 2 <= (int64_t)pl.a_slots * kASlotBytes;
         if (gated && pl.n_split == 1 &&
             (int64_t)pl.n_total * tc::kTileRows * 4 > (int64_t)pl.a_slots * kASlotBytes + (int64_t)pl.x_slots * pl.b_bytes)
             return fail(P2P_EUNSUPPORTED, "p2p_spmm_tc_gated: %d tokens do not fit the staged tile", tn);
@@ -1054,6 +1079,7 @@ int grouped_impl(const void* x, int dtype, int64_t x_rows, int64_t cols, int64_t
     prm.n_ys = 0;
     prm.vec4 = 0;
     prm.y_col0 = 0;
+    prm.stage_peers = 0;
     for (int k = 0; k < 8; ++k) prm.ys[k] = nullptr;
     if (gated && (int64_t)pl.n_total * tc::kTileRows * 4 + (gated == 2 ? 64 * 8 * 4 : 0) >
                      (int64_t)pl.a_slots * kASlotBytes + (int64_t)pl.x_slots * pl.b_bytes)
