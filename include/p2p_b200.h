@@ -144,15 +144,11 @@ typedef struct {
 
 /* y [tokens, ldy] (columns row0.. of each block) = x [tokens, cols] (row stride ldx) times the blocks' rows, fp32
  * sums, on CUDA cores straight from the row layout (values + column indices). Any token count. bf16, f16 or f32;
- * idx_bytes 2 or 4. cols * element size <= 200 KiB. Up to 32 tokens whose x fits 200 KiB (rows 16-byte aligned),
- * one block an SM stages all of x by bulk copies; otherwise blocks stage token tiles column-major.
+ * idx_bytes 2 or 4. cols * element size <= 200 KiB. Up to 32 tokens whose x fits 200 KiB, one block an SM stages all
+ * of x; otherwise blocks stage token tiles.
  * Replaces p2p/compact.cu:265-278 (spmm) for row-layout weights; p2p/compact.py:192-199 (Tiles.__call__). */
 int p2p_spmm_rows(const void* x, int dtype, int64_t tokens, int64_t cols, int64_t ldx, const p2p_row_block* blocks,
                   int nblocks, int idx_bytes, void* y, int64_t ldy, void* stream);
-
-/* P2P_OK unless a p2p_spmm_rows launch of at most 32 tokens (x staged whole by bulk copies) gave up waiting for its
- * copies since the last reset (P2P_ECUDA); reset != 0 clears it. Syncs the stream. No counterpart in the reference. */
-int p2p_spmm_rows_status(int reset, void* stream);
 
 /* The tensor-core layout of a module (bf16 / f16 weights): rows in tiles of 128, columns in tiles of 64; each
  * (row tile, column tile) segment holds its kept weights as 32-bit words (value bits << 16 | row << 6 | column, bit 13

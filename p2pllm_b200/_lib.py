@@ -41,7 +41,6 @@ SIGNATURES = {
     "p2p_unpack": ([_vp, _int, _i64, _i64, _i64, _vp, _i64, _vp, _int, _i64, _i64, _vp, _i64, _vp], _int),
     "p2p_check_idx": ([_vp, _int, _i64, _i64, _i64, _i64, _vp], _int),
     "p2p_spmm_rows": ([_vp, _int, _i64, _i64, _i64, ctypes.POINTER(RowBlock), _int, _int, _vp, _i64, _vp], _int),
-    "p2p_spmm_rows_status": ([_int, _vp], _int),
     "p2p_tiles_workspace": ([ctypes.POINTER(RowBlock), _int, _i64], _sz),
     "p2p_tiles_plan": ([ctypes.POINTER(RowBlock), _int, _int, _i64, _vp, ctypes.POINTER(_i64), _vp, _sz, _vp], _int),
     "p2p_tiles_fill": ([ctypes.POINTER(RowBlock), _int, _int, _i64, _int, _vp, _vp, _i64, _vp, _sz, _vp], _int),

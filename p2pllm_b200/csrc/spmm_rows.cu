@@ -11,13 +11,12 @@
 // shuffles. Blocks of the same rows but different token tiles are adjacent in launch order, so a row's weights come
 // from HBM once and from L2 for the other tiles.
 //
-// Few tokens (a draft pass of 16 + 1): one block per SM stages ALL of x at once, row-major, with one bulk copy
-// (cp.async.bulk, the TMA engine's untiled form) per token row completing on an mbarrier, while its warps prefetch
-// their first rows' weights into L2; then every warp of the grid takes whole rows in turn. x is read from L2 once per
-// SM instead of once per (token tile, row group) block, and each block does a share of the rows large enough to hide
-// the staging. The wait for the copies is bounded (2 s): past it the block records the failure
-// (p2p_spmm_rows_status) and returns without computing.
-#include "sm100.cuh"
+// Few tokens (a draft pass of 16 + 1): one block per SM stages ALL of x at once, column-major (each kept weight's
+// column for every token is a few 16-byte shared loads), while its warps prefetch their first rows' weights into L2;
+// then every warp of the grid takes whole rows in turn, each lane keeping a chunk of the row's loads in flight. x is
+// read from L2 once per SM instead of once per (token tile, row group) block. (Staging x row-major by bulk copies
+// was measured slower: a column then costs one shared load a token, with bank conflicts.)
+#include "common.cuh"
 
 namespace p2p {
 namespace {
@@ -190,35 +189,28 @@ constexpr int kStagedBlock = 512;
 constexpr int kStagedWarps = kStagedBlock / 32;
 constexpr int kStagedMaxTokens = 32;
 constexpr int kStagedSmem = 200 * 1024;
-constexpr uint64_t kStagedWaitNs = 2000000000ull;
 
-__device__ int g_rows_error;   // 1 once a staged block's wait for its copies of x gave up (since the last reset)
+// Token tiles of the staged kernel: fp32 columns in multiples of 4 tokens (16-byte loads), 2-byte ones of 8.
+template <typename T> constexpr int staged_step() { return sizeof(T) == 4 ? 4 : 8; }
+template <typename T> int staged_tt(int64_t tokens) {
+    const int q = staged_step<T>();
+    return (int)((tokens + q - 1) / q * q);
+}
 
-// y rows of the grid's warps, x [tokens <= TT, cols] staged row-major in shared memory (xs[t * cols + c]).
+// y rows of the grid's warps; x [tokens <= TT, cols] staged column-major in shared memory (xs[c * TT + t], zeros past
+// the tokens), so a kept weight's column for every token is TT / VEC 16-byte shared loads.
 template <typename T, typename I, int TT>
 __global__ void __launch_bounds__(kStagedBlock, 1) spmm_rows_staged_kernel(const T* __restrict__ x, int tokens,
                                                                            int cols, int64_t ldx, BlockTable bt,
                                                                            int64_t total_rows, T* __restrict__ y,
                                                                            int64_t ldy) {
     constexpr int VEC = 16 / sizeof(T);
-    extern __shared__ __align__(128) unsigned char smem_raw[];
-    __shared__ __align__(8) uint64_t bar;
-    __shared__ int go;
-    const T* xs = reinterpret_cast<const T*>(smem_raw);
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    T* xs = reinterpret_cast<T*>(smem_raw);
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const uint32_t b = sm100::smem_u32(&bar);
-    if (tid == 0) {
-        sm100::mbar_init(b, 1);
-        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        const uint32_t row_bytes = (uint32_t)cols * sizeof(T);
-        sm100::mbar_expect_tx(b, row_bytes * (uint32_t)tokens);
-        const uint32_t dst = sm100::smem_u32(smem_raw);
-        for (int t = 0; t < tokens; ++t) sm100::bulk_load(dst + t * row_bytes, x + t * ldx, row_bytes, b);
-    }
-    // while x lands: the first row of this warp, into L2 (a 128-byte line a lane)
     const int64_t gw = (int64_t)blockIdx.x * kStagedWarps + warp;
     const int64_t stride = (int64_t)gridDim.x * kStagedWarps;
+    // the first row of this warp, into L2 (a 128-byte line a lane), while x is staged
     if (gw < total_rows) {
         int bi = 0;
         while (bi + 1 < bt.n && gw >= bt.start[bi + 1]) ++bi;
@@ -233,15 +225,14 @@ __global__ void __launch_bounds__(kStagedBlock, 1) spmm_rows_staged_kernel(const
                 asm volatile("prefetch.global.L2 [%0];" ::"l"(ix + off));
         }
     }
-    if (tid == 0) {
-        bool ok = sm100::mbar_try(b, 0);
-        const uint64_t t0 = sm100::now_ns();
-        while (!ok && sm100::now_ns() - t0 < kStagedWaitNs) ok = sm100::mbar_try(b, 0);
-        if (!ok) atomicExch(&g_rows_error, 1);
-        go = ok;
+    // stage: one column a thread (a warp reads 32 consecutive columns of a token row), one vector store
+    for (int c = tid; c < cols; c += kStagedBlock) {
+        XCol<T, TT> col;
+#pragma unroll
+        for (int t = 0; t < TT; ++t) col.v[t] = t < tokens ? x[t * ldx + c] : from_f32<T>(0.f);
+        reinterpret_cast<XCol<T, TT>*>(xs)[c] = col;
     }
     __syncthreads();
-    if (!go) return;
 
     const unsigned cmax = (unsigned)(cols - 1);
     for (int64_t r = gw; r < total_rows; r += stride) {
@@ -255,9 +246,8 @@ __global__ void __launch_bounds__(kStagedBlock, 1) spmm_rows_staged_kernel(const
         float acc[TT];
 #pragma unroll
         for (int t = 0; t < TT; ++t) acc[t] = 0.f;
-        // kSteps steps of the row's values and indices in flight at once (one round trip a chunk, not one a step),
-        // then their products
-        constexpr int kSteps = (TT > 20 ? 16 : 32) / VEC;
+        // kSteps steps of the row's values and indices in flight at once, then their products
+        constexpr int kSteps = (TT >= 32 ? 8 : TT >= 16 ? 16 : 32) / VEC;
         for (int64_t e0 = (base & ~(int64_t)(VEC - 1)) + lane * VEC; e0 < end; e0 += (int64_t)kSteps * 32 * VEC) {
             float fv[kSteps][VEC];
             int ci[kSteps][VEC];
@@ -278,10 +268,10 @@ __global__ void __launch_bounds__(kStagedBlock, 1) spmm_rows_staged_kernel(const
 #pragma unroll
                 for (int i = 0; i < VEC; ++i) {
                     if (!whole && (e + i < base || e + i >= end)) continue;
-                    const T* col = xs + min((unsigned)ci[st][i], cmax);
+                    float xv[TT];
+                    gather<T, TT>(xs, (int)min((unsigned)ci[st][i], cmax), xv);
 #pragma unroll
-                    for (int t = 0; t < TT; ++t)
-                        if (t < tokens) acc[t] = fmaf(fv[st][i], to_f32(col[(size_t)t * cols]), acc[t]);
+                    for (int t = 0; t < TT; ++t) acc[t] = fmaf(fv[st][i], xv[t], acc[t]);
                 }
             }
         }
@@ -298,18 +288,17 @@ __global__ void __launch_bounds__(kStagedBlock, 1) spmm_rows_staged_kernel(const
     }
 }
 
-// The staged kernel takes the launch when all tokens fit one block's shared memory and x's rows are 16-byte aligned.
+// The staged kernel takes the launch when all tokens (padded to its token step) fit one block's shared memory.
 template <typename T>
-bool staged_fits(const void* x, int64_t tokens, int64_t cols, int64_t ldx) {
-    return tokens >= 1 && tokens <= kStagedMaxTokens && tokens * cols * (int64_t)sizeof(T) <= kStagedSmem &&
-           (cols * (int64_t)sizeof(T)) % 16 == 0 && (ldx * (int64_t)sizeof(T)) % 16 == 0 && aligned16(x);
+bool staged_fits(int64_t tokens, int64_t cols) {
+    return tokens >= 1 && tokens <= kStagedMaxTokens && cols * staged_tt<T>(tokens) * (int64_t)sizeof(T) <= kStagedSmem;
 }
 
 template <typename T, typename I, int TT>
 int launch_staged(const void* x, int64_t tokens, int64_t cols, int64_t ldx, const BlockTable& bt, int64_t total_rows,
                   void* y, int64_t ldy, cudaStream_t s) {
     auto kern = spmm_rows_staged_kernel<T, I, TT>;
-    const int smem = (int)(tokens * cols * sizeof(T));
+    const int smem = (int)(cols * TT * sizeof(T));
     if (int e = allow_smem((const void*)kern, kStagedSmem, "p2p_spmm_rows")) return e;
     const int64_t want = (total_rows + kStagedWarps - 1) / kStagedWarps;
     const int grid = (int)(want < sm_count() ? want : sm_count());
@@ -321,11 +310,22 @@ int launch_staged(const void* x, int64_t tokens, int64_t cols, int64_t ldx, cons
 template <typename T, typename I>
 int dispatch_staged(const void* x, int64_t tokens, int64_t cols, int64_t ldx, const BlockTable& bt, int64_t total_rows,
                     void* y, int64_t ldy, cudaStream_t s) {
-    if (tokens <= 4) return launch_staged<T, I, 4>(x, tokens, cols, ldx, bt, total_rows, y, ldy, s);
-    if (tokens <= 8) return launch_staged<T, I, 8>(x, tokens, cols, ldx, bt, total_rows, y, ldy, s);
-    if (tokens <= 16) return launch_staged<T, I, 16>(x, tokens, cols, ldx, bt, total_rows, y, ldy, s);
-    if (tokens <= 20) return launch_staged<T, I, 20>(x, tokens, cols, ldx, bt, total_rows, y, ldy, s);
-    return launch_staged<T, I, 32>(x, tokens, cols, ldx, bt, total_rows, y, ldy, s);
+    switch (staged_tt<T>(tokens)) {
+        case 4: if constexpr (sizeof(T) == 4) return launch_staged<T, I, 4>(x, tokens, cols, ldx, bt, total_rows, y, ldy, s);
+                break;
+        case 8: return launch_staged<T, I, 8>(x, tokens, cols, ldx, bt, total_rows, y, ldy, s);
+        case 12: if constexpr (sizeof(T) == 4) return launch_staged<T, I, 12>(x, tokens, cols, ldx, bt, total_rows, y, ldy, s);
+                 break;
+        case 16: return launch_staged<T, I, 16>(x, tokens, cols, ldx, bt, total_rows, y, ldy, s);
+        case 20: if constexpr (sizeof(T) == 4) return launch_staged<T, I, 20>(x, tokens, cols, ldx, bt, total_rows, y, ldy, s);
+                 break;
+        case 24: return launch_staged<T, I, 24>(x, tokens, cols, ldx, bt, total_rows, y, ldy, s);
+        case 28: if constexpr (sizeof(T) == 4) return launch_staged<T, I, 28>(x, tokens, cols, ldx, bt, total_rows, y, ldy, s);
+                 break;
+        case 32: return launch_staged<T, I, 32>(x, tokens, cols, ldx, bt, total_rows, y, ldy, s);
+        default: break;
+    }
+    return fail(P2P_EINVAL, "p2p_spmm_rows: no staged tile for %lld tokens", (long long)tokens);
 }
 
 template <typename T, typename I, int TT>
@@ -412,27 +412,12 @@ extern "C" int p2p_spmm_rows(const void* x, int dtype, int64_t tokens, int64_t c
                 (long long)ldy);
     cudaStream_t s = as_stream(stream);
     P2P_DISPATCH(dtype, {
-        if (staged_fits<scalar_t>(x, tokens, cols, ldx)) {
+        if (staged_fits<scalar_t>(tokens, cols)) {
             if (idx_bytes == 2) return dispatch_staged<scalar_t, int16_t>(x, tokens, cols, ldx, bt, total, y, ldy, s);
             return dispatch_staged<scalar_t, int32_t>(x, tokens, cols, ldx, bt, total, y, ldy, s);
         }
         if (idx_bytes == 2) return dispatch_tt<scalar_t, int16_t>(x, tokens, cols, ldx, bt, total, y, ldy, s);
         return dispatch_tt<scalar_t, int32_t>(x, tokens, cols, ldx, bt, total, y, ldy, s);
     });
-    return P2P_OK;
-}
-
-extern "C" int p2p_spmm_rows_status(int reset, void* stream) {
-    cudaStream_t st = as_stream(stream);
-    int v = 0;
-    if (cudaMemcpyFromSymbolAsync(&v, g_rows_error, sizeof(int), 0, cudaMemcpyDeviceToHost, st) != cudaSuccess ||
-        cudaStreamSynchronize(st) != cudaSuccess)
-        return fail(P2P_ECUDA, "p2p_spmm_rows_status: %s", cudaGetErrorString(cudaGetLastError()));
-    if (reset && v) {
-        const int zero = 0;
-        cudaMemcpyToSymbolAsync(g_rows_error, &zero, sizeof(int), 0, cudaMemcpyHostToDevice, st);
-        cudaStreamSynchronize(st);
-    }
-    if (v) return fail(P2P_ECUDA, "p2p_spmm_rows: a block's wait for its staged x gave up");
     return P2P_OK;
 }
