@@ -336,16 +336,16 @@ int p2p_member_part(const void* y, const void* x, void* out, int dtype, int64_t 
  * combine of p2p_combine over parts, h and h_copy. */
 enum { P2P_PART_SUM = 0, P2P_PART_DIFF = 1, P2P_PART_COMBINE = 2 };
 
-/* Bytes of one rank's hop inbox: 256 bytes of counters, then n_ranks x ring slots of cap_elems elements (each slot
- * rounded up to 256 bytes). Allocate it where every rank of the node addresses it (symmetric memory or CUDA IPC),
+/* Bytes of one rank's hop inbox: 256 bytes of counters, then n_ranks x ring slots of cap_elems elements (each 32 bits
+ * of a part stored as a 64-bit word with the pass's flag, so a slot takes twice the part's bytes, rounded up to 256). Allocate it where every rank of the node addresses it (symmetric memory or CUDA IPC),
  * zeroed before the first hop; 0 for arguments out of range (1..8 ranks, 1..64 slots). */
 size_t p2p_hop_inbox_bytes(int n_ranks, int64_t cap_elems, int dtype, int ring);
 
 /* Sender side of the hop of pass `pass` (0, 1, 2, ... per sender and receiver pair; read from device memory at
  * *pass_at instead when pass_at is not null, so a CUDA graph can replay the hop pass after pass): computes this
  * rank's part (mode above) of n_elem elements and stores it into slot [me][pass % ring] of the inbox of every rank in dsts
- * (inboxes[r]: rank r's inbox as this GPU addresses it), then signals each of them. Before storing it waits until
- * each destination has consumed pass - ring of this rank. n_elem * element size a multiple of 16 bytes, at most
+ * (inboxes[r]: rank r's inbox as this GPU addresses it) as flagged words, so no separate signal follows. Before
+ * storing it waits until each destination has consumed pass - ring of this rank. n_elem * element size a multiple of 16 bytes, at most
  * cap_elems; parts, h, h_copy 16-byte aligned. Waits are bounded by wait_us (1 ms .. 60 s); a wait that gives up is
  * reported by p2p_hop_status. Replaces p2p/route.py:800-810 (_send_piece, one NCCL isend per destination) with the
  * part of p2p/route.py:1268-1274 (_member) or the combine of p2p/replica.py:81-85 computed in the same pass. */

@@ -4,23 +4,26 @@
 //
 // Every rank owns an inbox in memory that every rank of the job addresses (a symmetric allocation):
 //
-//   [0, 128)     arrived[n_ranks]  u32: + 1 for every sender CTA that has finished storing a pass (index: sender rank)
 //   [128, 256)   freed[n_ranks]    u32: + 1 for every receiver CTA that has consumed a pass of ours (index: receiver)
-//   [256, ...)   slots[n_ranks][ring][slot_bytes]: the part of sender s for pass p sits in slot [s][p % ring]
+//   [256, ...)   slots[n_ranks][ring][slot_bytes]: the part of sender s for pass p sits in slot [s][p % ring], every
+//                32 bits of it as one 64-bit word whose upper half is the flag p + 1
 //
 // p2p_hop_send (one launch on the sender): each CTA first waits until every destination has consumed pass
 // p - ring of this sender (so the slot is free), then computes its share of the part -- a copy or fp32 sum of parts,
 // a member's difference dtype(y - x), or the whole group combine of p2p/replica.py:81-85 -- and stores it straight
-// into every destination's slot over NVLink; then, after a CTA barrier, one thread fences (acquire-release, system
-// scope) and adds 1 to every destination's arrived[me] with a release. p2p_hop_recv (one launch on the receiver): each CTA waits until arrived[s] shows all
-// of pass p from every source s, adds the parts in fp32 in member order into `out` (rounded once, to the model dtype),
-// and adds 1 to every source's freed[me]. Both kernels run hop_grid(n) CTAs, so a pass is complete at
-// (p + 1) * grid arrivals; counters only grow (compared modulo 2^32).
+// into every destination's slot over NVLink as flagged words. No fence and no counter: a 64-bit word is written at
+// once, so the receiver knows a word has arrived when it carries this pass's flag. p2p_hop_recv (one launch on the
+// receiver): each thread polls its own words until they carry the flag (so the work starts as the data lands, word
+// by word), adds the parts in fp32 in member order into `out` (rounded once, to the model dtype), and after a CTA
+// barrier one thread frees the slots (adds 1 to every source's freed[me] with a release). Both kernels run
+// hop_grid(n) CTAs, so a pass is freed at (p + 1) * grid; counters only grow (compared modulo 2^32). Slots take
+// twice the part's bytes.
 //
-// Every wait is bounded (%globaltimer): past its limit the CTA records the site and the rank it gave up on and returns
-// without storing or signalling, so the peer's own wait runs out too and both hosts read an error from p2p_hop_status
-// instead of a hang; every later hop on that GPU then returns at once until the status is reset. A sender and its receiver must run on different GPUs (one process per GPU), or, on one GPU, in
-// stream order with the send first -- a wait that depends on a later launch on the same GPU is never made.
+// Every wait is bounded (%globaltimer): past its limit the thread records the site and the rank it gave up on and
+// returns without storing or signalling, so the peer's own wait runs out too and both hosts read an error from
+// p2p_hop_status instead of a hang; every later hop on that GPU then returns at once until the status is reset.
+// A sender and its receiver must run on different GPUs (one process per GPU), or, on one GPU, in stream order with
+// the send first -- a wait that depends on a later launch on the same GPU is never made.
 #include "elementwise.cuh"
 
 namespace p2p {
@@ -28,7 +31,6 @@ namespace {
 
 constexpr int kHopBlock = 256;
 constexpr int kHopRanks = 8;
-constexpr int kArrivedAt = 0;
 constexpr int kFreedAt = 128;
 constexpr int kSlotsAt = 256;
 constexpr int kMaxHopCtas = 128;
@@ -97,16 +99,17 @@ __global__ void __launch_bounds__(kHopBlock) hop_send_kernel(const __grid_consta
     __syncthreads();
     if (!go) return;
     const int64_t slot = kSlotsAt + ((int64_t)me * ring + (int64_t)(pass % (uint32_t)ring)) * slot_bytes;
+    const uint64_t flag = (uint64_t)(pass + 1u) << 32;
     for (int64_t v = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; v < n_vec; v += (int64_t)gridDim.x * blockDim.x) {
         float total[VEC];
         member_value<T, VEC, MODE>(parts, h, hc, v * VEC, total);
         const uint4 raw = pack_vec<T, VEC>(total);
-        for (int d = 0; d < dst.n; ++d) *reinterpret_cast<uint4*>(dst.inbox[d] + slot + v * 16) = raw;
-    }
-    __syncthreads();                            // every thread's stores of the part happen before the signal
-    if (threadIdx.x == 0) {
-        asm volatile("fence.acq_rel.sys;" ::: "memory");
-        for (int d = 0; d < dst.n; ++d) signal(reinterpret_cast<uint32_t*>(dst.inbox[d] + kArrivedAt) + me);
+        const uint64_t w0 = flag | raw.x, w1 = flag | raw.y, w2 = flag | raw.z, w3 = flag | raw.w;
+        for (int d = 0; d < dst.n; ++d) {
+            char* at = dst.inbox[d] + slot + v * 32;
+            asm volatile("st.relaxed.sys.global.v2.u64 [%0], {%1, %2};" ::"l"(at), "l"(w0), "l"(w1) : "memory");
+            asm volatile("st.relaxed.sys.global.v2.u64 [%0], {%1, %2};" ::"l"(at + 16), "l"(w2), "l"(w3) : "memory");
+        }
     }
 }
 
@@ -117,25 +120,37 @@ __global__ void __launch_bounds__(kHopBlock) hop_recv_kernel(const __grid_consta
                                                               int64_t n_vec, void* __restrict__ out, uint64_t wait_ns) {
     constexpr int VEC = 16 / sizeof(T);
     const uint32_t pass = pass_at ? *pass_at : pass_arg;
-    __shared__ int go;
-    if (threadIdx.x == 0) {
-        const uint32_t target = (pass + 1u) * gridDim.x;
-        bool ok = !hop_failed();
-        for (int s = 0; s < src.n && ok; ++s) {
-            ok = wait_count(reinterpret_cast<const uint32_t*>(my_inbox + kArrivedAt) + src.rank[s], target, wait_ns);
-            if (!ok) gave_up(2, src.rank[s]);
-        }
-        go = ok;
-    }
+    __shared__ int failed;
+    if (threadIdx.x == 0) failed = hop_failed();
     __syncthreads();
-    if (!go) return;
+    if (failed) return;
     const int64_t ring_at = (int64_t)(pass % (uint32_t)ring) * slot_bytes;
-    for (int64_t v = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; v < n_vec; v += (int64_t)gridDim.x * blockDim.x) {
+    const uint32_t want = pass + 1u;
+    bool ok = true;
+    for (int64_t v = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; v < n_vec && ok; v += (int64_t)gridDim.x * blockDim.x) {
         float total[VEC];
-        for (int s = 0; s < src.n; ++s) {
-            // written by peers over NVLink: read through L2 (.cg), never from a stale L1 line
-            const uint4 raw = __ldcg(reinterpret_cast<const uint4*>(
-                my_inbox + kSlotsAt + (int64_t)src.rank[s] * ring * slot_bytes + ring_at + v * 16));
+        for (int s = 0; s < src.n && ok; ++s) {
+            // four flagged words: each 64-bit word is written at once, so a word whose flag is this pass's carries
+            // this pass's 32 bits of data
+            const char* at = my_inbox + kSlotsAt + (int64_t)src.rank[s] * ring * slot_bytes + ring_at + v * 32;
+            uint64_t w0, w1, w2, w3;
+            uint64_t t0 = 0;
+            for (;;) {
+                asm volatile("ld.relaxed.sys.global.v2.u64 {%0, %1}, [%2];" : "=l"(w0), "=l"(w1) : "l"(at) : "memory");
+                asm volatile("ld.relaxed.sys.global.v2.u64 {%0, %1}, [%2];" : "=l"(w2), "=l"(w3) : "l"(at + 16) : "memory");
+                if ((uint32_t)(w0 >> 32) == want && (uint32_t)(w1 >> 32) == want && (uint32_t)(w2 >> 32) == want &&
+                    (uint32_t)(w3 >> 32) == want)
+                    break;
+                const uint64_t now = hop_now();
+                if (t0 == 0) t0 = now;
+                if (now - t0 > wait_ns || hop_failed()) {
+                    gave_up(2, src.rank[s]);
+                    ok = false;
+                    break;
+                }
+            }
+            if (!ok) break;
+            const uint4 raw = make_uint4((uint32_t)w0, (uint32_t)w1, (uint32_t)w2, (uint32_t)w3);
             const T* e = reinterpret_cast<const T*>(&raw);
             if (s == 0) {
 #pragma unroll
@@ -145,10 +160,11 @@ __global__ void __launch_bounds__(kHopBlock) hop_recv_kernel(const __grid_consta
                 for (int q = 0; q < VEC; ++q) total[q] += to_f32(e[q]);
             }
         }
-        store_vec<T, VEC>(out, v * VEC, total);
+        if (ok) store_vec<T, VEC>(out, v * VEC, total);
     }
+    if (!ok) atomicExch(&failed, 1);
     __syncthreads();                            // every read of the slots is done before the slots are freed
-    if (threadIdx.x == 0) {
+    if (threadIdx.x == 0 && !failed) {
         asm volatile("fence.acq_rel.sys;" ::: "memory");
         for (int s = 0; s < src.n; ++s) signal(reinterpret_cast<uint32_t*>(src.inbox[s] + kFreedAt) + me);
     }
@@ -158,7 +174,8 @@ __global__ void hop_advance_kernel(uint32_t* counters, int n) {
     if ((int)threadIdx.x < n) counters[threadIdx.x] += 1u;
 }
 
-int64_t slot_bytes_of(int64_t cap_elems, int dtype) { return (cap_elems * dtype_size(dtype) + 255) / 256 * 256; }
+// A slot holds every 32 bits of a part as one 64-bit word with the pass's flag in its upper half.
+int64_t slot_bytes_of(int64_t cap_elems, int dtype) { return (cap_elems * dtype_size(dtype) * 2 + 255) / 256 * 256; }
 
 // CTAs of a hop over n elements (the same on both sides, so a pass is complete at (p + 1) * grid arrivals).
 int hop_grid(int64_t n_elem, int dtype) {
