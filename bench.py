@@ -804,7 +804,7 @@ def run_sharded(args, layer, rank, world, device, peaks):
                            "copies its own columns of y back to pinned host memory on an output stream overlapping "
                            "the next step",
                     "d2h_mb_per_step": d2h / 1e6},
-            "gpu_launches": args.steps * (len(names) + 1),
+            "gpu_launches": args.steps * (len(names) + 1) * world,
             "clocks": clocks.summary(),
         }
         print(json.dumps(out), flush=True)
