@@ -64,6 +64,9 @@ def parse():
     p.add_argument("--module", default="gate_up_proj", choices=list(MODULES))
     p.add_argument("--layout", default=None, choices=["tc", "mask"],
                    help="the tensor-core layout of the compact modules (default: the package's)")
+    p.add_argument("--push", default="auto", choices=["auto", "on", "off"],
+                   help="row sharding: the rank's rows to its peers by a push kernel after the GEMM (on, the "
+                        "default), or from the GEMM's epilogue (off)")
     p.add_argument("--pass-tokens", type=int, default=17,
                    help="cfg5: tokens of a pass (a draft pass of 16 + 1 by default)")
     p.add_argument("--cfg5-single-layer", action="store_true",
@@ -601,7 +604,9 @@ def run_sharded(args, layer, rank, world, device, peaks):
     names = list(MODULES)
     blocks = {m: [("compact", *layer.selected[n], layer.proj[n].cols) for n in MODULES[m][1]] for m in names}
     peers = shard.PeerGroup(None, device)
-    sharded = {m: shard.ShardedCompact(blocks[m], fused=True, peers=peers, layout=args.layout) for m in names}
+    push = None if args.push == "auto" else args.push == "on"
+    sharded = {m: shard.ShardedCompact(blocks[m], fused=True, peers=peers, layout=args.layout, push=push)
+               for m in names}
     for m in names:
         sharded[m].prepare(args.tokens, torch.bfloat16, device)
     xs = {m: layer.inputs[MODULES[m][0]] for m in names}
@@ -779,13 +784,15 @@ def run_sharded(args, layer, rank, world, device, peaks):
                                    f"T={args.tokens}", "tokens": args.tokens,
                        "layout": sharded[names[0]].local.tiles.layout,
                        "parallelism": f"row-sharded over {world} GPUs (whole 128-row tiles of every module a rank, "
-                                      "full x); y gathered in the GEMM's epilogue by peer stores over NVLink, one "
-                                      "bounded peer barrier a step",
+                                      "full x); " + ("each rank's rows pushed to every peer's y by one kernel after "
+                                                     "its GEMM" if sharded[names[0]].push else
+                                                     "y gathered in the GEMM's epilogue by peer stores") +
+                                      " over NVLink, one bounded peer barrier a step",
                        "l2": "inputs larger than L2: each rank cycles through %d copies of its %.0f MB of shard "
                              "weights (%.0f MB) vs %d MB L2" % (copies, shard_bytes / 1e6, copies * shard_bytes / 1e6,
                                                                 L2_BYTES >> 20)},
             "parity": {"passed": True, "checks": checks},
-            "breakdown_us_per_step": {"fused_gemms": kern_ms / args.steps * 1e3,
+            "breakdown_us_per_step": {"gemms_and_gather": kern_ms / args.steps * 1e3,
                                       "barrier_and_skew": (total_ms - kern_ms) / args.steps * 1e3,
                                       "step": ms_per_step * 1e3},
             "nccl_path": {"ms_per_step": nccl_ms / args.steps, "all_gathers_us": gath_ms / args.steps * 1e3,

@@ -305,6 +305,15 @@ int p2p_spmm_tc_withhold(const void* x, int dtype, int64_t tokens, int64_t cols,
  * No counterpart in the reference (its hops go through NCCL send/recv, p2p/route.py:798-831). */
 int p2p_peer_barrier(void* const* flags, int n_ranks, int me, uint32_t epoch, int64_t timeout_us, void* stream);
 
+/* The all-gather of a row-sharded module as a push: columns col0 .. col0 + width - 1 of the first `tokens` rows of
+ * this rank's y [.., ldy] (its own rows of the module, written there by its GEMM) stored into the same place of each
+ * of the n_peers (0..7) other ranks' y buffers (peer memory), 16-byte loads and stores over all SMs. Column offsets,
+ * width and ldy in elements, 16-byte aligned. The peers read the columns after a p2p_peer_barrier that follows on
+ * every rank. The form of the fused all-gather for many ranks, where storing every value to every rank from the
+ * GEMM's epilogue would lengthen it N-fold. No counterpart in the reference. */
+int p2p_peer_push(const void* y, void* const* peers, int n_peers, int64_t tokens, int64_t col0, int64_t width,
+                  int64_t ldy, int dtype, void* stream);
+
 /* P2P_OK unless a p2p_peer_barrier since the last reset gave up (P2P_ECUDA, naming the rank); reset != 0 clears it.
  * Syncs the stream. */
 int p2p_peer_status(int reset, void* stream);

@@ -54,6 +54,7 @@ SIGNATURES = {
                              _sz, _vp], _int),
     "p2p_peer_barrier": ([ctypes.POINTER(_vp), _int, _int, ctypes.c_uint32, _i64, _vp], _int),
     "p2p_peer_status": ([_int, _vp], _int),
+    "p2p_peer_push": ([_vp, ctypes.POINTER(_vp), _int, _i64, _i64, _i64, _i64, _int, _vp], _int),
     "p2p_hop_inbox_bytes": ([_int, _i64, _int, _int], _sz),
     "p2p_hop_send": ([_int, ctypes.POINTER(_vp), _int, _vp, _vp, _int, _i64, ctypes.POINTER(_vp), _int, _int,
                       ctypes.POINTER(_int), _int, ctypes.c_uint32, _vp, _int, _i64, _i64, _vp], _int),

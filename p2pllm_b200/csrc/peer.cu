@@ -51,10 +51,54 @@ __global__ void peer_barrier_kernel(PeerFlags f, int n, int me, uint32_t epoch, 
     }
 }
 
+struct PushDst {
+    char* y[kMaxRanks];   // the other ranks' y buffers, as this GPU addresses them
+    int n;
+};
+
+// Columns [col0, col0 + width) of tokens rows of y (row stride ld elements) from this rank's buffer to every other
+// rank's: 16-byte loads and stores, the grid striding over (row, 16-byte chunk) pairs, each chunk to every peer.
+__global__ void __launch_bounds__(256) peer_push_kernel(const char* __restrict__ src, const __grid_constant__ PushDst dst,
+                                                        int64_t tokens, int64_t row_bytes, int64_t ld_bytes,
+                                                        int64_t col0_bytes) {
+    const int64_t chunks = row_bytes / 16;
+    const int64_t total = tokens * chunks;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t t = i / chunks, c = i - t * chunks;
+        const int64_t at = t * ld_bytes + col0_bytes + c * 16;
+        const uint4 v = *reinterpret_cast<const uint4*>(src + at);
+        for (int k = 0; k < dst.n; ++k) *reinterpret_cast<uint4*>(dst.y[k] + at) = v;
+    }
+}
+
 }  // namespace
 }  // namespace p2p
 
 using namespace p2p;
+
+extern "C" int p2p_peer_push(const void* y, void* const* peers, int n_peers, int64_t tokens, int64_t col0,
+                             int64_t width, int64_t ldy, int dtype, void* stream) {
+    P2P_REQUIRE(y && peers && n_peers >= 0 && n_peers < kMaxRanks, "p2p_peer_push: 0 to %d peers", kMaxRanks - 1);
+    P2P_REQUIRE(dtype_ok(dtype) && tokens >= 0 && col0 >= 0 && width >= 0 && col0 + width <= ldy,
+                "p2p_peer_push: columns %lld.. (%lld) of rows of %lld", (long long)col0, (long long)width,
+                (long long)ldy);
+    const int64_t es = dtype_size(dtype);
+    P2P_REQUIRE((col0 * es) % 16 == 0 && (width * es) % 16 == 0 && (ldy * es) % 16 == 0 && aligned16(y),
+                "p2p_peer_push: the columns, the row stride and y must be 16-byte aligned");
+    if (tokens == 0 || width == 0 || n_peers == 0) return P2P_OK;
+    PushDst d = {};
+    d.n = n_peers;
+    for (int k = 0; k < n_peers; ++k) {
+        P2P_REQUIRE(peers[k] && aligned16(peers[k]), "p2p_peer_push: peer buffer %d is null or misaligned", k);
+        d.y[k] = reinterpret_cast<char*>(peers[k]);
+    }
+    const int64_t total = tokens * (width * es / 16);
+    const int64_t want = (total + 255) / 256;
+    const int64_t cap = (int64_t)sm_count() * 4;
+    peer_push_kernel<<<(unsigned)(want < cap ? want : cap), 256, 0, as_stream(stream)>>>(
+        reinterpret_cast<const char*>(y), d, tokens, width * es, ldy * es, col0 * es);
+    return launch_status("p2p_peer_push");
+}
 
 extern "C" int p2p_peer_barrier(void* const* flags, int n_ranks, int me, uint32_t epoch, int64_t timeout_us,
                                 void* stream) {

@@ -225,12 +225,18 @@ __global__ void __launch_bounds__(kStagedBlock, 1) spmm_rows_staged_kernel(const
                 asm volatile("prefetch.global.L2 [%0];" ::"l"(ix + off));
         }
     }
-    // stage: one column a thread (a warp reads 32 consecutive columns of a token row), one vector store
-    for (int c = tid; c < cols; c += kStagedBlock) {
-        XCol<T, TT> col;
+    // stage: one column a thread (a warp reads 32 consecutive columns of a token row), one vector store; two columns
+    // a thread at a time, so that all their loads are in flight together
+    for (int c = tid; c < cols; c += 2 * kStagedBlock) {
+        const int c2 = c + kStagedBlock;
+        XCol<T, TT> col, col2;
 #pragma unroll
-        for (int t = 0; t < TT; ++t) col.v[t] = t < tokens ? x[t * ldx + c] : from_f32<T>(0.f);
+        for (int t = 0; t < TT; ++t) {
+            col.v[t] = t < tokens ? x[t * ldx + c] : from_f32<T>(0.f);
+            col2.v[t] = (t < tokens && c2 < cols) ? x[t * ldx + c2] : from_f32<T>(0.f);
+        }
         reinterpret_cast<XCol<T, TT>*>(xs)[c] = col;
+        if (c2 < cols) reinterpret_cast<XCol<T, TT>*>(xs)[c2] = col2;
     }
     __syncthreads();
 

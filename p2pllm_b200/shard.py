@@ -6,9 +6,10 @@ computes its rows of y, and y [T, rows] is assembled on every rank. Runs of rows
 earlier ranks taking the extra tile.
 
 Two ways to assemble y:
-  fused (the default on GPUs of one node): the rank's tensor-core GEMM (either layout) stores each of its rows of y
-      straight into every rank's y buffer (symmetric memory, plain stores over NVLink), and a bounded peer barrier (PeerGroup) makes them
-      visible -- the all-gather fused into the GEMM's epilogue, no separate collective, no copies;
+  fused (the default on GPUs of one node): the rank's tensor-core GEMM writes its rows of y into its own y buffer and
+      a push kernel (p2p_peer_push, all SMs, 16-byte stores) writes them into every other rank's -- or, push=False,
+      the GEMM's epilogue stores each value straight into every rank's y buffer; y buffers in symmetric memory, plain
+      stores over NVLink, then a bounded peer barrier (PeerGroup) makes them visible: no NCCL call, no copy engine;
   "nccl": the rank's GEMM writes its slot of a gather buffer, one NCCL all_gather_into_tensor collects the slots.
 
     row_ranges(rows, world)          [(start, stop)] per rank
@@ -109,12 +110,13 @@ class ShardedCompact:
     """One rank's share of a compact module: its rows as a Compact, and apply() returning the whole y on every rank.
 
     fused (the default with more than one rank): the rank's GEMM (the tensor-core layout `layout`, the package's
-    default unless given) stores its rows of y into every rank's y buffer over NVLink, then a peer barrier; y is a view of one of two symmetric buffers, used in turn, so it
+    default unless given) writes its rows of y into its own y buffer and a push kernel stores them into every other
+    rank's over NVLink (push=False: the GEMM's epilogue stores them into every rank's), then a peer barrier; y is a view of one of two symmetric buffers, used in turn, so it
     stays valid until this module's next-but-one apply. Otherwise ("nccl"): the GEMM writes its slot of a gather
     buffer, and one all_gather_into_tensor over the process group collects the slots into y."""
 
     def __init__(self, blocks: list, group=None, fused: bool | None = None, peers: PeerGroup | None = None,
-                 layout: str | None = None):
+                 layout: str | None = None, push: bool | None = None):
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
@@ -131,6 +133,10 @@ class ShardedCompact:
         self.width = max(b - a for a, b in self.ranges)
         self.mine = stop - start
         self.peers = peers
+        # fused: by default the GEMM writes its rows into its own y buffer (TMA stores) and one push kernel over all
+        # SMs stores them into every peer's; push=False stores every value to every rank's y from the GEMM's
+        # epilogue instead (N stores a value on the epilogue's critical path; measured slower at 2 ranks)
+        self.push = True if push is None else push
         self._bufs, self._turn, self._cap = [], 0, 0
 
     # ---- fused: y stored into every rank's buffer by the GEMM ----------------------------------------------------------
@@ -141,6 +147,8 @@ class ShardedCompact:
         if self.peers is None:
             self.peers = PeerGroup(self.group, device)
         self._bufs = [_symmetric((tokens, self.rows), dtype, device, self.group) for _ in range(2)]
+        self._others = [(ctypes.c_void_p * max(self.world - 1, 1))(*[ptrs[r] for r in range(self.world) if r != self.rank])
+                        for _, ptrs in self._bufs]
         self._cap = tokens
 
     def apply_fused(self, x2: torch.Tensor, sync: bool = True) -> torch.Tensor:
@@ -148,8 +156,14 @@ class ShardedCompact:
         if T > self._cap:
             self.prepare(T, x2.dtype, x2.device)
         buf, ptrs = self._bufs[self._turn]
+        others = self._others[self._turn]
         self._turn ^= 1
-        if self.local is not None:
+        if self.local is not None and self.push:
+            a, b = self.ranges[self.rank]
+            self.local.tiles(x2, out=buf[:T, a:b])
+            _lib.call("p2p_peer_push", buf.data_ptr(), others, self.world - 1, T, a, b - a, self.rows,
+                      _lib.dtype_code(buf), torch.cuda.current_stream(buf.device).cuda_stream)
+        elif self.local is not None:
             t = self.local.tiles
             if t.layout == "tc":
                 kernels.spmm_tc_peers(x2, t.words, t.seg, self.mine, self.cols, t.seg_cap, ptrs, self.world,

@@ -34,13 +34,13 @@ def _module(seed=0, rows=(1024, 256, 256), cols=2048, keep=33):
     return blocks, x
 
 
-def _sharded(rank, world, fused=None, layout=None):
+def _sharded(rank, world, fused=None, layout=None, push=None):
     """(rel-L2 of the sharded y against the whole module's, y's shape, a hash of y's bits). The shards may split their
     columns differently from the whole module, so sums can differ in the last bf16 bit."""
     import hashlib
     from p2pllm_b200 import compact, shard
     blocks, x = _module()
-    sc = shard.ShardedCompact(blocks, fused=fused, layout=layout)
+    sc = shard.ShardedCompact(blocks, fused=fused, layout=layout, push=push)
     y = sc.apply(None, x)
     y2 = sc.apply(None, x * 2)                          # the other of the two buffers (fused), then the first again
     y3 = sc.apply(None, x)
@@ -58,6 +58,10 @@ def _sharded_nccl(rank, world):
 
 def _sharded_mask(rank, world):
     return _sharded(rank, world, layout="mask")
+
+
+def _sharded_push(rank, world):
+    return _sharded(rank, world, push=True)
 
 
 def _barrier_gives_up(rank, world):
@@ -202,8 +206,8 @@ def test_sharded_module_on_one_gpu_is_the_module():
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-@pytest.mark.parametrize("fn", [_sharded, _sharded_mask, _sharded_nccl],
-                         ids=["fused_peer_stores_tc", "fused_peer_stores_mask", "nccl_all_gather"])
+@pytest.mark.parametrize("fn", [_sharded, _sharded_mask, _sharded_push, _sharded_nccl],
+                         ids=["fused_peer_stores_tc", "fused_peer_stores_mask", "push_kernel", "nccl_all_gather"])
 def test_sharded_module_over_two_gpus(fn):
     out = _spawn(fn, 2)
     for rank in range(2):
