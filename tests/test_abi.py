@@ -102,3 +102,48 @@ def test_torch_ops_load_and_propagate_shapes_on_meta_tensors(lib):
     assert ops.combine([h, h, h], h, h).shape == (8, 96) and ops.sum_parts([h, h]).shape == (8, 96)
     names = {"spmm_tc", "spmm_tc_into", "spmm_mask", "spmm_mask_into", "sumsq_cols", "combine", "sum_parts"}
     assert all(hasattr(ops, n) for n in names)
+
+
+def _ptrs(*vals):
+    return (ctypes.c_void_p * len(vals))(*vals)
+
+
+def _ints(*vals):
+    return (ctypes.c_int * len(vals))(*vals)
+
+
+def test_hop_inbox_size_is_host_only(lib):
+    """Counters (256 bytes) and n_ranks x ring slots, each part's 32-bit words stored with a 32-bit flag (twice the
+    bytes), rounded to 256; arguments out of range give 0."""
+    assert lib.p2p_hop_inbox_bytes(2, 17 * 5120, 0, 2) == 256 + 2 * 2 * (17 * 5120 * 2 * 2)
+    assert lib.p2p_hop_inbox_bytes(8, 100, 2, 1) == 256 + 8 * ((100 * 4 * 2 + 255) // 256 * 256)
+    assert lib.p2p_hop_inbox_bytes(9, 100, 0, 2) == 0
+    assert lib.p2p_hop_inbox_bytes(2, 100, 0, 0) == 0
+
+
+@pytest.mark.parametrize("call,needle", [
+    (lambda lib: lib.p2p_hop_send(0, _ptrs(65536), 1, None, None, 0, 64, _ptrs(4096, 8192), 2, 0, _ints(1, 1), 2, 0,
+                                  None, 2, 64, 1000000, None), b"listed twice"),
+    (lambda lib: lib.p2p_hop_send(0, _ptrs(65536), 1, None, None, 0, 65, _ptrs(4096, 8192), 2, 0, _ints(1), 1, 0,
+                                  None, 2, 128, 1000000, None), b"multiple of 16 bytes"),
+    (lambda lib: lib.p2p_hop_send(0, _ptrs(65536), 1, None, None, 0, 64, _ptrs(4100, 8192), 2, 0, _ints(1), 1, 0,
+                                  None, 2, 64, 1000000, None), b"256-byte aligned"),
+    (lambda lib: lib.p2p_hop_send(5, _ptrs(65536), 1, None, None, 0, 64, _ptrs(4096, 8192), 2, 0, _ints(1), 1, 0,
+                                  None, 2, 64, 1000000, None), b"mode"),
+    (lambda lib: lib.p2p_hop_recv(_ptrs(4096, 8192), 2, 1, _ints(2), 1, 0, None, 2, 64, 0, 64, _ptrs(65536)[0], 1000000,
+                                  None), b"rank 2 of 2"),
+    (lambda lib: lib.p2p_hop_recv(_ptrs(4096, 8192), 2, 1, _ints(0), 1, 0, None, 2, 64, 0, 128, 65536, 1000000, None),
+     b"slots hold"),
+    (lambda lib: lib.p2p_hop_recv(_ptrs(4096, 8192), 2, 1, _ints(0), 1, 0, None, 2, 64, 0, 64, 65536, 10, None),
+     b"time limit"),
+    (lambda lib: lib.p2p_peer_push(65536, _ptrs(4096), 1, 17, 3, 8, 64, 0, None), b"16-byte aligned"),
+    (lambda lib: lib.p2p_peer_push(65536, _ptrs(4096), 8, 17, 0, 8, 64, 0, None), b"peers"),
+    (lambda lib: lib.p2p_spmm_tc_gated(65536, 0, 17, 64, 64, 65536, 65536, 200, 64, 65536, 100, None, 0, None),
+     b"not whole row tiles"),
+    (lambda lib: lib.p2p_spmm_tc_peers(65536, 0, 17, 64, 64, 65536, 65536, 128, 64, _ptrs(4096), 1, 64, 128, None, 0,
+                                       None), b"do not fit"),
+], ids=["hop-dup-dst", "hop-size", "hop-inbox-align", "hop-mode", "hop-src-rank", "hop-capacity", "hop-limit",
+        "push-align", "push-peers", "gated-rows", "peers-columns"])
+def test_multi_gpu_entries_refuse_bad_arguments(lib, call, needle):
+    assert call(lib) != 0
+    assert needle in lib.p2p_last_error(), lib.p2p_last_error()
