@@ -69,16 +69,27 @@ def build(force: bool = False, verbose: bool = False) -> str:
         return LIB
     out_dir = os.path.join(ROOT, "_build")
     os.makedirs(out_dir, exist_ok=True)
-    objs = []
-    for src in SOURCES:
+    headers = [p for p in DEPS if not p.endswith(".cu")]
+    newest_header = max(os.path.getmtime(p) for p in headers)
+
+    def compile_one(src: str) -> str:
         obj = os.path.join(out_dir, os.path.basename(src).replace(".cu", ".o"))
-        cmd = [nvcc(), *ARCH, *FLAGS, "-I", os.path.join(ROOT, "include"), "-c", src, "-o", obj]
+        # An object newer than its source and every header is reused (each .cu includes only the headers listed).
+        if not force and os.path.exists(obj) and os.path.getmtime(obj) >= max(os.path.getmtime(src), newest_header):
+            return obj
+        cmd = [nvcc(), *ARCH, *FLAGS, "-I", os.path.join(ROOT, "include"), "-c", src, "-o", obj + ".tmp"]
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode:
             raise RuntimeError(f"nvcc failed on {os.path.basename(src)}:\n{r.stderr[-6000:]}")
         if verbose:
             sys.stderr.write(r.stderr)
-        objs.append(obj)
+        os.replace(obj + ".tmp", obj)
+        return obj
+
+    # The sources compile side by side (nvcc is single-threaded; the largest files take minutes each).
+    from concurrent.futures import ThreadPoolExecutor
+    with ThreadPoolExecutor(max_workers=max(1, min(len(SOURCES), os.cpu_count() or 1))) as pool:
+        objs = list(pool.map(compile_one, SOURCES))
     tmp = LIB + ".tmp"
     r = subprocess.run([nvcc(), *ARCH, "-shared", "-o", tmp, *objs], capture_output=True, text=True)
     if r.returncode:

@@ -7,7 +7,7 @@
 //
 //   warp 16 (producer)  per column tile: TMA of the x tile [tokens x 64] (128-byte swizzle) into the x ring, one
 //                       producer lane per ring slot.
-//   warps 0-15 (expand) two groups of 8 warps take alternate column tiles. Each warp zeroes its 16 rows of a
+//   warps 0-15 (expand) four groups of 4 warps take column tiles in turn. Each warp zeroes its 32 rows of a
 //                       128 x 64 bf16 tile in the A ring and writes its slice of the segment's words at the swizzled
 //                       byte offsets they carry, with no barrier between warps. The words come straight from HBM into
 //                       registers (coalesced, 16 bytes a lane), never through shared memory.
@@ -41,8 +41,9 @@ namespace {
 
 using namespace sm100;
 
-constexpr int kGroupWarps = 8;                                     // warps expanding one tile (16 rows each)
-constexpr int kGroups = 2;                                         // groups taking alternate column tiles
+constexpr int kGroupWarps = 4;                                     // warps expanding one tile (32 rows each)
+constexpr int kGroups = 4;                                         // groups taking column tiles in turn
+constexpr int kWarpRows = tc::kTileRows / kGroupWarps;             // a warp's rows of a tile
 constexpr int kExpWarps = kGroupWarps * kGroups;
 constexpr int kProducerWarp = kExpWarps;
 constexpr int kMmaWarp = kExpWarps + 1;                           // and kMmaWarp + 1: two MMA issuers
@@ -51,7 +52,7 @@ constexpr int kATileBytes = tc::kTileRows * tc::kTileCols * 2;   // 16 KiB
 constexpr int kASlotBytes = kATileBytes;                           // 1 KiB aligned, as the 128-byte swizzle needs
 constexpr int kMaxASlots = 12;                                     // A tiles in flight (even: the groups alternate)
 constexpr int kMaxXSlots = 4;                                      // x tiles in flight
-constexpr int kChunks = 4;                                         // 16-byte loads a lane holds for one tile
+constexpr int kChunks = 8;                                         // 16-byte loads a lane holds for one tile
 constexpr int kL2Ahead = 8;                                        // tiles between a segment's L2 prefetch and its loads
 constexpr uint32_t kOffsetMask = 0x3FFEu;                         // an even byte offset inside the 16 KiB tile
 constexpr int kMaxTilesPerCta = 256;                               // segment offsets and headers staged in smem
@@ -152,13 +153,14 @@ __device__ __forceinline__ void store_gated(T* yt, int64_t c0, int64_t limit, fl
     }
 }
 
-// A warp's share of one segment's words: the entries of its 16 rows (8-row groups 2 wg and 2 wg + 1), [lo, hi) in
+// A warp's share of one segment's words: the entries of its 32 rows (8-row groups 4 wg .. 4 wg + 3), [lo, hi) in
 // words from the CTA's first segment, from the segment's header (cumulative counts of its 8-row groups).
 __device__ __forceinline__ void warp_piece(const int64_t* offs, const uint16_t* hdr, int i, int wg, int& lo, int& hi) {
     const uint16_t* h = hdr + i * 2 * tc::kHeaderWords;
     const int s0 = (int)(offs[i] - offs[0]) + tc::kHeaderWords;
-    lo = s0 + (wg ? h[2 * wg - 1] : 0);
-    hi = s0 + h[2 * wg + 1];
+    constexpr int g8 = kWarpRows / 8;                              // 8-row groups a warp
+    lo = s0 + (wg ? h[g8 * wg - 1] : 0);
+    hi = s0 + h[g8 * wg + g8 - 1];
 }
 
 __device__ __forceinline__ uint32_t ldg_stream(const uint32_t* p) {
@@ -212,7 +214,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const uint32_t a_ring = base;                                  // SA slots of kASlotBytes
     const uint32_t x_ring = a_ring + SA * kASlotBytes;             // SX slots of b_bytes
     const uint32_t bars = x_ring + SX * p.b_bytes;
-    // fulla(s): the A tile expanded (8 warps arrive); fullx(s): the x tile landed (the producer's arrive with the TMA
+    // fulla(s): the A tile expanded (4 warps arrive); fullx(s): the x tile landed (the producer's arrive with the TMA
     // transaction count); emptya / emptyx: consumed (MMA commits).
     auto fulla = [&](int s) { return bars + 8u * s; };
     auto emptya = [&](int s) { return bars + 8u * (kMaxASlots + s); };
@@ -344,8 +346,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         }
         __syncwarp();
     } else {
-        // Expanders: group `grp` builds the dense 128 x 64 tiles of every other column tile in shared memory. Warp wg
-        // owns rows 16 wg .. 16 wg + 15 of the tile: it zeroes them and writes their entries at the offsets the words
+        // Expanders: group `grp` builds the dense 128 x 64 tiles of every fourth column tile in shared memory. Warp wg
+        // owns rows 32 wg .. 32 wg + 31 of the tile: it zeroes them and writes their entries at the offsets the words
         // carry, apart from the other warps (no barrier between them), then arrives on the slot's barrier. The words
         // come straight from HBM (or L2, see below) into registers in 16-byte loads, never through shared memory.
         const int grp = warp / kGroupWarps, wg = warp % kGroupWarps;
@@ -376,9 +378,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         // waits; with two, the slot is zeroed just before its own scatter.
         const bool zero_ahead = SA / kGroups >= 3;
         auto zero_rows = [&](int slot) {
-            uint4* rows16 = reinterpret_cast<uint4*>(gbase + (size_t)slot * kASlotBytes + wg * 2048);
+            uint4* rows16 = reinterpret_cast<uint4*>(gbase + (size_t)slot * kASlotBytes + wg * kWarpRows * 128);
 #pragma unroll
-            for (int z = 0; z < 4; ++z) rows16[lane + 32 * z] = make_uint4(0, 0, 0, 0);
+            for (int z = 0; z < kWarpRows / 4; ++z) rows16[lane + 32 * z] = make_uint4(0, 0, 0, 0);
         };
         if (zero_ahead && grp < nk) {
             zero_rows(s);                               // the group's first slot: no earlier use to wait for
@@ -430,9 +432,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             return true;
         };
         constexpr int G = kGroups;
-        // Each tile's words are loaded just before they are written. Loading one or two of the group's tiles ahead
-        // into more register buffers measured 1-3% slower on the bench layer at 17 and 272 tokens: the other group's
-        // tile and the slot waits cover the loads, and the extra live registers cost the scheduler more.
+        // Each tile's words are loaded just before they are written: a warp's loads are complete by the fence and
+        // arrive that end its tile, so the tiles whose words are in flight at once are one a group. Four groups of 4
+        // warps (32 rows a warp) measured 5.5% faster at 17 tokens and 7.7% at 272 on the bench layer than two groups
+        // of 8; loading a group's next tile ahead into more register buffers measured slower.
         for (int i = grp; i < nk; i += G) {
             fetch(i, b0, l0, h0);
             if (!expand(i, b0, l0, h0)) break;
@@ -710,12 +713,13 @@ int plan_tokens(int tn, TcPlan& pl) {
     // earlier, unfinished use. When both issuers take every tile, three large x slots are enough.
     const int step_x = pl.acc_stride ? 2 : 1;
     pl.x_slots = (pl.b_bytes <= 4096 || pl.acc_stride) ? 4 : 3;
-    while (pl.x_slots - step_x >= 2 && kSmemLimit - fixed - pl.x_slots * pl.b_bytes < 2 * kASlotBytes)
+    while (pl.x_slots - step_x >= 2 && kSmemLimit - fixed - pl.x_slots * pl.b_bytes < kGroups * kASlotBytes)
         pl.x_slots -= step_x;
     pl.a_slots = (kSmemLimit - fixed - pl.x_slots * pl.b_bytes) / kASlotBytes;
     if (pl.a_slots > kMaxASlots) pl.a_slots = kMaxASlots;
     pl.a_slots &= ~1;
-    if (pl.a_slots < 2) return fail(P2P_EUNSUPPORTED, "p2p_spmm_tc: %d tokens exceed shared memory", tn);
+    // Each expander group needs a slot of its own (a group's tile i takes slot i % SA, advancing kGroups a tile).
+    if (pl.a_slots < kGroups) return fail(P2P_EUNSUPPORTED, "p2p_spmm_tc: %d tokens exceed shared memory", tn);
     pl.smem = fixed + pl.a_slots * kASlotBytes + pl.x_slots * pl.b_bytes;
     return P2P_OK;
 }
