@@ -108,7 +108,7 @@ struct TcParams {
     // through peer memory) at column y_col0 + row, instead of y. Plain stores only (no TMA); vec4: 8-byte stores of 4
     // values are aligned.
     void* ys[8];
-    int n_ys, vec4;
+    int n_ys, vec4;                   // vec4: 8-byte stores of 4 values of y (or of every ys[k]) are aligned
     int64_t y_col0;
     int stage_peers;                  // unsplit: the tile staged in shared memory, then 16-byte stores to every ys[k]
 };
@@ -118,6 +118,14 @@ template <typename T, bool kPeers>
 __device__ __forceinline__ void put4(const TcParams& p, int64_t yrow, int64_t c0, const float (&v)[4]) {
     if constexpr (!kPeers) {
         T* yt = reinterpret_cast<T*>(p.y) + yrow * p.ldy;
+        if (p.vec4 && c0 + 3 < p.rows) {
+            uint2 raw;
+            T* e = reinterpret_cast<T*>(&raw);
+#pragma unroll
+            for (int c = 0; c < 4; ++c) e[c] = from_f32<T>(v[c]);
+            *reinterpret_cast<uint2*>(yt + c0) = raw;
+            return;
+        }
 #pragma unroll
         for (int c = 0; c < 4; ++c)
             if (c0 + c < p.rows) yt[c0 + c] = from_f32<T>(v[c]);
@@ -452,6 +460,16 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         const int64_t row = col0 + row_local;                       // y's column: the module's (or expert's) row
         const bool row_ok = row < p.rows;
         const bool two = p.acc_stride != 0 && nk > 1;                // issuer 1 took tiles: add its accumulator
+        // Where the tile goes, decided once per CTA, with no test left inside the value loop (the chain of tests per
+        // value it replaces took about 170 cycles a value: 5-9 us a CTA at 272 tokens): 0 = fp32 [token][128 rows] in the freed rings (gated, or column splits
+        // added in the cluster), 1 = the dtype the same way (TMA stores of y, or peer stores), 2 = y directly,
+        // 3 = the fp32 partials of the workspace.
+        const int mode = ((p.gated && p.n_split == 1) || (p.n_split > 1 && p.cluster)) ? 0
+                         : (p.y_tma || (kPeers && p.stage_peers))                    ? 1
+                         : p.n_split == 1                                            ? 2
+                                                                                     : 3;
+        float* const tile_f = reinterpret_cast<float*>(gbase) + row_local;        // [t * 128] of this lane's row
+        T* const tile_t = reinterpret_cast<T*>(gbase) + row_local;
         for (int c = cgroup; c < n_total / 16; c += kExpWarps / 4) {
             float v[16];
             const uint32_t ta = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(c * 16);
@@ -462,29 +480,38 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 #pragma unroll
                 for (int q = 0; q < 16; ++q) v[q] += u[q];
             }
+            const int t0 = c * 16, jn = min(16, tokens - t0);            // this chunk's tokens
+            if (mode == 0) {
+                float* d = tile_f + t0 * tc::kTileRows;
 #pragma unroll
-            for (int j = 0; j < 16; ++j) {
-                const int t = c * 16 + j;
-                if (t < tokens) {
-                    if (p.gated && p.n_split == 1) {
-                        reinterpret_cast<float*>(gbase)[t * tc::kTileRows + row_local] = v[j];   // rings are free
-                    } else if (p.y_tma || (kPeers && p.stage_peers)) {
-                        reinterpret_cast<T*>(gbase)[t * tc::kTileRows + row_local] = from_f32<T>(v[j]);  // rings free
-                    } else if (p.n_split == 1) {
-                        if (row_ok) {
-                            if constexpr (!kPeers) {
-                                reinterpret_cast<T*>(p.y)[(xrow0 + t) * p.ldy + row] = from_f32<T>(v[j]);
-                            } else {
-                                const int64_t at = (xrow0 + t) * p.ldy + p.y_col0 + row;
-                                for (int k = 0; k < p.n_ys; ++k) reinterpret_cast<T*>(p.ys[k])[at] = from_f32<T>(v[j]);
-                            }
+                for (int j = 0; j < 16; ++j)
+                    if (j < jn) d[j * tc::kTileRows] = v[j];
+            } else if (mode == 1) {
+                T* d = tile_t + t0 * tc::kTileRows;
+#pragma unroll
+                for (int j = 0; j < 16; ++j)
+                    if (j < jn) d[j * tc::kTileRows] = from_f32<T>(v[j]);
+            } else if (mode == 2) {
+                if (row_ok) {
+                    if constexpr (!kPeers) {
+                        T* d = reinterpret_cast<T*>(p.y) + (xrow0 + t0) * p.ldy + row;
+                        const int64_t ld = p.ldy;
+#pragma unroll
+                        for (int j = 0; j < 16; ++j)
+                            if (j < jn) d[j * ld] = from_f32<T>(v[j]);
+                    } else {
+                        for (int j = 0; j < jn; ++j) {
+                            const int64_t at = (xrow0 + t0 + j) * p.ldy + p.y_col0 + row;
+                            for (int k = 0; k < p.n_ys; ++k) reinterpret_cast<T*>(p.ys[k])[at] = from_f32<T>(v[j]);
                         }
-                    } else if (p.cluster) {
-                        reinterpret_cast<float*>(gbase)[t * tc::kTileRows + row_local] = v[j];   // rings are free
-                    } else if (row_ok) {
-                        p.partial[((int64_t)split * p.tokens + t) * p.rows_pad + row] = v[j];
                     }
                 }
+            } else if (row_ok) {
+                float* d = p.partial + ((int64_t)split * p.tokens + t0) * p.rows_pad + row;
+                const int64_t ld = p.rows_pad;
+#pragma unroll
+                for (int j = 0; j < 16; ++j)
+                    if (j < jn) d[j * ld] = v[j];
             }
         }
         if (p.y_tma) asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // the staged tile, for the TMA
@@ -594,23 +621,35 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             cluster_sync_all();
             return;
         }
-        const int64_t n4 = (int64_t)tokens * (tc::kTileRows / 4);
-        const int64_t u_begin = n4 * split / ns, u_end = n4 * (split + 1) / ns;
-        for (int64_t u = u_begin + threadIdx.x; u < u_end; u += kTcThreads) {
-            const int t = (int)(u / 32), r4 = (int)(u % 32) * 4;
-            const uint32_t off = part + (uint32_t)(t * tc::kTileRows + r4) * 4u;
-            float4 parts[8];
-            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-            for (int sp = 0; sp < 8; ++sp)
-                if (sp < ns) parts[sp] = ld_cluster_f4(cluster_addr(off, sp));
+        // Units of (token, 4 rows); each thread takes two at a time, every split's loads of both in flight together
+        // (a remote load's latency, not the bytes, set the pace of one unit at a time); the sums still run split by
+        // split, in order.
+        const int n4 = tokens * (tc::kTileRows / 4);
+        const int u_begin = (int)((int64_t)n4 * split / ns), u_end = (int)((int64_t)n4 * (split + 1) / ns);
+        for (int u = u_begin + (int)threadIdx.x; u < u_end; u += 2 * kTcThreads) {
+            const int ub = u + kTcThreads < u_end ? u + kTcThreads : u;             // the second unit (or again u)
+            const uint32_t off_a = part + (uint32_t)((u >> 5) * tc::kTileRows + (u & 31) * 4) * 4u;
+            const uint32_t off_b = part + (uint32_t)((ub >> 5) * tc::kTileRows + (ub & 31) * 4) * 4u;
+            float4 pa[8], pb[8];
 #pragma unroll
             for (int sp = 0; sp < 8; ++sp)
                 if (sp < ns) {
-                    acc.x += parts[sp].x; acc.y += parts[sp].y; acc.z += parts[sp].z; acc.w += parts[sp].w;
+                    pa[sp] = ld_cluster_f4(cluster_addr(off_a, sp));
+                    pb[sp] = ld_cluster_f4(cluster_addr(off_b, sp));
                 }
-            const float v[4] = {acc.x, acc.y, acc.z, acc.w};
-            put4<T, kPeers>(p, xrow0 + t, col0 + r4, v);
+            float4 a = make_float4(0.f, 0.f, 0.f, 0.f), b = a;
+#pragma unroll
+            for (int sp = 0; sp < 8; ++sp)
+                if (sp < ns) {
+                    a.x += pa[sp].x; a.y += pa[sp].y; a.z += pa[sp].z; a.w += pa[sp].w;
+                    b.x += pb[sp].x; b.y += pb[sp].y; b.z += pb[sp].z; b.w += pb[sp].w;
+                }
+            const float va[4] = {a.x, a.y, a.z, a.w};
+            put4<T, kPeers>(p, xrow0 + (u >> 5), col0 + (u & 31) * 4, va);
+            if (ub != u) {
+                const float vb[4] = {b.x, b.y, b.z, b.w};
+                put4<T, kPeers>(p, xrow0 + (ub >> 5), col0 + (ub & 31) * 4, vb);
+            }
         }
         cluster_sync_all();
         return;
@@ -956,6 +995,7 @@ int spmm_tc_impl(const void* x, int dtype, int64_t tokens, int64_t cols, int64_t
         for (int k = 0; k < 8; ++k) {
             prm.ys[k] = k < n_ys ? reinterpret_cast<char*>(ys[k]) + t0 * ldy * elem : nullptr;
             if (k < n_ys && (reinterpret_cast<uintptr_t>(ys[k]) & 7)) prm.vec4 = 0;
+            if (k == 0 && n_ys == 0 && (reinterpret_cast<uintptr_t>(prm.y) & 7)) prm.vec4 = 0;
             if (k < n_ys && (reinterpret_cast<uintptr_t>(ys[k]) & 15)) al16 = false;
         }
         prm.stage_peers = n_ys > 0 && pl.n_split == 1 && al16 &&
