@@ -111,7 +111,19 @@ struct TcParams {
     int n_ys, vec4;                   // vec4: 8-byte stores of 4 values of y (or of every ys[k]) are aligned
     int64_t y_col0;
     int stage_peers;                  // unsplit: the tile staged in shared memory, then 16-byte stores to every ys[k]
+    // Persistent runs (the kRuns instantiation; plain launches only): the module's n_units (row tile, column tile)
+    // units in row-major order are cut into gridDim.x contiguous runs, CTA b taking [b U / G, (b + 1) U / G). A run
+    // walks its row tiles in turn, row tile k of the run accumulating in TMEM set k % acc_sets; a row tile the run
+    // holds whole goes to y, its first and last, when other runs share them, leave fp32 partials (run_partial
+    // [G][2][tokens][128]: 0 = the run's first row tile, 1 = its last), and the last run of a row tile to leave its
+    // partial (a ticket a row tile) adds them all in run order.
+    int64_t n_units;
+    float* run_partial;
+    int acc_sets;
 };
+
+// The run holding unit u of a persistent launch (runs b hold [b U / G, (b + 1) U / G)).
+__device__ __forceinline__ int64_t run_of(int64_t u, int64_t U, int64_t G) { return ((u + 1) * G - 1) / U; }
 
 // Four values of y row `yrow` from module row c0 on (rows past the module are not written): to y, or to every ys[k].
 template <typename T, bool kPeers>
@@ -205,7 +217,8 @@ __device__ __forceinline__ void l2_prefetch(const void* src, uint32_t bytes) {
 
 // kL2: the launch prefetches segments into L2 ahead of the register loads (few tokens; see the expanders).
 // kPeers: y goes to every ys[k] (row sharding with the all-gather fused in) instead of y.
-template <typename T, bool kL2, bool kPeers>
+// kRuns: a persistent run of units across row tiles (see TcParams::n_units) instead of one row tile's column range.
+template <typename T, bool kL2, bool kPeers, bool kRuns = false>
 __global__ void __launch_bounds__(kTcThreads, 1)
     spmm_tc_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_y, TcParams p) {
     extern __shared__ uint8_t smem_raw[];
@@ -229,6 +242,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     auto fullx = [&](int s) { return bars + 8u * (2 * kMaxASlots + s); };
     auto emptyx = [&](int s) { return bars + 8u * (2 * kMaxASlots + kMaxXSlots + s); };
     const uint32_t done = bars + 8u * (2 * kMaxASlots + 2 * kMaxXSlots);
+    // Runs: accfull(s) -- a row tile's MMAs into accumulator set s complete (both issuers commit); accempty(s) -- the set
+    // read out (the 16 expander warps arrive); partdone / tickdone -- a shared row tile's partial written (16 warps) /
+    // its ticket taken (thread 0).
+    auto accfull = [&](int st) { return done + 8u * (1 + st); };
+    auto accempty = [&](int st) { return done + 8u * (3 + st); };
+    const uint32_t partdone = done + 40u, tickdone = done + 48u;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const WaitCtl wc{&g_tc_error, &g_tc_failed_seq, p.wait_ns, p.seq};
@@ -254,13 +273,37 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         n_total = p.n_total;
         col0 = (int64_t)rt * tc::kTileRows;
     }
-    const int kt0 = split * p.kt_per_split;
-    const int kt1 = min(p.col_tiles, kt0 + p.kt_per_split);
-    const int nk = kt1 - kt0;                                      // column tiles of this CTA
-    const int64_t seg0 = (int64_t)rt * p.col_tiles + kt0;
+    // This CTA's units [u0, u1) of the module's row-major (row tile, column tile) units: one row tile's column tiles
+    // kt0 .. kt0 + nk - 1, or (a run) units that may span row tiles r0 .. r0 + n_rows - 1.
+    const int64_t C = p.col_tiles;
+    int kt0, nk, n_rows = 1;
+    int64_t u0, u1, r0 = rt;
+    if constexpr (kRuns) {
+        u0 = (int64_t)blockIdx.x * p.n_units / gridDim.x;
+        u1 = ((int64_t)blockIdx.x + 1) * p.n_units / gridDim.x;
+        nk = (int)(u1 - u0);
+        r0 = u0 / C;
+        n_rows = nk > 0 ? (int)((u1 - 1) / C - r0 + 1) : 0;
+        kt0 = (int)(u0 - r0 * C);
+        rt = (int)r0;
+        col0 = r0 * tc::kTileRows;
+    } else {
+        kt0 = split * p.kt_per_split;
+        nk = min(p.col_tiles, kt0 + p.kt_per_split) - kt0;
+        u0 = (int64_t)rt * C + kt0;
+        u1 = u0 + nk;
+    }
+    const int64_t seg0 = u0;
     for (int j = threadIdx.x; j <= nk; j += blockDim.x) s_offs[j] = p.seg[seg0 + j];
-    for (int j = threadIdx.x; j < nk * tc::kHeaderWords; j += blockDim.x)
-        s_hdr[j] = __ldg(p.words + p.seg[seg0 + j / tc::kHeaderWords] + j % tc::kHeaderWords);
+    if constexpr (kRuns) {
+        // a run's many segments: their offsets first, then every header load from them at once
+        __syncthreads();
+        for (int j = threadIdx.x; j < nk * tc::kHeaderWords; j += blockDim.x)
+            s_hdr[j] = __ldg(p.words + s_offs[j / tc::kHeaderWords] + j % tc::kHeaderWords);
+    } else {
+        for (int j = threadIdx.x; j < nk * tc::kHeaderWords; j += blockDim.x)
+            s_hdr[j] = __ldg(p.words + p.seg[seg0 + j / tc::kHeaderWords] + j % tc::kHeaderWords);
+    }
 
     if (threadIdx.x == 0) {
         const uint32_t consumers = p.acc_stride ? 1u : 2u;        // issuers that commit a tile's slots
@@ -273,6 +316,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             mbar_init(emptyx(s), consumers);
         }
         mbar_init(done, 2);
+        if constexpr (kRuns) {
+            for (int st = 0; st < 2; ++st) {
+                mbar_init(accfull(st), 2);
+                mbar_init(accempty(st), kExpWarps);
+            }
+            mbar_init(partdone, kExpWarps);
+            mbar_init(tickdone, 1);
+        }
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     }
@@ -301,6 +352,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             const int s = lane;
             uint32_t ph = 0;
             int uses = 0;                                           // loads issued into slot s
+            int col = kt0 + lane;                                   // the x tile's column tile (runs wrap at C)
+            if constexpr (kRuns) col = (int)(col % C);
             for (int i = lane; i < nk; i += SX) {
                 if (i >= SX) {
                     if (!mbar_wait(emptyx(s), ph, 1, wc)) break;
@@ -309,9 +362,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 if (i == p.hold_tile) break;                        // a test withholds this load
                 mbar_expect_tx(fullx(s), (uint32_t)p.b_bytes);
                 for (int b = 0; b < p.n_boxes; ++b)
-                    tma_load_2d(x_ring + s * p.b_bytes + b * p.box_rows * 128, &tmap_x, (kt0 + i) * tc::kTileCols,
+                    tma_load_2d(x_ring + s * p.b_bytes + b * p.box_rows * 128, &tmap_x, col * tc::kTileCols,
                                 (int)xrow0 + b * p.box_rows, fullx(s));
                 ++uses;
+                col += SX;
+                if constexpr (kRuns) {
+                    while (col >= C) col -= (int)C;
+                }
             }
             // The slot's last load must have landed before the CTA exits (the TMA unit writes its shared memory): on
             // a normal run the MMA consumed it long ago; after a give-up this waits for the copy itself.
@@ -335,7 +392,42 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             const int step = by_tile ? 2 : 1;
             int sa = by_tile ? j : 0, sx = sa;
             uint32_t pha = 0, phx = 0, acc = 0;
-            for (int i = by_tile ? j : 0; i < nk; i += step) {
+            if constexpr (kRuns) {
+                // Row tile by row tile: row tile k into accumulator set k % acc_sets, once the expanders have read that
+                // set's previous row tile out; each row tile ends with a commit to its set's accfull.
+                const int SC = p.acc_sets;
+                const uint32_t set_cols = by_tile ? 2u * (uint32_t)p.acc_stride : 0u;
+                int i = by_tile ? j : 0;
+                bool ok = true;
+                for (int k = 0; k < n_rows && ok; ++k) {
+                    const int ub = (int)(min(u1, (r0 + k + 1) * C) - u0);
+                    const int st = k % SC;
+                    if (k >= SC) {
+                        if (!(ok = mbar_wait(accempty(st), (uint32_t)((k / SC - 1) & 1), 8, wc))) break;
+                        tc_fence_after();
+                    }
+                    const uint32_t dk = d + (uint32_t)st * set_cols;
+                    acc = 0u;
+                    for (; i < ub; i += step) {
+                        if (!(ok = mbar_wait(fulla(sa), pha, 2, wc))) break;
+                        if (!(ok = mbar_wait(fullx(sx), phx, 3, wc))) break;
+                        tc_fence_after();
+                        const uint64_t a_desc = a0 + (uint64_t)((sa * kASlotBytes) >> 4);
+                        const uint64_t b_desc = b0 + (uint64_t)((sx * p.b_bytes) >> 4);
+#pragma unroll
+                        for (int kk = 0; kk < tc::kTileCols / 16; ++kk)
+                            umma_f16(dk, a_desc + 2 * kk, b_desc + 2 * kk, id, acc | kk);
+                        acc = 1u;
+                        umma_commit(emptya(sa));
+                        umma_commit(emptyx(sx));
+                        advance(sa, pha, step, SA);
+                        advance(sx, phx, step, SX);
+                    }
+                    if (ok) umma_commit(accfull(st));   // this row tile's MMAs of this issuer, once complete
+                }
+                umma_commit(done);
+            }
+            for (int i = by_tile ? j : 0; !kRuns && i < nk; i += step) {
                 if (!mbar_wait(fulla(sa), pha, 2, wc)) break;     // no MMA on a tile not there
                 if (!mbar_wait(fullx(sx), phx, 3, wc)) break;
                 tc_fence_after();
@@ -350,7 +442,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 advance(sa, pha, step, SA);
                 advance(sx, phx, step, SX);
             }
-            umma_commit(done);                          // arrives once every MMA this thread issued completed
+            if (!kRuns) umma_commit(done);              // arrives once every MMA this thread issued completed
         }
         __syncwarp();
     } else {
@@ -444,6 +536,142 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         // arrive that end its tile, so the tiles whose words are in flight at once are one a group. Four groups of 4
         // warps (32 rows a warp) measured 5.5% faster at 17 tokens and 7.7% at 272 on the bench layer than two groups
         // of 8; loading a group's next tile ahead into more register buffers measured slower.
+        if constexpr (kRuns) {
+            // A run. Row tile k of the run is read out of TMEM set k % SC by every expander warp (lane quarter warp %
+            // 4, every fourth 16-column chunk) -- to y when the run holds the whole row tile, else to this run's fp32
+            // partial, the last of the row tile's runs adding all partials in run order. A warp reads a row tile out
+            // only when it must: before expanding a tile whose slot is freed by MMAs that wait for that read-out (so
+            // the ring is full of the next row tile's tiles meanwhile), once it is G tiles into the next row tile
+            // when there are two sets, and at the end. Every wait is bounded; a warp whose wait gave up expands no
+            // further tile but keeps to the same barrier sequence.
+            const int quarter = warp & 3, cgroup = warp >> 2;
+            const int row_local = quarter * 32 + lane;
+            const bool by_tile = p.acc_stride != 0;
+            const int SC = p.acc_sets;
+            const uint32_t set_cols = by_tile ? 2u * (uint32_t)p.acc_stride : 0u;
+            const int64_t RG = gridDim.x, U = p.n_units;
+            int n_shared = 0;                                       // shared row tiles read out so far
+            auto epilogue = [&](int k) {
+                const int ia = (int)(max(u0, (r0 + k) * C) - u0), ib = (int)(min(u1, (r0 + k + 1) * C) - u0);
+                const int st = k % SC;
+                int ok = 1;
+                if (lane == 0) ok = mbar_wait(accfull(st), (uint32_t)((k / SC) & 1), 9, wc);
+                ok = __shfl_sync(0xffffffffu, ok, 0);
+                tc_fence_after();
+                const int64_t r = r0 + k;
+                const bool whole = u0 + ia == r * C && u0 + ib == (r + 1) * C;
+                const int64_t row = r * tc::kTileRows + row_local;
+                const bool row_ok = row < p.rows;
+                const int j_first = by_tile ? (ia & 1) : 0;             // issuer j took the run's tiles i = j mod 2
+                const bool both = by_tile && ib - ia >= 2;
+                const uint32_t tset = tmem + (uint32_t)st * set_cols + ((uint32_t)(quarter * 32) << 16);
+                float* part = p.run_partial + ((int64_t)blockIdx.x * 2 + (k == 0 ? 0 : 1)) * tokens * tc::kTileRows +
+                              row_local;
+                for (int c = cgroup; ok && c < n_total / 16; c += kExpWarps / 4) {
+                    float v[16];
+                    const uint32_t ta = tset + (uint32_t)(c * 16);
+                    tmem_ld16(ta + (uint32_t)(j_first * p.acc_stride), v);
+                    if (both) {
+                        float w2[16];
+                        tmem_ld16(ta + (uint32_t)((j_first ^ 1) * p.acc_stride), w2);
+#pragma unroll
+                        for (int q = 0; q < 16; ++q) v[q] += w2[q];
+                    }
+                    const int t0 = c * 16, jn = min(16, tokens - t0);
+                    if (whole) {
+                        if (row_ok) {
+                            T* dst = reinterpret_cast<T*>(p.y) + (xrow0 + t0) * p.ldy + row;
+                            const int64_t ld = p.ldy;
+#pragma unroll
+                            for (int jj = 0; jj < 16; ++jj)
+                                if (jj < jn) dst[jj * ld] = from_f32<T>(v[jj]);
+                        }
+                    } else {
+                        float* dst = part + t0 * tc::kTileRows;
+#pragma unroll
+                        for (int jj = 0; jj < 16; ++jj)
+                            if (jj < jn) dst[jj * tc::kTileRows] = v[jj];
+                    }
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(accempty(st));              // the set may take its next row tile
+                if (whole) return;
+                // A shared row tile: once the 16 warps have written the partial, thread 0 takes the row tile's ticket;
+                // the last run to take it adds every run's partial, run by run.
+                __threadfence();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(partdone);
+                const uint32_t par = (uint32_t)(n_shared & 1);
+                ++n_shared;
+                const int64_t b_first = run_of(r * C, U, RG), b_last = run_of((r + 1) * C - 1, U, RG);
+                if (threadIdx.x == 0) {
+                    s_last = mbar_wait(partdone, par, 10, wc) &&
+                             atomicAdd(&p.tickets[r], 1u) == (unsigned)(b_last - b_first);
+                    mbar_arrive(tickdone);
+                }
+                int ok2 = 1;
+                if (lane == 0) ok2 = mbar_wait(tickdone, par, 11, wc);
+                if (!__shfl_sync(0xffffffffu, ok2, 0) || !s_last) return;
+                __threadfence();
+                // Units of (token, 4 rows), eight a thread at a time with every load of a run's partial in flight
+                // together (one unit at a time, the L2 latency made this 17 us at 272 tokens); runs added in order.
+                constexpr int kU = 8, kThr = kExpWarps * 32;
+                const int nu = tokens * (tc::kTileRows / 4);
+                for (int ub0 = threadIdx.x; ub0 < nu; ub0 += kThr * kU) {
+                    float4 a[kU];
+#pragma unroll
+                    for (int q = 0; q < kU; ++q) a[q] = make_float4(0.f, 0.f, 0.f, 0.f);
+                    for (int64_t b = b_first; b <= b_last; ++b) {
+                        const int wb = (b * U / RG) / C == r ? 0 : 1;      // r is run b's first row tile, or its last
+                        const float* base = p.run_partial + (b * 2 + wb) * tokens * tc::kTileRows;
+                        float4 pv[kU];
+#pragma unroll
+                        for (int q = 0; q < kU; ++q) {
+                            const int u = ub0 + q * kThr;
+                            pv[q] = u < nu ? __ldcg(reinterpret_cast<const float4*>(base + (u >> 5) * tc::kTileRows +
+                                                                                    (u & 31) * 4))
+                                           : make_float4(0.f, 0.f, 0.f, 0.f);
+                        }
+#pragma unroll
+                        for (int q = 0; q < kU; ++q) {
+                            a[q].x += pv[q].x; a[q].y += pv[q].y; a[q].z += pv[q].z; a[q].w += pv[q].w;
+                        }
+                    }
+#pragma unroll
+                    for (int q = 0; q < kU; ++q) {
+                        const int u = ub0 + q * kThr;
+                        if (u >= nu) break;
+                        const float vv[4] = {a[q].x, a[q].y, a[q].z, a[q].w};
+                        put4<T, false>(p, xrow0 + (u >> 5), r * tc::kTileRows + (u & 31) * 4, vv);
+                    }
+                }
+                if (threadIdx.x == 0) p.tickets[r] = 0u;                  // zero again for the next call
+            };
+            bool live = true;
+            int k_epi = 0;
+            // The tile whose slot expand(i) waits for (i - SA, or i + G - SA when zeroing ahead) and its row tile in
+            // the run, kept by increments (no division on the warp's per-tile path).
+            int dep = (zero_ahead ? G - SA : -SA) + grp, dep_row = 0;
+            int dep_row_end = (int)(min(u1, (r0 + 1) * C) - u0);      // local end of row tile dep_row
+            for (int i = grp;; i += G, dep += G) {
+                int need = n_rows;                                      // row tiles to have read out first
+                if (live && i < nk) {
+                    while (dep >= dep_row_end) {
+                        ++dep_row;
+                        dep_row_end += (int)C;
+                    }
+                    need = dep >= 0 ? dep_row - SC + 1 : 0;
+                }
+                while (k_epi < need) epilogue(k_epi++);
+                if (!live || i >= nk) break;
+                fetch(i, b0, l0, h0);
+                live = expand(i, b0, l0, h0);
+            }
+            while (k_epi < n_rows) epilogue(k_epi++);
+            if (lane == 0) mbar_drain(done, 0, 6, wc);                 // no MMA may still write TMEM
+            __syncwarp();
+        } else {
         for (int i = grp; i < nk; i += G) {
             fetch(i, b0, l0, h0);
             if (!expand(i, b0, l0, h0)) break;
@@ -515,6 +743,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             }
         }
         if (p.y_tma) asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // the staged tile, for the TMA
+        }
     }
 
     tc_fence_before();
@@ -523,6 +752,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(p.tmem_cols) : "memory");
     }
+    if constexpr (kRuns) return;
     if (p.gated == 2) {
         // Column sums of squares of the gated activations: thread (unit j, token group tg) adds tokens tg, tg + 8,
         // ... in fp32; then the 8 groups are added in order (the result does not depend on scheduling).
@@ -737,7 +967,7 @@ struct TcPlan {
 // Token-dependent part of a launch plan: MMA N, x boxes, TMEM columns, ring depths, shared memory. Fails when the
 // tokens do not fit shared memory.
 int plan_tokens(int tn, TcPlan& pl) {
-    const int fixed = 1024 + 8 * (2 * kMaxASlots + 2 * kMaxXSlots + 1) + 64;
+    const int fixed = 1024 + 8 * (2 * kMaxASlots + 2 * kMaxXSlots + 7) + 64;   // + done and the runs' six barriers
     pl.n_total = (tn + 15) / 16 * 16;
     pl.n_boxes = pl.n_total <= 256 ? 1 : 2;
     pl.box_rows = pl.n_total / pl.n_boxes;
@@ -770,6 +1000,7 @@ int launch_tc(const CUtensorMap& map, const CUtensorMap& ymap, const TcParams& p
     const bool l2 = prm.n_total <= 64;
     auto kernel = spmm_tc_kernel<T, false, false>;
     if (prm.n_ys) kernel = l2 ? spmm_tc_kernel<T, true, true> : spmm_tc_kernel<T, false, true>;
+    else if (prm.run_partial) kernel = l2 ? spmm_tc_kernel<T, true, false, true> : spmm_tc_kernel<T, false, false, true>;
     else if (l2) kernel = spmm_tc_kernel<T, true, false>;
     if (int e = allow_smem((const void*)kernel, smem, "p2p_spmm_tc")) return e;
     // A programmatic dependent of the stream's previous kernel (the kernel waits for it before loading x), and with
@@ -885,6 +1116,26 @@ void plan_split(int64_t row_tiles, int col_tiles, int tokens, int sms, int* n_sp
     *n_split = (col_tiles + k - 1) / k;
 }
 
+// Persistent runs (see TcParams::n_units): one CTA an SM, each a run of about units / SMs units (more CTAs only when
+// a run would pass kMaxTilesPerCta), every SM busy to the end, instead of one CTA a row tile, which leaves a partial
+// last wave when there are more row tiles than SMs. Taken for such modules when a row tile's accumulators fit TMEM
+// twice (at most 128 tokens: the next row tile accumulates while the last is read out). Measured on the bench layer at
+// 17 tokens: gate_up (224 row tiles, two waves on 148 SMs, the second half empty) 69.4 -> 63.9 us. Not taken: at 272
+// tokens (one accumulator set, the MMAs waiting on each read-out) runs made the layer step slower, and modules of
+// fewer row tiles than SMs were slower in runs than in their column splits. Returns the grid, 0 for no runs.
+int64_t run_grid(int64_t row_tiles, int col_tiles, int tokens, int sms) {
+    const int n = (tokens + 15) / 16 * 16;
+    if (n > 128 || row_tiles <= sms) return 0;
+    const int64_t U = row_tiles * col_tiles;
+    int64_t g = sms;
+    if ((U + g - 1) / g > kMaxTilesPerCta) g = (U + kMaxTilesPerCta - 1) / kMaxTilesPerCta;
+    return g;
+}
+
+size_t run_workspace(int64_t grid, int tokens) {
+    return kTicketRegion + (size_t)grid * 2 * tokens * tc::kTileRows * sizeof(float);
+}
+
 }  // namespace
 }  // namespace p2p
 
@@ -899,6 +1150,11 @@ extern "C" size_t p2p_spmm_tc_workspace(int64_t rows, int64_t cols, int64_t toke
     const int chunks[2] = {(int)(tokens < 512 ? tokens : 512), (int)(tokens % 512)};
     for (int t : chunks) {
         if (t <= 0) continue;
+        if (const int64_t g = run_grid(row_tiles, col_tiles, t, sm_count())) {
+            const size_t w = run_workspace(g, t);
+            need = need > w ? need : w;
+            continue;
+        }
         int n = 1, per = col_tiles;
         plan_split(row_tiles, col_tiles, t, sm_count(), &n, &per);
         if (n == 1) continue;
@@ -947,8 +1203,20 @@ int spmm_tc_impl(const void* x, int dtype, int64_t tokens, int64_t cols, int64_t
         TcPlan pl;
         if (int e = plan_tokens(tn, pl)) return e;
         plan_split(row_tiles, col_tiles, tn, sms, &pl.n_split, &pl.kt_per_split);
+        const int64_t run_g = (!gated && n_ys == 0) ? run_grid(row_tiles, col_tiles, tn, sms) : 0;
+        int acc_sets = 1;
+        if (run_g) {
+            pl.n_split = 1;
+            pl.kt_per_split = col_tiles;
+            // two accumulator sets (a row tile accumulates while the last one is read out); n_total <= 128 here
+            acc_sets = 2;
+            pl.tmem_cols = 4 * pl.acc_stride;
+        }
 
         TcParams prm;
+        prm.n_units = row_tiles * col_tiles;
+        prm.run_partial = nullptr;
+        prm.acc_sets = acc_sets;
         prm.words = words;
         prm.seg = seg;
         prm.rows = (int)rows;
@@ -969,7 +1237,15 @@ int spmm_tc_impl(const void* x, int dtype, int64_t tokens, int64_t cols, int64_t
         prm.rows_pad = row_tiles * tc::kTileRows;
         prm.partial = nullptr;
         prm.tickets = nullptr;
-        prm.cluster = cluster_reduce(pl, pl.n_split, row_tiles) ? 1 : 0;
+        prm.cluster = !run_g && cluster_reduce(pl, pl.n_split, row_tiles) ? 1 : 0;
+        if (run_g) {
+            const size_t need = run_workspace(run_g, tn);
+            P2P_REQUIRE(workspace && workspace_bytes >= need, "p2p_spmm_tc: workspace of %zu bytes, %zu needed",
+                        workspace_bytes, need);
+            if (row_tiles > kMaxRowTiles) return fail(P2P_EUNSUPPORTED, "p2p_spmm_tc: %lld rows is too many", (long long)rows);
+            prm.tickets = reinterpret_cast<unsigned*>(workspace);
+            prm.run_partial = reinterpret_cast<float*>(reinterpret_cast<char*>(workspace) + kTicketRegion);
+        }
         if (pl.n_split > 1 && !prm.cluster) {
             const size_t need = kTicketRegion + (size_t)pl.n_split * tn * prm.rows_pad * sizeof(float);
             P2P_REQUIRE(workspace && workspace_bytes >= need, "p2p_spmm_tc: workspace of %zu bytes, %zu needed",
@@ -1008,11 +1284,11 @@ int spmm_tc_impl(const void* x, int dtype, int64_t tokens, int64_t cols, int64_t
         if (int e = encode_x_map(&map, xt, dtype, tn, cols, ldx, pl.box_rows)) return e;
         // y through TMA stores when unsplit and aligned (rows of y start on 16 bytes); the staged tile is
         // n_total x 128 x 2 bytes of the rings
-        prm.y_tma = !gated && n_ys == 0 && pl.n_split == 1 && ldy % 8 == 0 && aligned16(prm.y) &&
+        prm.y_tma = !run_g && !gated && n_ys == 0 && pl.n_split == 1 && ldy % 8 == 0 && aligned16(prm.y) &&
                     (int64_t)pl.n_total * tc::kTileRows * 2 <= (int64_t)pl.a_slots * kASlotBytes;
         ymap = map;
         if (prm.y_tma && encode_y_map(&ymap, prm.y, dtype, tn, rows, ldy, pl.box_rows) != P2P_OK) prm.y_tma = 0;
-        const dim3 grid((unsigned)row_tiles, (unsigned)pl.n_split);
+        const dim3 grid(run_g ? (unsigned)run_g : (unsigned)row_tiles, (unsigned)pl.n_split);
         if (int e = dtype == P2P_BF16 ? launch_tc<__nv_bfloat16>(map, ymap, prm, grid, pl.smem, st)
                                       : launch_tc<__half>(map, ymap, prm, grid, pl.smem, st))
             return e;
@@ -1124,6 +1400,9 @@ int grouped_impl(const void* x, int dtype, int64_t x_rows, int64_t cols, int64_t
     prm.vec4 = 0;
     prm.y_col0 = 0;
     prm.stage_peers = 0;
+    prm.n_units = 0;
+    prm.run_partial = nullptr;
+    prm.acc_sets = 1;
     for (int k = 0; k < 8; ++k) prm.ys[k] = nullptr;
     if (gated && (int64_t)pl.n_total * tc::kTileRows * 4 + (gated == 2 ? 64 * 8 * 4 : 0) >
                      (int64_t)pl.a_slots * kASlotBytes + (int64_t)pl.x_slots * pl.b_bytes)

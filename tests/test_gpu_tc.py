@@ -162,6 +162,26 @@ def test_llama_shapes_at_17_and_272_tokens():
             _check(y[:, sample], want, torch.bfloat16)
 
 
+@pytest.mark.parametrize("t", [1, 17, 100, 256, 272, 300])
+@pytest.mark.parametrize("rows,cols,keep", [(19000, 1000, 7), (28772, 640, 40), (40000, 64, 50), (20000, 200, 30)])
+def test_persistent_runs_match_the_dense_matmul(t, rows, cols, keep):
+    """Modules of more row tiles than SMs run as one CTA an SM, each a contiguous run of (row tile, column tile) units
+    across row tiles: runs shorter and longer than a row tile, a ragged last row tile, a single column tile (every row
+    tile whole in its run), both accumulator layouts (N <= 256: one per issuer; above: one shared). Against the oracle
+    on a sample of rows and the last rows; a second call repeats the first bit for bit (the shared row tiles' partials
+    are added in run order, and their tickets are left zero)."""
+    values, idx = _module(rows, cols, keep, seed=rows + t)
+    tiles = compact.Tiles([("compact", values, idx, cols)])
+    x = torch.randn(t, cols, device="cuda").bfloat16()
+    y = tiles(x)
+    kernels.spmm_tc_status()
+    sample = torch.cat([torch.arange(0, rows, 37, device="cuda"), torch.arange(rows - 130, rows, device="cuda")])
+    want = oracle.forward(_bits(x), _bits(values[sample]), idx[sample].cpu().numpy(), cols, "bf16")
+    _check(y[:, sample], want, torch.bfloat16)
+    assert torch.equal(tiles(x), y)
+    kernels.spmm_tc_status()
+
+
 def test_split_launches_of_different_shapes_share_a_workspace():
     """Column-split launches with few row tiles, then many: each finds its ticket counters zero."""
     for rows, cols in ((256, 4096), (14336, 4096), (512, 14336), (28672, 4096)):
