@@ -41,7 +41,7 @@ namespace {
 
 using namespace sm100;
 
-constexpr int kGroupWarps = 4;                                     // warps expanding one tile (32 rows each)
+constexpr int kGroupWarps = tc::kTileRows / tc::kSliceRows;        // warps expanding one tile (a slice each)
 constexpr int kGroups = 4;                                         // groups taking column tiles in turn
 constexpr int kWarpRows = tc::kTileRows / kGroupWarps;             // a warp's rows of a tile
 constexpr int kExpWarps = kGroupWarps * kGroups;
@@ -52,7 +52,7 @@ constexpr int kATileBytes = tc::kTileRows * tc::kTileCols * 2;   // 16 KiB
 constexpr int kASlotBytes = kATileBytes;                           // 1 KiB aligned, as the 128-byte swizzle needs
 constexpr int kMaxASlots = 12;                                     // A tiles in flight (even: the groups alternate)
 constexpr int kMaxXSlots = 4;                                      // x tiles in flight
-constexpr int kChunks = 8;                                         // 16-byte loads a lane holds for one tile
+constexpr int kChunks = tc::kSliceChunks;                          // 16-byte loads a lane holds for one tile
 constexpr int kL2Ahead = 8;                                        // tiles between a segment's L2 prefetch and its loads
 constexpr uint32_t kOffsetMask = 0x3FFEu;                         // an even byte offset inside the 16 KiB tile
 constexpr int kMaxTilesPerCta = 256;                               // segment offsets and headers staged in smem

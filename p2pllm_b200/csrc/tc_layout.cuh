@@ -5,11 +5,11 @@
 // tile) pair is a segment holding the kept weights that fall in it:
 //
 //   words 0..7    header: 16 uint16 (two a word, low half first); header[j] = entries in the segment's rows
-//                 0 .. 8j + 7, so 16-row slice s owns entries [header[2s-1], header[2s+1]) (header[-1] = 0) and
-//                 header[15] is the segment's entry count
+//                 0 .. 8j + 7, so 32-row slice s (the rows one GEMM warp expands) owns entries
+//                 [header[4s-1], header[4s+3]) (header[-1] = 0) and header[15] is the segment's entry count
 //   words 8..     one word per kept weight, slice after slice. Within a slice the order is free (every word
-//                 carries its place); the builder fills the GEMM's store rounds (tiles.cu, bank_order_kernel) so
-//                 that the entries one store writes fall in as few passes of shared-memory banks as the slice
+//                 carries its place); the builder fills the GEMM warp's store rounds (tiles.cu, bank_order_kernel)
+//                 so that the entries one store writes fall in as few passes of shared-memory banks as the slice
 //                 allows, round by round. Each word:
 //                   bits 31..16  the value (bf16 or f16 bits)
 //                   bits 13..0   the byte offset of that weight in the 128 x 64 tile as the tensor cores read it:
@@ -30,6 +30,8 @@ constexpr int kTileRows = 128;
 constexpr int kTileCols = 64;
 constexpr int kHeaderWords = 8;
 constexpr int kGroupRows = 8;
+constexpr int kSliceRows = 32;                       // rows of a tile one GEMM expander warp writes
+constexpr int kSliceChunks = 8;                      // 16-byte loads a GEMM lane holds for its slice (then one word)
 constexpr uint32_t kFillWord = 16384u;
 
 __host__ __device__ __forceinline__ uint32_t swizzled_offset(int row_local, int col_local) {

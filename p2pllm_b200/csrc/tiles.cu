@@ -183,32 +183,26 @@ __global__ void __launch_bounds__(kBuildBlock) fill_kernel(Blocks bl, int64_t ro
     }
 }
 
-// Reorders the entries of every 16-row slice of every segment for the GEMM's stores. The GEMM's warp loads its slice
-// in 16-byte pieces from the 4-word boundary A at or below the slice's start: lane l's load c holds words
-// A + 4 (l + 32 c) .. + 3, and store round 4 c + j writes word j of every lane's load c (rounds 0..15, the first 512
-// words from A); past those, round 16 + m stores words A + 512 + 32 m + l. A store takes one pass per entry on its
-// busiest shared-memory bank (bits 2..6 of the entry's byte offset), so the entries of one round should differ in
-// bank. Round by round, the places are filled greedily: the fewest entries of any one bank the remaining entries allow
-// (every bank gives up to m - 1, the banks with the most left give the m-th ones), which also keeps the banks' counts
-// level for the later rounds. (Dealing entries in (rank within bank, bank) order instead lets the rounds drift off the
-// bank boundaries once banks run out, and costs about half again as many store passes at keep 36.) One warp a slice
-// (16 rows x 64 columns: at most 32 entries a bank, 1024 in all).
-constexpr int kOrderWarps = 4;
-constexpr int kSliceMax = 16 * tc::kTileCols;
-constexpr int kStoreRounds = 16 + (kSliceMax + 3 - 512 + 31) / 32;   // rounds over the slice's words from A
+// Reorders the entries of every 32-row slice of every segment for the GEMM's stores (a slice: the rows one expander
+// warp writes, tc::kSliceRows). The GEMM's warp loads its slice in 16-byte pieces from the 4-word boundary A at or
+// below the slice's start: lane l's load c (c < tc::kSliceChunks) holds words A + 4 (l + 32 c) .. + 3, and store round
+// 4 c + j writes word j of every lane's load c (rounds 0..31, the first 1024 words from A); past those, round 32 + m
+// stores words A + 1024 + 32 m + l. A store takes one pass per entry on its busiest shared-memory bank (bits 2..6 of
+// the entry's byte offset), so the entries of one round should differ in bank. Round by round, the places are filled
+// greedily: the fewest entries of any one bank the remaining entries allow (every bank gives up to m - 1, the banks
+// with the most left give the m-th ones), which also keeps the banks' counts level for the later rounds. (Dealing
+// entries in (rank within bank, bank) order instead lets the rounds drift off the bank boundaries once banks run out,
+// and costs about half again as many store passes at keep 36.) One warp a slice (32 rows x 64 columns: at most 64
+// entries a bank, 2048 in all).
+constexpr int kOrderWarps = 2;
+constexpr int kSlices = tc::kTileRows / tc::kSliceRows;                // a segment's slices
+constexpr int kSliceMax = tc::kSliceRows * tc::kTileCols;
+constexpr int kRegWords = tc::kSliceChunks * 128;                        // words the lanes' 16-byte loads hold
+constexpr int kRegRounds = tc::kSliceChunks * 4;
+constexpr int kStoreRounds = kRegRounds + (kSliceMax + 3 - kRegWords + 31) / 32;   // rounds over the slice's words
+static_assert(kSlices % kOrderWarps == 0, "a block takes whole segments' slices");
 
 __device__ __forceinline__ int ceil_div4(int x) { return (x + 3) >> 2; }   // arithmetic shift: negative x too
-
-// The store round of word A + pr, and its lane.
-__device__ __forceinline__ void store_round(int pr, int& round, int& lane) {
-    if (pr < 512) {
-        round = (pr >> 7) * 4 + (pr & 3);
-        lane = (pr & 127) >> 2;
-    } else {
-        round = 16 + ((pr - 512) >> 5);
-        lane = (pr - 512) & 31;
-    }
-}
 
 __global__ void __launch_bounds__(kOrderWarps * 32) bank_order_kernel(const int64_t* __restrict__ seg, int64_t n_seg,
                                                                       uint32_t* __restrict__ words) {
@@ -221,13 +215,14 @@ __global__ void __launch_bounds__(kOrderWarps * 32) bank_order_kernel(const int6
     __shared__ int rstart[kOrderWarps][kStoreRounds + 1];       // and its lanes in the slice
     const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const unsigned below = (1u << lane) - 1u;
-    const int64_t n_work = n_seg * (8 / kOrderWarps);
+    const int64_t n_work = n_seg * (kSlices / kOrderWarps);
     for (int64_t item = blockIdx.x; item < n_work; item += gridDim.x) {
-        const int64_t sg = item / (8 / kOrderWarps);
-        const int slice = (int)(item % (8 / kOrderWarps)) * kOrderWarps + w;
+        const int64_t sg = item / (kSlices / kOrderWarps);
+        const int slice = (int)(item % (kSlices / kOrderWarps)) * kOrderWarps + w;
         const int64_t s0 = seg[sg];
         auto hdr = [&](int j) { return (int)((words[s0 + j / 2] >> (16 * (j & 1))) & 0xffffu); };
-        const int lo = slice ? hdr(2 * slice - 1) : 0, hi = hdr(2 * slice + 1);
+        constexpr int g8 = tc::kSliceRows / tc::kGroupRows;           // 8-row groups a slice
+        const int lo = slice ? hdr(g8 * slice - 1) : 0, hi = hdr(g8 * slice + g8 - 1);
         const int n = hi - lo;
         const int64_t first = s0 + tc::kHeaderWords + lo;        // the slice's first word
         const int lo_rel = (int)(first & 3);                      // its place above the 4-word boundary A
@@ -269,12 +264,12 @@ __global__ void __launch_bounds__(kOrderWarps * 32) bank_order_kernel(const int6
             if (lane == 0) {
                 for (int R = 0; R < kStoreRounds; ++R) {
                     int lo_l, hi_l;
-                    if (R < 16) {
+                    if (R < kRegRounds) {
                         const int c = R >> 2, j = R & 3;
                         lo_l = max(0, ceil_div4(lo_rel - 128 * c - j));
                         hi_l = min(32, ceil_div4(lo_rel + n - 128 * c - j));
                     } else {
-                        const int b0 = 512 + 32 * (R - 16);
+                        const int b0 = kRegWords + 32 * (R - kRegRounds);
                         lo_l = max(0, lo_rel - b0);
                         hi_l = min(32, lo_rel + n - b0);
                     }
@@ -310,7 +305,8 @@ __global__ void __launch_bounds__(kOrderWarps * 32) bank_order_kernel(const int6
                 off -= take;
                 for (int q = 0; q < take; ++q) {
                     const int l = llo[w][R] + off + q;                    // the round's lane, hence its word
-                    const int pr = R < 16 ? 128 * (R >> 2) + 4 * l + (R & 3) : 512 + 32 * (R - 16) + l;
+                    const int pr = R < kRegRounds ? 128 * (R >> 2) + 4 * l + (R & 3)
+                                                  : kRegWords + 32 * (R - kRegRounds) + l;
                     base[pr] = byrank[w][start + taken + q];
                 }
                 rem -= take;
@@ -549,7 +545,7 @@ extern "C" int p2p_tiles_fill(const p2p_row_block* blocks, int nblocks, int idx_
         }
     }
     if (s.n_seg > 0) {
-        const int64_t items = s.n_seg * (8 / kOrderWarps);
+        const int64_t items = s.n_seg * (kSlices / kOrderWarps);
         bank_order_kernel<<<(unsigned)(items < sm_count() * 8 ? items : sm_count() * 8), kOrderWarps * 32, 0, st>>>(
             seg, s.n_seg, words);
     }

@@ -34,7 +34,7 @@ def _check(got, want, dtype):
                                             (200, 5120, 90)])
 def test_layout_decodes_to_the_selection(rows, cols, keep):
     """Every segment: a header of cumulative 8-row-group counts, then one word per kept weight holding its value and
-    its swizzled byte offset in the 128 x 64 tile, 16-row slice after slice, each slice dealt to the GEMM's store rounds
+    its swizzled byte offset in the 128 x 64 tile, 32-row slice after slice, each slice dealt to the GEMM's store rounds
     so that each store round holds as few entries of any one shared-memory bank as the slice's remaining entries allow
     (the smallest m with sum over banks of min(left, m) >= the round's places); decoded, the layout is the selection,
     bit for bit."""
@@ -57,15 +57,15 @@ def test_layout_decodes_to_the_selection(rows, cols, keep):
         assert (off % 2 == 0).all()
         r = off >> 7
         c = ((((off >> 4) & 7) ^ (r & 7)) << 3) | ((off & 15) >> 1)
-        sl = r // 16
+        sl = r // 32
         e = np.arange(count)
-        bounds = np.concatenate([[0], hdr[1::2]])                   # slice s: [hdr[2s-1], hdr[2s+1])
+        bounds = np.concatenate([[0], hdr[3::4]])                   # slice s: [hdr[4s-1], hdr[4s+3])
         assert ((bounds[sl] <= e) & (e < bounds[sl + 1])).all()
         bank = (off >> 2) & 31
-        for q in range(8):                                          # each slice's store rounds, in order
+        for q in range(4):                                          # each slice's store rounds, in order
             first = s[i] + 8 + bounds[q]
             pr = np.arange(bounds[q + 1] - bounds[q]) + (first & 3)  # places above the 4-word boundary
-            rnd = np.where(pr < 512, (pr >> 7) * 4 + (pr & 3), 16 + ((pr - 512) >> 5))
+            rnd = np.where(pr < 1024, (pr >> 7) * 4 + (pr & 3), 32 + ((pr - 1024) >> 5))
             b = bank[bounds[q]:bounds[q + 1]]
             left = np.bincount(b, minlength=32)
             for R in np.unique(rnd):
