@@ -206,7 +206,9 @@ int p2p_spmm_mask_peers(const void* x, int dtype, int64_t tokens, int64_t cols, 
  * the site); reset != 0 clears it. Syncs the stream. */
 int p2p_spmm_mask_status(int reset, void* stream);
 
-/* Bytes of workspace p2p_spmm_tc needs for this shape (0 if it does not split the columns). */
+/* Bytes of workspace p2p_spmm_tc needs for this shape: 0 if one CTA takes each row tile whole; ticket counters and
+ * fp32 partials when the columns are split (and not added in a cluster), or when the module runs as persistent runs
+ * (more row tiles than SMs at up to 128 tokens: the partials of row tiles two runs share). */
 size_t p2p_spmm_tc_workspace(int64_t rows, int64_t cols, int64_t tokens);
 
 /* y [tokens, ldy] = x [tokens, cols] (row stride ldx, 16-byte aligned rows) times the module in the tensor-core
@@ -216,7 +218,9 @@ size_t p2p_spmm_tc_workspace(int64_t rows, int64_t cols, int64_t tokens);
  * Each launch is a programmatic dependent of the stream's previous kernel: it may start while that kernel finishes,
  * reading words and seg (and setting up) at once, but it reads x and writes y / the workspace only after that kernel
  * has completed. So x may be the previous kernel's output; words and seg must not be (build them, then synchronize,
- * as p2p_tiles_fill does). Column splits of a row tile may run as a thread-block cluster reducing over DSMEM.
+ * as p2p_tiles_fill does). Column splits of a row tile may run as a thread-block cluster reducing over DSMEM; a module
+ * of more row tiles than SMs at up to 128 tokens runs as one CTA an SM, each a contiguous run of (row tile, column
+ * tile) units. Results are deterministic for a shape on a device (fixed reduction orders, whatever the scheduling).
  * Replaces p2p/compact.cu:82-278 (spmm_kernel, sum_parts, spmm) and p2p/compact.py:192-199 (Tiles.__call__). */
 int p2p_spmm_tc(const void* x, int dtype, int64_t tokens, int64_t cols, int64_t ldx, const uint32_t* words,
                 const int64_t* seg, int64_t rows, int64_t seg_cap_words, void* y, int64_t ldy, void* workspace,
