@@ -182,6 +182,20 @@ def test_persistent_runs_match_the_dense_matmul(t, rows, cols, keep):
     kernels.spmm_tc_status()
 
 
+@pytest.mark.parametrize("t", [17, 64])
+def test_persistent_runs_in_f16(t):
+    """The run instantiation for f16 weights (a module of 160 row tiles, ragged last one), against the oracle."""
+    rows, cols = 20400, 512
+    values, idx = _module(rows, cols, 33, torch.float16, seed=t)
+    tiles = compact.Tiles([("compact", values, idx, cols)])
+    x = torch.randn(t, cols, device="cuda").half()
+    y = tiles(x)
+    kernels.spmm_tc_status()
+    sample = torch.cat([torch.arange(0, rows, 29, device="cuda"), torch.arange(rows - 70, rows, device="cuda")])
+    want = oracle.forward(_bits(x), _bits(values[sample]), idx[sample].cpu().numpy(), cols, "f16")
+    _check(y[:, sample], want, torch.float16)
+
+
 def test_split_launches_of_different_shapes_share_a_workspace():
     """Column-split launches with few row tiles, then many: each finds its ticket counters zero."""
     for rows, cols in ((256, 4096), (14336, 4096), (512, 14336), (28672, 4096)):
