@@ -27,7 +27,9 @@ from safetensors.torch import save_file
 
 from . import compact, family, wanda
 
-SAVES = 0.9            # a pruned block is stored compact only if that takes at most this share of its dense bytes
+# Largest ratio of compact bytes (values + mask words) to dense bytes at which a replica file keeps a pruned block in
+# compact form; above it the block is written dense (the same rule as the reference's writer, so files match).
+SAVES = 0.9
 
 
 def _on_gpu(t: torch.Tensor) -> torch.Tensor:
