@@ -740,12 +740,15 @@ def run_sharded(args, layer, rank, world, device, peaks):
             for m in names:
                 dist.all_gather_into_tensor(full[buf][m], stage[buf][m])
             mods = rotation[k % copies]
+            # The y buffers of this parity were last read by this rank's copy-out of step k - 2 (its own columns,
+            # which only its own GEMM writes; peers push their columns), so the GEMMs wait for that copy alone and
+            # the copy-out of step k - 1 overlaps them.
+            stream.wait_event(copied[buf])
             ys = {}
             for m in names:
                 mods[m]._turn = buf                    # y buffer by step parity, whichever weight copy runs
                 ys[m] = mods[m].apply_fused(full[buf][m][:args.tokens], sync=False)
             consumed[buf].record(stream)
-            stream.wait_event(copied[buf ^ 1])         # this rank's copy-out of step k - 1 has finished
             peers.barrier()
             done = torch.cuda.Event()
             done.record(stream)
