@@ -541,9 +541,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             // 4, every fourth 16-column chunk) -- to y when the run holds the whole row tile, else to this run's fp32
             // partial, the last of the row tile's runs adding all partials in run order. A warp reads a row tile out
             // only when it must: before expanding a tile whose slot is freed by MMAs that wait for that read-out (so
-            // the ring is full of the next row tile's tiles meanwhile), once it is G tiles into the next row tile
-            // when there are two sets, and at the end. Every wait is bounded; a warp whose wait gave up expands no
-            // further tile but keeps to the same barrier sequence.
+            // the ring is full of later row tiles' tiles meanwhile; with two sets that is two row tiles on), and at
+            // the end. (Reading out as soon as a warp is a few tiles into the next row tile stalled every warp on the
+            // MMAs at once.) Every wait is bounded; a warp whose wait gave up expands no further tile but keeps to
+            // the same barrier sequence.
             const int quarter = warp & 3, cgroup = warp >> 2;
             const int row_local = quarter * 32 + lane;
             const bool by_tile = p.acc_stride != 0;
