@@ -203,7 +203,8 @@ int p2p_spmm_mask_peers(const void* x, int dtype, int64_t tokens, int64_t cols, 
                         void* workspace, size_t workspace_bytes, void* stream);
 
 /* P2P_OK unless a p2p_spmm_mask launch since the last reset gave up waiting on its pipeline (then P2P_ECUDA, naming
- * the site); reset != 0 clears it. Syncs the stream. */
+ * the site); reset != 0 clears it. Syncs the stream. After a give-up the launch's workspace is undefined: zero it
+ * again before the next launch that uses it. */
 int p2p_spmm_mask_status(int reset, void* stream);
 
 /* Bytes of workspace p2p_spmm_tc needs for this shape: 0 if one CTA takes each row tile whole; ticket counters and
@@ -290,7 +291,8 @@ int p2p_moe_combine(const void* y, int dtype, int64_t ldy, const int64_t* where,
 
 /* P2P_OK unless a p2p_spmm_tc launch since the last reset gave up waiting on its pipeline (then P2P_ECUDA, naming
  * the site); reset != 0 clears the flag. Syncs the stream. A launch that gives up issues no further loads or MMAs,
- * drains what it issued and exits; its y is then undefined. */
+ * drains what it issued and exits; its y is then undefined, and so is its workspace (a run or column split that stopped
+ * may leave its row tile's ticket counter taken): zero the workspace again before the next launch that uses it. */
 int p2p_spmm_tc_status(int reset, void* stream);
 
 /* Test of that give-up path: p2p_spmm_tc (one launch, tokens <= 512) in which every CTA withholds the x tile of local

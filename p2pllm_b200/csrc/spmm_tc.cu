@@ -48,6 +48,8 @@ constexpr int kExpWarps = kGroupWarps * kGroups;
 constexpr int kProducerWarp = kExpWarps;
 constexpr int kMmaWarp = kExpWarps + 1;                           // and kMmaWarp + 1: two MMA issuers
 constexpr int kTcThreads = kExpWarps * 32 + 96;
+constexpr int kZeroWarp = kExpWarps + 3;                           // runs: zero copies into the A slots
+constexpr int kRunThreads = kTcThreads + 32;
 constexpr int kATileBytes = tc::kTileRows * tc::kTileCols * 2;   // 16 KiB
 constexpr int kASlotBytes = kATileBytes;                           // 1 KiB aligned, as the 128-byte swizzle needs
 constexpr int kMaxASlots = 12;                                     // A tiles in flight (even: the groups alternate)
@@ -67,6 +69,7 @@ constexpr size_t kTicketRegion = kMaxRowTiles * sizeof(unsigned);
 
 __device__ int g_tc_error;            // site of the first wait that gave up since the last reset (0: none)
 __device__ unsigned g_tc_failed_seq;  // sequence number of the last launch in which a wait gave up
+__device__ __align__(128) uint4 g_zero_tile[kATileBytes / 16];   // zeros, bulk-copied into a run's A slots
 
 struct TcParams {
     const uint32_t* words;            // the module's packed words
@@ -219,7 +222,7 @@ __device__ __forceinline__ void l2_prefetch(const void* src, uint32_t bytes) {
 // kPeers: y goes to every ys[k] (row sharding with the all-gather fused in) instead of y.
 // kRuns: a persistent run of units across row tiles (see TcParams::n_units) instead of one row tile's column range.
 template <typename T, bool kL2, bool kPeers, bool kRuns = false>
-__global__ void __launch_bounds__(kTcThreads, 1)
+__global__ void __launch_bounds__(kRuns ? kRunThreads : kTcThreads, 1)
     spmm_tc_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_y, TcParams p) {
     extern __shared__ uint8_t smem_raw[];
     __shared__ uint32_t s_tmem;
@@ -244,10 +247,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const uint32_t done = bars + 8u * (2 * kMaxASlots + 2 * kMaxXSlots);
     // Runs: accfull(s) -- a row tile's MMAs into accumulator set s complete (both issuers commit); accempty(s) -- the set
     // read out (the 16 expander warps arrive); partdone / tickdone -- a shared row tile's partial written (16 warps) /
-    // its ticket taken (thread 0).
+    // its ticket taken (thread 0); zeroed(s) -- A slot s holds zeros for its next tile (the zero warp's bulk copy).
     auto accfull = [&](int st) { return done + 8u * (1 + st); };
     auto accempty = [&](int st) { return done + 8u * (3 + st); };
     const uint32_t partdone = done + 40u, tickdone = done + 48u;
+    auto zeroed = [&](int st) { return done + 56u + 8u * st; };
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const WaitCtl wc{&g_tc_error, &g_tc_failed_seq, p.wait_ns, p.seq};
@@ -323,6 +327,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             }
             mbar_init(partdone, kExpWarps);
             mbar_init(tickdone, 1);
+            for (int st = 0; st < SA; ++st) mbar_init(zeroed(st), 1);
         }
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -445,6 +450,24 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             if (!kRuns) umma_commit(done);              // arrives once every MMA this thread issued completed
         }
         __syncwarp();
+    } else if (kRuns && warp == kZeroWarp) {
+        // A run's A slots are zeroed by bulk copies from a zero tile in L2, tile after tile, each once the MMAs have
+        // read the slot's previous tile; the expanders wait for the copy instead of storing zeros themselves, which
+        // takes the zero stores (a quarter of the expanders' shared-memory stores at 17 tokens) off their path.
+        if (lane == 0) {
+            int issued = 0;
+            for (int i = 0; i < nk; ++i) {
+                const int st = i % SA, u = i / SA;
+                if (u > 0 && !mbar_wait(emptya(st), (uint32_t)((u - 1) & 1), 12, wc)) break;
+                mbar_expect_tx(zeroed(st), (uint32_t)kATileBytes);
+                bulk_load(a_ring + (uint32_t)(st * kASlotBytes), g_zero_tile, (uint32_t)kATileBytes, zeroed(st));
+                issued = i + 1;
+            }
+            // every copy has landed before the CTA exits (after a give-up too)
+            for (int st = 0; st < SA && st < issued; ++st)
+                mbar_drain(zeroed(st), (uint32_t)(((issued - 1 - st) / SA) & 1), 13, wc);
+        }
+        __syncwarp();
     } else {
         // Expanders: group `grp` builds the dense 128 x 64 tiles of every fourth column tile in shared memory. Warp wg
         // owns rows 32 wg .. 32 wg + 31 of the tile: it zeroes them and writes their entries at the offsets the words
@@ -475,8 +498,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         };
         // Zeroing a slot's rows: with three or more slots a group, the group's next slot is zeroed while this tile is
         // scattered (its last use is two tiles back, long consumed), which takes the zeroing off the warp's chain of
-        // waits; with two, the slot is zeroed just before its own scatter.
-        const bool zero_ahead = SA / kGroups >= 3;
+        // waits; with two, the slot is zeroed just before its own scatter. (A run's slots are zeroed by the zero warp.)
+        const bool zero_ahead = !kRuns && SA / kGroups >= 3;
         auto zero_rows = [&](int slot) {
             uint4* rows16 = reinterpret_cast<uint4*>(gbase + (size_t)slot * kASlotBytes + wg * kWarpRows * 128);
 #pragma unroll
@@ -488,7 +511,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         }
         // false: a wait gave up, and the warp stops expanding (no further tiles for the MMAs to read)
         auto expand = [&](int i, const uint4 (&cur)[kChunks], int lo, int hi) -> bool {
-            if (zero_ahead) {
+            if (kRuns) {
+                const int ok = mbar_wait(zeroed(s), ph, 5, wc);              // every lane sees the zeros landed
+                if (!__all_sync(0xffffffffu, ok)) return false;
+            } else if (zero_ahead) {
                 int sn = s + kGroups;
                 uint32_t pn = ph;
                 if (sn >= SA) {
@@ -651,9 +677,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             };
             bool live = true;
             int k_epi = 0;
-            // The tile whose slot expand(i) waits for (i - SA, or i + G - SA when zeroing ahead) and its row tile in
-            // the run, kept by increments (no division on the warp's per-tile path).
-            int dep = (zero_ahead ? G - SA : -SA) + grp, dep_row = 0;
+            // The tile whose MMAs expand(i) waits for, i - SA (the zero warp copies zeros into a slot, in tile order, once
+            // the MMAs have read the slot's previous tile), and its row tile in the run, kept by increments (no division
+            // on the warp's per-tile path).
+            int dep = grp - SA, dep_row = 0;
             int dep_row_end = (int)(min(u1, (r0 + 1) * C) - u0);      // local end of row tile dep_row
             for (int i = grp;; i += G, dep += G) {
                 int need = n_rows;                                      // row tiles to have read out first
@@ -968,7 +995,8 @@ struct TcPlan {
 // Token-dependent part of a launch plan: MMA N, x boxes, TMEM columns, ring depths, shared memory. Fails when the
 // tokens do not fit shared memory.
 int plan_tokens(int tn, TcPlan& pl) {
-    const int fixed = 1024 + 8 * (2 * kMaxASlots + 2 * kMaxXSlots + 7) + 64;   // + done and the runs' six barriers
+    // + done, the runs' six barriers and their zeroed(s) per A slot
+    const int fixed = 1024 + 8 * (3 * kMaxASlots + 2 * kMaxXSlots + 7) + 64;
     pl.n_total = (tn + 15) / 16 * 16;
     pl.n_boxes = pl.n_total <= 256 ? 1 : 2;
     pl.box_rows = pl.n_total / pl.n_boxes;
@@ -1015,7 +1043,7 @@ int launch_tc(const CUtensorMap& map, const CUtensorMap& ymap, const TcParams& p
     attr[1].val.clusterDim.y = grid.y;
     attr[1].val.clusterDim.z = 1;
     cfg.gridDim = grid;
-    cfg.blockDim = dim3(kTcThreads);
+    cfg.blockDim = dim3(prm.run_partial ? kRunThreads : kTcThreads);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
     cfg.attrs = attr;

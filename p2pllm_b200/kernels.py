@@ -28,6 +28,19 @@ def _workspace(device: torch.device, nbytes: int, purpose: str = "sumsq") -> tor
     return ws
 
 
+def _rezero_workspaces(dev: torch.device, purpose: str) -> int:
+    """Zeroes every cached workspace of `purpose` on `dev` (all streams), and the torch operators' own workspaces
+    there; returns how many of this module's it zeroed."""
+    n = 0
+    for (kind, index, what, _), ws in _workspaces.items():
+        if kind == dev.type and index == dev.index and what == purpose:
+            ws.zero_()
+            n += 1
+    if dev.type == "cuda" and _lib._ops is not None:
+        _lib._ops.zero_workspaces(dev.index)
+    return n
+
+
 def _rows2d(x: torch.Tensor) -> torch.Tensor:
     x = x.reshape(-1, x.shape[-1])
     if x.stride(-1) != 1:
@@ -295,9 +308,16 @@ def spmm_mask_peers(x: torch.Tensor, data: torch.Tensor, seg: torch.Tensor, rows
 
 
 def spmm_mask_status(device=None, reset: bool = True) -> None:
-    """Raises if a bitmask-layout GEMM launch gave up waiting on its pipeline since the last reset. Syncs."""
+    """Raises if a bitmask-layout GEMM launch gave up waiting on its pipeline since the last reset. Syncs. As with
+    spmm_tc_status, the device's bitmask-GEMM workspaces are zeroed again before raising."""
     dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
-    call("p2p_spmm_mask_status", int(reset), torch.cuda.current_stream(dev).cuda_stream)
+    try:
+        call("p2p_spmm_mask_status", int(reset), torch.cuda.current_stream(dev).cuda_stream)
+    except P2PError:
+        torch.cuda.synchronize(dev)
+        _rezero_workspaces(dev, "spmm_mask")
+        torch.cuda.synchronize(dev)
+        raise
 
 
 def spmm_tc(x: torch.Tensor, words: torch.Tensor, seg: torch.Tensor, rows: int, cols: int, seg_cap: int,
@@ -370,9 +390,18 @@ def spmm_tc_withhold(x: torch.Tensor, words: torch.Tensor, seg: torch.Tensor, ro
 
 
 def spmm_tc_status(device=None, reset: bool = True) -> None:
-    """Raises if a tensor-core GEMM launch gave up waiting on its pipeline since the last reset. Syncs."""
+    """Raises if a tensor-core GEMM launch gave up waiting on its pipeline since the last reset. Syncs. A launch that
+    gave up may leave ticket counters of its workspace taken (a run that stopped before the last one of its row tile
+    came), so before raising, the device's tensor-core workspaces are zeroed again: the next launch finds them as a
+    fresh one would."""
     dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
-    call("p2p_spmm_tc_status", int(reset), torch.cuda.current_stream(dev).cuda_stream)
+    try:
+        call("p2p_spmm_tc_status", int(reset), torch.cuda.current_stream(dev).cuda_stream)
+    except P2PError:
+        torch.cuda.synchronize(dev)                   # launches on other streams may share none of them any more
+        _rezero_workspaces(dev, "spmm_tc")
+        torch.cuda.synchronize(dev)
+        raise
 
 
 def _ptr_array(ts) -> ctypes.Array:

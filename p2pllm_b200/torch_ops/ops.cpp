@@ -38,11 +38,13 @@ void* stream_of(const at::Tensor& t) {
 
 // A zeroed scratch buffer per device, purpose and stream, kept for the process (the kernels leave it zeroed again;
 // launches on one stream run in order and may share it, launches on two streams may overlap and must not).
+std::mutex ws_mu;
+std::map<std::tuple<int, int, void*>, at::Tensor> ws_cache;
+
 void* workspace(const at::Tensor& like, size_t bytes, int purpose) {
     if (bytes == 0) return nullptr;
-    static std::mutex mu;
-    static std::map<std::tuple<int, int, void*>, at::Tensor> cache;
-    std::lock_guard<std::mutex> lock(mu);
+    auto& cache = ws_cache;
+    std::lock_guard<std::mutex> lock(ws_mu);
     const auto key = std::make_tuple((int)like.device().index(), purpose, stream_of(like));
     auto it = cache.find(key);
     if (it == cache.end() || (size_t)it->second.numel() < bytes) {
@@ -51,6 +53,16 @@ void* workspace(const at::Tensor& like, size_t bytes, int purpose) {
         it = cache.find(key);
     }
     return it->second.data_ptr();
+}
+
+// Zeroes every cached workspace of `device` (after a launch gave up, which may leave ticket counters taken).
+void zero_workspaces(int64_t device) {
+    std::lock_guard<std::mutex> lock(ws_mu);
+    for (auto& [key, ws] : ws_cache) {
+        if (std::get<0>(key) != (int)device) continue;
+        const c10::cuda::CUDAGuard guard(ws.device());
+        ws.zero_();
+    }
 }
 
 // x as the GEMMs take it: 2-D, unit column stride, 16-byte aligned rows.
@@ -186,6 +198,7 @@ TORCH_LIBRARY(p2p_b200, m) {
     m.def("sumsq_cols(Tensor x, Tensor(a!) sums) -> ()");
     m.def("combine(Tensor[] parts, Tensor h, Tensor h_copy) -> Tensor");
     m.def("sum_parts(Tensor[] parts) -> Tensor");
+    m.def("zero_workspaces(int device) -> ()", &zero_workspaces);
 }
 
 TORCH_LIBRARY_IMPL(p2p_b200, CUDA, m) {

@@ -100,8 +100,28 @@ def test_torch_ops_load_and_propagate_shapes_on_meta_tensors(lib):
     assert y.shape == (272, 1024)
     h = meta(8, 96)
     assert ops.combine([h, h, h], h, h).shape == (8, 96) and ops.sum_parts([h, h]).shape == (8, 96)
-    names = {"spmm_tc", "spmm_tc_into", "spmm_mask", "spmm_mask_into", "sumsq_cols", "combine", "sum_parts"}
+    names = {"spmm_tc", "spmm_tc_into", "spmm_mask", "spmm_mask_into", "sumsq_cols", "combine", "sum_parts",
+             "zero_workspaces"}
     assert all(hasattr(ops, n) for n in names)
+    ops.zero_workspaces(0)                              # no workspace cached on this host: nothing to zero
+
+
+def test_a_give_up_zeroes_the_gemm_workspaces_of_its_device_again():
+    """After a pipeline wait gave up, a launch may have left ticket counters of its workspace taken; the status check
+    zeroes the cached workspaces of that purpose on that device (every stream), and no others."""
+    import torch
+    from p2pllm_b200 import kernels
+    keys = [("cpu", None, "spmm_tc", 1), ("cpu", None, "spmm_tc", 2), ("cpu", None, "spmm_mask", 1),
+            ("cpu", 3, "spmm_tc", 1)]
+    saved = dict(kernels._workspaces)
+    try:
+        for k in keys:
+            kernels._workspaces[k] = torch.full((64,), 7, dtype=torch.uint8)
+        assert kernels._rezero_workspaces(torch.device("cpu"), "spmm_tc") == 2
+        assert [int(kernels._workspaces[k].sum()) for k in keys] == [0, 0, 7 * 64, 7 * 64]
+    finally:
+        kernels._workspaces.clear()
+        kernels._workspaces.update(saved)
 
 
 def _ptrs(*vals):

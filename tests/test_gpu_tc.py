@@ -6,7 +6,7 @@ import pytest
 import torch
 
 import oracle
-from p2pllm_b200 import compact, kernels, wanda
+from p2pllm_b200 import _lib, compact, kernels, wanda
 
 pytestmark = pytest.mark.gpu
 
@@ -242,6 +242,41 @@ def test_dependent_launches_see_the_previous_kernels_output():
         got = m.apply(None, x2)
         torch.cuda.synchronize()
         assert torch.equal(got, m.apply(None, (x * scale)))
+
+
+@pytest.mark.parametrize("tokens", [17, 100])
+def test_a_withheld_tile_in_persistent_runs_ends_with_an_error_status(tokens):
+    """The give-up path of the persistent runs (a module of 149 row tiles, one CTA an SM): every run withholds its
+    first x tile, so its MMAs, the zero copies into the A slots, the expanders and the row tiles' read-outs all stop
+    at bounded waits. The launch ends by itself, the status names a wait, and the next launch through the same
+    workspace (re-zeroed by the status check: a stopped run may leave a row tile's ticket taken) is right and
+    repeats bit for bit."""
+    import time
+    from p2pllm_b200._lib import P2PError
+    rows, cols = 19000, 1024
+    values, idx = _module(rows, cols, 36, seed=11)
+    tiles = compact.Tiles([("compact", values, idx, cols)])
+    x = torch.randn(tokens, cols, device="cuda").bfloat16()
+    y = tiles(x)                                                    # the workspace cached for this stream
+    kernels.spmm_tc_status(reset=True)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    kernels.spmm_tc_withhold(x, tiles.words, tiles.seg, tiles.rows, tiles.cols, tiles.seg_cap, hold_tile=0,
+                             wait_us=20000)
+    torch.cuda.synchronize()
+    assert time.perf_counter() - t0 < 1.0
+    with pytest.raises(P2PError, match="timed out"):
+        kernels.spmm_tc_status(reset=True)
+    kernels.spmm_tc_status()
+    need = _lib.load().p2p_spmm_tc_workspace(rows, cols, tokens)
+    assert need > 0                                                 # the runs' ticket counters and partials
+    assert int(torch.count_nonzero(kernels._workspace(x.device, need, "spmm_tc"))) == 0
+    again = tiles(x)
+    kernels.spmm_tc_status()
+    assert torch.equal(again, y)
+    sample = torch.cat([torch.arange(0, rows, 41, device="cuda"), torch.arange(rows - 130, rows, device="cuda")])
+    want = oracle.forward(_bits(x), _bits(values[sample]), idx[sample].cpu().numpy(), cols, "bf16")
+    _check(again[:, sample], want, torch.bfloat16)
 
 
 @pytest.mark.parametrize("tokens", [17, 272])
