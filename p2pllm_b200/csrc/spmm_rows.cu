@@ -13,7 +13,8 @@
 //
 // Few tokens (a draft pass of 16 + 1): one block per SM stages ALL of x at once, column-major (each kept weight's
 // column for every token is a few 16-byte shared loads), while its warps prefetch their first rows' weights into L2;
-// then every warp of the grid takes whole rows in turn, each lane keeping a chunk of the row's loads in flight. x is
+// then every warp of the grid takes whole rows in turn (dealt across the blocks first, so all SMs share the gathers,
+// which bind: random columns make them bank-conflicted), each lane keeping a chunk of the row's loads in flight. x is
 // read from L2 once per SM instead of once per (token tile, row group) block. (Staging x row-major by bulk copies
 // was measured slower: a column then costs one shared load a token, with bank conflicts.)
 #include "common.cuh"
@@ -208,7 +209,9 @@ __global__ void __launch_bounds__(kStagedBlock, 1) spmm_rows_staged_kernel(const
     extern __shared__ __align__(16) unsigned char smem_raw[];
     T* xs = reinterpret_cast<T*>(smem_raw);
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int64_t gw = (int64_t)blockIdx.x * kStagedWarps + warp;
+    // rows dealt across the blocks first (row r to block r % grid), so every SM's shared memory takes an equal share
+    // of the gathers even when the rows do not fill every block's warps
+    const int64_t gw = (int64_t)warp * gridDim.x + blockIdx.x;
     const int64_t stride = (int64_t)gridDim.x * kStagedWarps;
     // the first row of this warp, into L2 (a 128-byte line a lane), while x is staged
     if (gw < total_rows) {
@@ -306,8 +309,7 @@ int launch_staged(const void* x, int64_t tokens, int64_t cols, int64_t ldx, cons
     auto kern = spmm_rows_staged_kernel<T, I, TT>;
     const int smem = (int)(cols * TT * sizeof(T));
     if (int e = allow_smem((const void*)kern, kStagedSmem, "p2p_spmm_rows")) return e;
-    const int64_t want = (total_rows + kStagedWarps - 1) / kStagedWarps;
-    const int grid = (int)(want < sm_count() ? want : sm_count());
+    const int grid = (int)(total_rows < sm_count() ? total_rows : sm_count());   // a block an SM, a row at least
     kern<<<grid, kStagedBlock, smem, s>>>(reinterpret_cast<const T*>(x), (int)tokens, (int)cols, ldx, bt, total_rows,
                                           reinterpret_cast<T*>(y), ldy);
     return launch_status("p2p_spmm_rows");

@@ -57,7 +57,8 @@ def test_compact_method_puts_blocks_in_row_order():
 @pytest.mark.parametrize("layout", [None, "rows"])
 @pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16, torch.float32])
 @pytest.mark.parametrize("t", [1, 3, 17, 32, 64, 100, 272])
-@pytest.mark.parametrize("rows,cols,keep", [(512, 5120, 40), (300, 1000, 7), (96, 80, 90), (1024, 2048, 25), (17, 8, 50)])
+@pytest.mark.parametrize("rows,cols,keep", [(512, 5120, 40), (300, 1000, 7), (96, 80, 90), (1024, 2048, 25), (17, 8, 50),
+                                            (5000, 256, 30)])
 def test_tiles_match_a_dense_matmul(layout, dtype, t, rows, cols, keep):
     """tests/test_compact.py:44-56 (its tolerance max|d| <= 1e-2 max|want|), plus rel-L2 <= 1e-2 for bf16/f16 and
     <= 1e-5 for fp32, any shape and any token count, in either layout (bf16/f16 default to the tensor-core one)."""
