@@ -80,6 +80,15 @@ __device__ __forceinline__ void gather(const T* xs, int c, float (&out)[TT]) {
     }
 }
 
+// One value as fp32 through the read-only path.
+__device__ __forceinline__ float ldg_f32(const float* p) { return __ldg(p); }
+__device__ __forceinline__ float ldg_f32(const __nv_bfloat16* p) {
+    return __uint_as_float((uint32_t)__ldg(reinterpret_cast<const unsigned short*>(p)) << 16);
+}
+__device__ __forceinline__ float ldg_f32(const __half* p) {
+    return __half2float(__ushort_as_half(__ldg(reinterpret_cast<const unsigned short*>(p))));
+}
+
 // VEC values and VEC column indices of one 16-byte-aligned step of a row.
 template <typename T, typename I, int VEC>
 __device__ __forceinline__ void load_step(const T* v, const I* ix, int64_t e, float (&fv)[VEC], int (&ci)[VEC]) {
@@ -205,7 +214,6 @@ __global__ void __launch_bounds__(kStagedBlock, 1) spmm_rows_staged_kernel(const
                                                                            int cols, int64_t ldx, BlockTable bt,
                                                                            int64_t total_rows, T* __restrict__ y,
                                                                            int64_t ldy) {
-    constexpr int VEC = 16 / sizeof(T);
     extern __shared__ __align__(16) unsigned char smem_raw[];
     T* xs = reinterpret_cast<T*>(smem_raw);
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -255,33 +263,29 @@ __global__ void __launch_bounds__(kStagedBlock, 1) spmm_rows_staged_kernel(const
         float acc[TT];
 #pragma unroll
         for (int t = 0; t < TT; ++t) acc[t] = 0.f;
-        // kSteps steps of the row's values and indices in flight at once, then their products
-        constexpr int kSteps = (TT >= 32 ? 8 : TT >= 16 ? 16 : 32) / VEC;
-        for (int64_t e0 = (base & ~(int64_t)(VEC - 1)) + lane * VEC; e0 < end; e0 += (int64_t)kSteps * 32 * VEC) {
-            float fv[kSteps][VEC];
-            int ci[kSteps][VEC];
+        // Lane l takes the row's entries l, l + 32, ...: one gather instruction then reads 32 consecutive kept columns,
+        // which fall on all eight 16-byte bank groups of the staged columns. (Four consecutive entries a lane, as
+        // 16-byte loads, put neighbouring lanes k / keep columns apart -- 10 at keep 40 -- which with 80-byte columns
+        // lands on four of the eight groups: twice the wavefronts a gather.) kPer entries a lane in flight at once.
+        constexpr int kPer = TT >= 32 ? 8 : TT >= 16 ? 16 : 32;
+        for (int64_t e0 = base + lane; e0 < end; e0 += (int64_t)kPer * 32) {
+            float fv[kPer];
+            int ci[kPer];
 #pragma unroll
-            for (int st = 0; st < kSteps; ++st) {
-                const int64_t e = e0 + (int64_t)st * 32 * VEC;
-                if (e < end) load_step<T, I, VEC>(v, ix, e, fv[st], ci[st]);
+            for (int j = 0; j < kPer; ++j) {
+                const int64_t e = e0 + (int64_t)j * 32;
+                if (e < end) {
+                    fv[j] = ldg_f32(v + e);
+                    ci[j] = ix ? (int)__ldg(ix + e) : (int)(e - base);
+                }
             }
 #pragma unroll
-            for (int st = 0; st < kSteps; ++st) {
-                const int64_t e = e0 + (int64_t)st * 32 * VEC;
-                if (e >= end) break;
-                if (ix == nullptr) {
+            for (int j = 0; j < kPer; ++j) {
+                if (e0 + (int64_t)j * 32 >= end) break;
+                float xv[TT];
+                gather<T, TT>(xs, (int)min((unsigned)ci[j], cmax), xv);
 #pragma unroll
-                    for (int i = 0; i < VEC; ++i) ci[st][i] += (int)(e - base);
-                }
-                const bool whole = e >= base && e + VEC <= end;
-#pragma unroll
-                for (int i = 0; i < VEC; ++i) {
-                    if (!whole && (e + i < base || e + i >= end)) continue;
-                    float xv[TT];
-                    gather<T, TT>(xs, (int)min((unsigned)ci[st][i], cmax), xv);
-#pragma unroll
-                    for (int t = 0; t < TT; ++t) acc[t] = fmaf(fv[st][i], xv[t], acc[t]);
-                }
+                for (int t = 0; t < TT; ++t) acc[t] = fmaf(fv[j], xv[t], acc[t]);
             }
         }
 #pragma unroll
