@@ -8,9 +8,12 @@
 //   warp 16 (producer)  per column tile: TMA of the x tile [tokens x 64] (128-byte swizzle) into the x ring, one
 //                       producer lane per ring slot.
 //   warps 0-15 (expand) four groups of 4 warps take column tiles in turn. Each warp zeroes its 32 rows of a
-//                       128 x 64 bf16 tile in the A ring and writes its slice of the segment's words at the swizzled
-//                       byte offsets they carry, with no barrier between warps. The words come straight from HBM into
-//                       registers (coalesced, 16 bytes a lane), never through shared memory.
+//                       128 x 64 bf16 tile in the A ring (in a persistent run, warp 19 zeroes the slot instead) and
+//                       writes its slice of the segment's words at the swizzled byte offsets they carry, with no
+//                       barrier between warps. The words come straight from HBM into registers (coalesced, 16 bytes a
+//                       lane), never through shared memory.
+//   warp 19 (zero)      persistent runs only (one CTA an SM over a contiguous run of (row tile, column tile) units):
+//                       a bulk copy of a zero tile into each A slot once the MMAs have read its previous tile.
 //   warps 17-18 (MMA)   one elected thread each issues tcgen05.mma (M = 128, N = tokens rounded to 16, K = 16 a step)
 //                       with fp32 accumulators in TMEM (alternate tiles, or halves of N past 256 tokens);
 //                       tcgen05.commit frees the rings' slots.
