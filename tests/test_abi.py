@@ -61,6 +61,23 @@ def test_workspace_query_is_host_only(lib):
     assert lib.p2p_sumsq_workspace(100, 4096, 9) == 0
 
 
+def test_persistent_runs_workspace_is_sized_on_the_host(lib):
+    """The tensor-core GEMM's workspace for a module of more row tiles than SMs at up to 128 tokens (one CTA an SM,
+    contiguous runs of units): the ticket region, then two fp32 partial tiles [tokens][128] a run. Without a GPU the
+    query assumes the B200's 148 SMs. A run takes at most 256 units, so very wide modules get more runs than SMs."""
+    import torch
+    if torch.cuda.is_available():
+        pytest.skip("with a GPU the query uses that device's SM count")
+    tickets = 16384 * 4
+    runs = lambda g, t: tickets + g * 2 * t * 128 * 4
+    assert lib.p2p_spmm_tc_workspace(149 * 128, 1024, 17) == runs(148, 17)
+    assert lib.p2p_spmm_tc_workspace(19000, 1024, 100) == runs(148, 100)
+    assert lib.p2p_spmm_tc_workspace(19000, 1024, 128) == runs(148, 128)
+    assert lib.p2p_spmm_tc_workspace(149 * 128, 65536, 17) == runs(-(-149 * 1024 // 256), 17)
+    assert lib.p2p_spmm_tc_workspace(148 * 128, 64, 17) == 0           # row tiles <= SMs: one CTA a row tile
+    assert lib.p2p_spmm_tc_workspace(19000, 1024, 0) == 0
+
+
 def test_cpu_tensors_are_refused():
     import torch
     from p2pllm_b200 import P2PError, kernels
